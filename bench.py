@@ -1,0 +1,487 @@
+#!/usr/bin/env python
+"""Decode-step benchmark of the kvquant_b200 quantized-KV attention path.
+
+Workload (default "longctx-1m-4bit"): LLaMA-2-7B shape -- batch 1, 32 KV heads
+of 128 channels, 1,048,576 cached tokens in each of 32 layers, 4-bit NUQ keys
+(per channel, pre-RoPE) and values (per token) with 1% fp16 outliers, RoPE
+theta 10000. One step = one decode step of attention over the whole cache:
+for every layer, the fused key kernel, softmax and the value kernel. Synthetic
+seeded data (the reference's wikitext-2 activations are not available); the
+cache is built on the GPU by this library's quantize-on-append kernels.
+
+Multi-GPU: one process per GPU (torchrun); KV heads are split across ranks
+(strong scaling: the total cache is fixed) and each layer's per-head outputs
+are all-gathered with NCCL. value = cached token positions (all heads, K and
+V) scanned per second over the whole job: batch * tokens * layers / step time,
+step time = max over ranks of CUDA-event time.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "kvquant-paper-repro_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "4-bit KV decode attention: keys+values scanned/s, % of B200 HBM BW; 1–8 GPUs"
+UNIT = "tokens/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", default="longctx-1m-4bit")
+    ap.add_argument("--layers", type=int, default=None, help="override the layer count")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# the GPU arm
+# ---------------------------------------------------------------------------
+def setup_dist(args):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def peak_hbm():
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def build_cache(wl, layers, h0, hl, dev, log):
+    """Quantized cache of this rank's heads, every layer (built with our kernels)."""
+    import torch
+    from kvquant import synthetic as syn
+    from kvquant.kernels import quantize_keys, quantize_values
+
+    B, T, C = wl.batch, wl.tokens, wl.channels
+    k = torch.empty((B, T, C), dtype=torch.float16, device=dev)
+    v = torch.empty((B, T, C), dtype=torch.float16, device=dev)
+    cache = []
+    cbk = cbv = None
+    t0 = time.time()
+    for layer in range(layers):
+        syn.fill_layer(k, v, layer, seed=0)
+        ks, kz = syn.key_calibration(k)
+        if cbk is None:  # one codebook pair for the synthetic model (same distribution per layer)
+            cbk, cbv = syn.fit_codebooks(k, v, ks, kz, wl.bits)
+        pk = quantize_keys(k, ks, kz, cbk, wl.bits, wl.outlier_ratio, True, h0=h0, n_heads=hl,
+                           capacity=T)
+        pv = quantize_values(v, cbv, wl.bits, wl.outlier_ratio, True, h0=h0, n_heads=hl,
+                             capacity=T)
+        cache.append((pk, pv))
+        if layer == 0 or (layer + 1) % 8 == 0:
+            torch.cuda.synchronize()
+            log(f"layer {layer + 1}/{layers} quantized ({time.time() - t0:.1f}s, "
+                f"{torch.cuda.memory_allocated(dev) / 2**30:.1f} GiB)")
+    del k, v
+    torch.cuda.empty_cache()
+    return cache
+
+
+def algorithmic_bytes(wl, pk, pv, hl, T):
+    """Bytes each kernel must move per layer (per launch) on this rank."""
+    B, G, bits = wl.batch, wl.q_per_kv, wl.bits
+    U = B * hl
+    nt = -(-T // 32)
+    codes = U * T * 16 * bits
+    key = (codes + pk["nnz"] * 4 + U * nt * 4 + 2 * hl * 128 * 4 + B * hl * 128 * 2
+           + B * hl * G * 128 * 2 + B * hl * G * T * 4)
+    value = (codes + pv["nnz"] * 4 + U * nt * 4 + B * T * 8 + B * hl * 128 * 2
+             + B * hl * G * T * 4 + B * hl * G * 128 * 2)
+    softmax = 3 * B * hl * G * T * 4
+    return {"key_scores": key, "value_output": value, "softmax": softmax}
+
+
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+    from kvquant import synthetic as syn
+    from kvquant.kernels import qk_scores, softmax, pv_out, rope_inv_freq, decode_attention
+    from kvquant.kernels.decode import DecodeWorkspace
+
+    world, rank, local = setup_dist(args)
+    dev = torch.device("cuda", local)
+    wl = syn.WORKLOADS[args.workload]
+    layers = args.layers or wl.layers
+    if wl.kv_heads % world:
+        raise SystemExit(f"{wl.kv_heads} KV heads do not split over {world} GPUs")
+    hl = wl.kv_heads // world
+    h0 = rank * hl
+    G = wl.q_per_kv
+    T = wl.tokens
+    log = (lambda m: print(f"[rank {rank}] {m}", file=sys.stderr, flush=True))
+
+    cache = build_cache(wl, layers, h0, hl, dev, log)
+    inv = rope_inv_freq(128, wl.rope_base).to(dev)
+    qs = [syn.make_query(wl.batch, wl.kv_heads * G, l, 0, dev)[:, h0 * G:(h0 + hl) * G].contiguous()
+          for l in range(layers)]
+    Hq_l = hl * G
+    scores = torch.empty((wl.batch, Hq_l, T), dtype=torch.float32, device=dev)
+    outs = [torch.empty((wl.batch, Hq_l, 128), dtype=torch.float16, device=dev)
+            for _ in range(layers)]
+    full = [torch.empty((world, wl.batch, Hq_l, 128), dtype=torch.float16, device=dev)
+            for _ in range(layers)] if world > 1 else None
+    stream = torch.cuda.current_stream(dev)
+    n_launch_per_layer = 5  # key, softmax x2, value, combine
+
+    def step(events=None):
+        handles = []
+        for l, (pk, pv) in enumerate(cache):
+            if events is not None:
+                events[l][0].record(stream)
+            qk_scores(qs[l], pk, inv, out=scores)
+            if events is not None:
+                events[l][1].record(stream)
+            p = softmax(scores)
+            if events is not None:
+                events[l][2].record(stream)
+            outs[l] = pv_out(p, pv)
+            if events is not None:
+                events[l][3].record(stream)
+            if world > 1:
+                handles.append(dist.all_gather_into_tensor(full[l], outs[l], async_op=True))
+        for h in handles:
+            h.wait()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(layers)]
+          for _ in range(args.steps)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t_start.record(stream)
+    for s in range(args.steps):
+        step(ev[s])
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    elapsed = t_start.elapsed_time(t_end)  # ms
+    key_ms = [ev[s][l][0].elapsed_time(ev[s][l][1]) for s in range(args.steps) for l in range(layers)]
+    sm_ms = [ev[s][l][1].elapsed_time(ev[s][l][2]) for s in range(args.steps) for l in range(layers)]
+    val_ms = [ev[s][l][2].elapsed_time(ev[s][l][3]) for s in range(args.steps) for l in range(layers)]
+    if world > 1:
+        t = torch.tensor([elapsed], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = float(t.item())
+    ms_step = elapsed / args.steps
+    total_tokens = wl.batch * T * layers
+    value = total_tokens / (ms_step / 1e3)
+
+    # e2e through the public API: pinned host q in, host output out, every step
+    e2e = None
+    if not args.no_e2e:
+        q_host = [q.cpu().pin_memory() for q in qs]
+        o_host = [torch.empty((world, wl.batch, Hq_l, 128), dtype=torch.float16).pin_memory()
+                  for _ in range(layers)]
+        q_dev = [torch.empty_like(q) for q in qs]
+        wsp = DecodeWorkspace()
+
+        def e2e_step():
+            handles = []
+            for l, (pk, pv) in enumerate(cache):
+                q_dev[l].copy_(q_host[l], non_blocking=True)
+                o = decode_attention(q_dev[l], pk, pv, inv, workspace=wsp)
+                if world > 1:
+                    handles.append((l, dist.all_gather_into_tensor(full[l], o, async_op=True)))
+                else:
+                    o_host[l][0].copy_(o, non_blocking=True)
+            for l, h in handles:
+                h.wait()
+                o_host[l].copy_(full[l], non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e_el = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([e_el], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_el = float(t.item())
+        e2e = {"value": total_tokens / (e_el / args.steps / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": sum(q.numel() * 2 for q in qs),
+               "d2h_bytes_per_step": layers * world * wl.batch * Hq_l * 128 * 2}
+
+    # roofline of the dominant kernel
+    pk0, pv0 = cache[0]
+    ab = algorithmic_bytes(wl, pk0, pv0, hl, T)
+    k_avg, v_avg, s_avg = (statistics.mean(key_ms), statistics.mean(val_ms),
+                           statistics.mean(sm_ms))
+    dom, dom_ms = ("key_scores", k_avg) if k_avg >= v_avg else ("value_output", v_avg)
+    peak, peak_src = peak_hbm()
+    achieved = ab[dom] / (dom_ms / 1e3) / 1e9
+    step_bytes = sum(ab.values()) * layers
+    result = None
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            cpu = cpu_baseline(wl, dev, log)
+        result = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": wl.name, "batch": wl.batch, "kv_heads": wl.kv_heads,
+                       "q_per_kv": G, "tokens": T, "layers": layers, "bits": wl.bits,
+                       "outlier_ratio": wl.outlier_ratio, "rope_base": wl.rope_base,
+                       "sharding": f"kv heads / {world} GPUs",
+                       "l2": f"inputs larger than L2 ({step_bytes / world / 1e9:.1f} GB read "
+                             f"per GPU per step)"},
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
+                         "peak_source": peak_src, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None,
+                         "bytes_per_launch": ab[dom], "launch_ms": dom_ms},
+            "step_bandwidth_gbs": step_bytes / (ms_step / 1e3) / 1e9,
+            "kernels_ms": {"key_scores": k_avg, "softmax": s_avg, "value_output": v_avg},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": n_launch_per_layer * layers * args.steps,
+            "clocks": clk,
+        }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# CPU port (the reference's algorithm restated in numpy) -- baseline and the
+# reference arm
+# ---------------------------------------------------------------------------
+def _cpu_unit(args):
+    """One worker: dequantize + decode one unit of the packed sample (fp32 numpy)."""
+    from oracle import kvq_oracle as O
+    (kc, kv_, kp, kr, ks, kz, kcb, ksink, vc, vv, vp, vr, vs, vz, vcb, vsink, q, inv, bits, T) = args
+    t0 = time.perf_counter()
+    kh = O.dequant_packed(kc, kv_, kp, kr, ks, kz, kcb, bits, "k", T, ksink)
+    vh = O.dequant_packed(vc, vv, vp, vr, vs, vz, vcb, bits, "v", T, vsink)
+    O.decode_packed(q, kh, vh, inv)
+    return time.perf_counter() - t0
+
+
+def make_cpu_sample(wl, dev, units: int, T: int):
+    """Packed cache of `units` KV heads (one layer, T tokens) copied to host arrays."""
+    import numpy as np
+    import torch
+    from kvquant import synthetic as syn
+    from kvquant.kernels import quantize_keys, quantize_values, rope_inv_freq
+
+    C = wl.channels
+    k = torch.empty((1, T, C), dtype=torch.float16, device=dev)
+    v = torch.empty((1, T, C), dtype=torch.float16, device=dev)
+    syn.fill_layer(k, v, 0, seed=0)
+    ks, kz = syn.key_calibration(k)
+    cbk, cbv = syn.fit_codebooks(k, v, ks, kz, wl.bits)
+    pk = quantize_keys(k, ks, kz, cbk, wl.bits, wl.outlier_ratio, True, n_heads=units)
+    pv = quantize_values(v, cbv, wl.bits, wl.outlier_ratio, True, n_heads=units)
+    q = syn.make_query(1, wl.kv_heads * wl.q_per_kv, 0, 0, dev)[0, :units].cpu().numpy()
+    inv = rope_inv_freq(128, wl.rope_base).numpy()
+    nt = -(-T // 32)
+    h = lambda x: x.cpu().numpy()  # noqa: E731
+    tasks = []
+    kr_all, vr_all = h(pk["outlier_rowptr"]), h(pv["outlier_rowptr"])
+    kv_all, kp_all = h(pk["outlier_values"]), h(pk["outlier_cols"]).view(np.uint16)
+    vv_all, vp_all = h(pv["outlier_values"]), h(pv["outlier_cols"]).view(np.uint16)
+    for u in range(units):
+        def seg(rp, vals, pos):
+            a, b = int(rp[u * nt]), int(rp[(u + 1) * nt])
+            r = (rp[u * nt:(u + 1) * nt + 1] - a).astype(np.int32)
+            return vals[a:b], pos[a:b], r
+        kvals, kpos, krp = seg(kr_all, kv_all, kp_all)
+        vvals, vpos, vrp = seg(vr_all, vv_all, vp_all)
+        tasks.append((h(pk["q_idx"][u:u + 1]), kvals, kpos, krp,
+                      h(pk["scale"])[u * 128:(u + 1) * 128][None], h(pk["zero"])[u * 128:(u + 1) * 128][None],
+                      h(pk["codebook"]), h(pk["sink"])[0:1, u * 128:(u + 1) * 128],
+                      h(pv["q_idx"][u:u + 1]), vvals, vpos, vrp, h(pv["scale"]), h(pv["zero"]),
+                      h(pv["codebook"]), h(pv["sink"])[0:1, u * 128:(u + 1) * 128],
+                      q[u:u + 1], inv, wl.bits, T))
+    del k, v
+    torch.cuda.empty_cache()
+    return tasks
+
+
+def _pool(n):
+    import multiprocessing as mp
+    return mp.get_context("spawn").Pool(n)
+
+
+def cpu_measure(tasks, pool, wl):
+    t0 = time.perf_counter()
+    pool.map(_cpu_unit, tasks)
+    wall = time.perf_counter() - t0
+    T = tasks[0][-1]
+    units = len(tasks)
+    # one "token" of the metric = one cached position with all KV heads of a layer
+    return (T * units / wl.kv_heads) / wall, wall
+
+
+def cpu_baseline(wl, dev, log):
+    cores = os.cpu_count() or 1
+    units = min(wl.kv_heads, max(2, cores))
+    T = min(wl.tokens, 1 << 16)
+    tasks = make_cpu_sample(wl, dev, units, T)
+    with _pool(min(cores, units)) as pool:
+        cpu_measure(tasks[:1], pool, wl)  # warm the workers
+        val, wall = cpu_measure(tasks, pool, wl)
+    log(f"cpu baseline: {val:.3g} tokens/s ({wall:.1f}s)")
+    return {"value": val, "unit": UNIT, "cores": min(cores, units), "kind": "port",
+            "sample": f"1 layer x {units} KV heads x {T} tokens of {wl.name}; numpy port "
+                      f"(dequant + RoPE + q.K + softmax + p.V), {min(cores, units)} processes"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+    from kvquant import synthetic as syn
+
+    wl = syn.WORKLOADS[args.workload]
+    cores = os.cpu_count() or 1
+    units = min(wl.kv_heads, max(2, cores))
+    T = min(wl.tokens, 1 << 15)
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    with _pool(min(cores, units)) as pool:  # started before the first GPU call
+        tasks = make_cpu_sample(wl, dev, units, T)
+        for _ in range(args.warmup):
+            cpu_measure(tasks, pool, wl)
+        vals, walls = [], []
+        for _ in range(args.steps):
+            v, w = cpu_measure(tasks, pool, wl)
+            vals.append(v)
+            walls.append(w)
+    value = statistics.mean(vals)
+    sample = (f"each step: 1 layer x {units} KV heads x {T} tokens of {wl.name}, numpy port of "
+              f"the reference path on {min(cores, units)} processes; value scaled to all "
+              f"{wl.kv_heads} heads")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": statistics.mean(walls) * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl.name, "batch": wl.batch, "kv_heads": wl.kv_heads,
+                   "tokens": wl.tokens, "layers": wl.layers, "bits": wl.bits},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": min(cores, units), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,174 @@
+/*
+ * kvquant_b200 -- C ABI of the B200 (sm_100a) KVQuant decode-time quantized-KV
+ * attention path.
+ *
+ * Conventions
+ *   - Every entry point returns KVQ_OK (0) or an error code; kvq_last_error()
+ *     returns a message for the calling thread's last failure.
+ *   - All pointers are device pointers unless stated otherwise. fp16 buffers
+ *     are passed as void* (IEEE binary16). `stream` is a cudaStream_t (NULL =
+ *     legacy default stream). Calls are asynchronous and allocate nothing:
+ *     scratch comes from the caller through (workspace, workspace_bytes),
+ *     sized by the matching *_workspace() query.
+ *   - Layout of the quantized cache (per layer; unit u = b*n_heads + h):
+ *       codes    uint8 [U, nt_cap, 512*bits]: tiles of 32 tokens; tile = 4
+ *                chunks x 32 tokens x (4*bits)-byte slabs; slab (j,i) at
+ *                byte (j*32+i)*4*bits; pair m at bits [2*bits*m, +2*bits).
+ *                Keys: pair m of chunk j = channels (16j+m, 64+16j+m).
+ *                Values: pair m of chunk j = channels (32j+2m, 32j+2m+1).
+ *       outliers CSR over rows (u, tile): ptr int32 [U*nt_cap+1],
+ *                vals fp16 [nnz] (normalized raw value), pos uint16 [nnz] =
+ *                (token_in_tile << 7) | channel_in_head.
+ *       sink     fp16 [B, n_heads*128]: token 0 kept unquantized.
+ *       keys:    scale/zero fp32 [n_heads*128] (per channel, calibrated).
+ *       values:  scale/zero fp32 [B, ld] (per token, over all C channels).
+ *   - head_dim is 128; bits is 2, 3 or 4.
+ */
+#ifndef KVQUANT_B200_H
+#define KVQUANT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KVQ_OK 0
+#define KVQ_ERR_INVALID 1
+#define KVQ_ERR_CUDA 2
+#define KVQ_ERR_UNSUPPORTED 3
+
+/* Message of the calling thread's last error ("" if none). */
+const char* kvq_last_error(void);
+/* ABI version (major*100 + minor). */
+int kvq_version(void);
+
+/* ---------------------------------------------------------------------------
+ * The reference's four ops (kvquant/kernels/csrc/kvquant_ops.cu:265-270).
+ * ------------------------------------------------------------------------- */
+
+/* Replaces rope_apply (kvquant/kernels/csrc/kvquant_ops.cu:156-182):
+ * rotate-half RoPE of x [B,H,S,D] fp16 with fp32 tables cos/sin [s_total, D/2]
+ * at positions s + pos_offset; out fp16 [B,H,S,D]. */
+int kvq_rope_apply(const void* x, const float* cos_tab, const float* sin_tab, void* out,
+                   int64_t B, int64_t H, int64_t S, int64_t D, int64_t pos_offset,
+                   int64_t s_total, void* stream);
+
+/* Replaces lut_matvec (kvquant/kernels/csrc/kvquant_ops.cu:184-216):
+ * out[i] = sum_j (lut[qmat[i,j]]*scale[s] + zero[s]) * vec[j], s = j if
+ * per_channel else i. qmat uint8 [N,D]; lut fp16 [lut_size <= 256];
+ * scale/zero fp16 [D] or [N]; vec fp16 [D]; out fp16 [N]. */
+int kvq_lut_matvec(const uint8_t* qmat, const void* lut, int64_t lut_size, const void* scale,
+                   const void* zero, const void* vec, void* out, int64_t N, int64_t D,
+                   int per_channel, void* stream);
+
+/* Replaces sparse_matvec_csr (kvquant/kernels/csrc/kvquant_ops.cu:218-241):
+ * out[r] = sum_{k in [row_ptr[r], row_ptr[r+1])} values[k] * vec[col_idx[k]].
+ * row_ptr int32 [R+1]; col_idx int32 [nnz]; values/vec/out fp16. Entries
+ * whose column is outside [0, vec_len) are skipped and make the call fail
+ * with KVQ_ERR_INVALID at the next kvq_check_status(). */
+int kvq_sparse_matvec_csr(const int32_t* row_ptr, const int32_t* col_idx, const void* values,
+                          const void* vec, void* out, int64_t R, int64_t nnz, int64_t vec_len,
+                          void* stream);
+
+/* Replaces lut_lookup (kvquant/kernels/csrc/kvquant_ops.cu:243-263):
+ * nearest centroid (first minimum) of x fp32 [N] in codebook fp32 [lut_size];
+ * idx_out int64 [N], dq_out fp32 [N]. */
+int kvq_lut_lookup(const float* x, const float* codebook, int64_t lut_size, int64_t* idx_out,
+                   float* dq_out, int64_t N, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Quantize-on-append (prefill block). Semantics of KVQuantizer.quantize_k /
+ * quantize_v (kvquant/quant/kv_quantizer.py:72-122) with dense-and-sparse
+ * outliers (kvquant/quant/dense_sparse.py:4-32): codes, outlier positions
+ * and fp16 outlier values match the reference bit for bit (ties at the top-k
+ * threshold: lower token / channel index wins).
+ *
+ * Input x [B, S, C_full] fp16 (the k_proj / v_proj output); the call handles
+ * heads [h0, h0+n_heads). Token 0 becomes the fp16 sink when sink && S > 1.
+ * Two phases: *_plan computes thresholds, per-(unit,tile) outlier counts,
+ * out_ptr and the total nnz (device int64); *_emit writes the codes, outlier
+ * entries, sink and (optionally) the fake-quant dequantized output
+ * [B, S, n_heads*128] fp16 -- the reference's return value.
+ * ------------------------------------------------------------------------- */
+size_t kvq_quantize_keys_workspace(int64_t B, int64_t S, int64_t n_heads);
+int kvq_quantize_keys_plan(const void* k, int64_t B, int64_t S, int64_t C_full, int64_t h0,
+                           int64_t n_heads, const float* scale, const float* zero,
+                           double outlier_ratio, int sink, int32_t* out_ptr, int64_t nt_cap,
+                           int64_t* nnz_out, void* workspace, size_t workspace_bytes,
+                           void* stream);
+int kvq_quantize_keys_emit(const void* k, int64_t B, int64_t S, int64_t C_full, int64_t h0,
+                           int64_t n_heads, const float* scale, const float* zero,
+                           const float* codebook, int bits, double outlier_ratio, int sink,
+                           uint8_t* codes, int64_t nt_cap, const int32_t* out_ptr,
+                           void* out_vals, uint16_t* out_pos, int64_t nnz_cap, void* sink_out,
+                           void* dequant_out, const void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+size_t kvq_quantize_values_workspace(int64_t B, int64_t S, int64_t n_heads);
+int kvq_quantize_values_plan(const void* v, int64_t B, int64_t S, int64_t C_full, int64_t h0,
+                             int64_t n_heads, double outlier_ratio, int sink, float* v_scale,
+                             float* v_zero, int64_t ld_stats, int32_t* out_ptr, int64_t nt_cap,
+                             int64_t* nnz_out, void* workspace, size_t workspace_bytes,
+                             void* stream);
+int kvq_quantize_values_emit(const void* v, int64_t B, int64_t S, int64_t C_full, int64_t h0,
+                             int64_t n_heads, const float* codebook, int bits,
+                             double outlier_ratio, int sink, const float* v_scale,
+                             const float* v_zero, int64_t ld_stats, uint8_t* codes,
+                             int64_t nt_cap, const int32_t* out_ptr, void* out_vals,
+                             uint16_t* out_pos, int64_t nnz_cap, void* sink_out,
+                             void* dequant_out, const void* workspace, size_t workspace_bytes,
+                             void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Decode attention over the packed cache (T cached tokens at positions
+ * 0..T-1, token 0 = sink). q fp16 [B, n_heads*group, 128] (already rotated
+ * to its own position); query head hq reads KV head hq / group.
+ * ------------------------------------------------------------------------- */
+
+/* Fused key kernel: scores[b,hq,t] = q . RoPE_t(Khat_t) (raw, unscaled) fp32
+ * [B, n_heads*group, T]. inv_freq fp32 [64] (rope_fused.py:7-8). */
+int kvq_key_scores(const uint8_t* codes, const void* out_vals, const uint16_t* out_pos,
+                   const int32_t* out_ptr, const float* k_scale, const float* k_zero,
+                   const void* k_sink, const float* codebook, int bits, const void* q,
+                   const float* inv_freq, int64_t B, int64_t n_heads, int64_t group,
+                   int64_t T, int64_t nt_cap, float* scores, void* stream);
+
+/* probs = softmax(scores * scale) along the last axis; rows x T fp32. */
+size_t kvq_softmax_workspace(int64_t rows, int64_t T);
+int kvq_softmax(const float* scores, int64_t rows, int64_t T, float scale, float* probs,
+                void* workspace, size_t workspace_bytes, void* stream);
+
+/* Value kernel: out[b,hq,:] = sum_t probs[b,hq,t] * Vhat_t (fp16 [B, Hq, 128]). */
+size_t kvq_value_output_workspace(int64_t B, int64_t n_heads, int64_t group, int64_t T);
+int kvq_value_output(const uint8_t* codes, const void* out_vals, const uint16_t* out_pos,
+                     const int32_t* out_ptr, const float* v_scale, const float* v_zero,
+                     int64_t ld_stats, const void* v_sink, const float* codebook, int bits,
+                     const float* probs, int64_t B, int64_t n_heads, int64_t group, int64_t T,
+                     int64_t nt_cap, void* out, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* scores -> softmax(scores / sqrt(128)) -> p.V in one call; scores_out and
+ * probs_out may be NULL (then they live in the workspace). */
+size_t kvq_decode_attention_workspace(int64_t B, int64_t n_heads, int64_t group, int64_t T);
+int kvq_decode_attention(const uint8_t* k_codes, const void* k_out_vals,
+                         const uint16_t* k_out_pos, const int32_t* k_out_ptr,
+                         const float* k_scale, const float* k_zero, const void* k_sink,
+                         const float* k_codebook, const uint8_t* v_codes,
+                         const void* v_out_vals, const uint16_t* v_out_pos,
+                         const int32_t* v_out_ptr, const float* v_scale, const float* v_zero,
+                         int64_t ld_stats, const void* v_sink, const float* v_codebook,
+                         int bits, const void* q, const float* inv_freq, int64_t B,
+                         int64_t n_heads, int64_t group, int64_t T, int64_t nt_cap, void* out,
+                         float* scores_out, float* probs_out, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* Reads and clears the device-side error flag set by kernels that skip
+ * out-of-range accesses (synchronizes `stream`). */
+int kvq_check_status(void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KVQUANT_B200_H */

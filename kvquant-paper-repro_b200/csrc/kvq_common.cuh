@@ -1,0 +1,115 @@
+// Shared definitions for the kvquant_b200 sm_100a kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+
+#include "../../include/kvquant_b200.h"
+
+namespace kvq {
+
+constexpr int kTileTokens = 32;   // tokens per code tile
+constexpr int kHeadDim = 128;     // channels per head
+constexpr int kPairs = 64;        // RoPE rotate-half pairs per head
+constexpr int kChunks = 4;        // slabs per token row (16 pairs each)
+constexpr int kPairsPerChunk = 16;
+
+__host__ __device__ inline int tile_bytes(int bits) { return kTileTokens * kHeadDim * bits / 8; }
+__host__ __device__ inline int slab_bytes(int bits) { return 4 * bits; }
+
+// Thread-local error message of the last failed entry point.
+void set_error(const char* fmt, ...);
+void clear_error();
+
+// Device-side sticky status word (set by kernels that skip an invalid access).
+// Single definition: the library is built as one translation unit (kvq_lib.cu).
+__device__ int g_status = 0;
+enum StatusBits : int { kStatusBadIndex = 1 };
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Returns KVQ_OK, or KVQ_ERR_CUDA with the message recorded.
+int check_launch(const char* what);
+
+// Outlier count k = max(1, min(int(n * ratio), n)) (kvquant/quant/dense_sparse.py:22-23),
+// with Python's float semantics (IEEE double product, truncation toward 0).
+inline int64_t outlier_count(int64_t n, double ratio) {
+  if (n <= 0) return 0;
+  int64_t k = (int64_t)(double(n) * ratio);
+  if (k > n) k = n;
+  if (k < 1) k = 1;
+  return k;
+}
+
+// Normalization n = (x - zero) / (scale + 1e-8) with IEEE fp32 rounding of every
+// step (kvquant/quant/kv_quantizer.py:82,110); never contracted into an FMA.
+__device__ __forceinline__ float normalize(float x, float zero, float scale) {
+  return __fdiv_rn(__fsub_rn(x, zero), __fadd_rn(scale, 1e-8f));
+}
+
+// First-minimum nearest centroid (kvquant/kernels/csrc/kvquant_ops.cu:141-148).
+__device__ __forceinline__ int nearest_centroid(float v, const float* cb, int n) {
+  float best_d = fabsf(__fsub_rn(v, cb[0]));
+  int best = 0;
+  for (int k = 1; k < n; ++k) {
+    float d = fabsf(__fsub_rn(v, cb[k]));
+    if (d < best_d) { best_d = d; best = k; }
+  }
+  return best;
+}
+
+// Fake-quant dequantization (q + o) * s + z with the reference's fp32 op order
+// (kvquant/quant/kv_quantizer.py:89,117): add, multiply, add, each rounded.
+__device__ __forceinline__ float dequant_ref(float cbq, float o, float s, float z) {
+  return __fadd_rn(__fmul_rn(__fadd_rn(cbq, o), s), z);
+}
+
+// Mixed-precision FMA: fp16 x fp16 (exact product) + fp32 -> fp32 (sm_100 `fma.rn.f32.f16`).
+__device__ __forceinline__ float fma_h(uint16_t a, uint16_t b, float c) {
+  float r;
+  asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(r) : "h"(a), "h"(b), "f"(c));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t lo16(uint32_t w) { return w & 0xffffu; }
+__device__ __forceinline__ uint32_t hi16(uint32_t w) { return w >> 16; }
+
+__device__ __forceinline__ uint32_t half2_bits(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Extracts the 2*bits-wide code pair m (0..15) from a slab held in registers
+// (little-endian bit stream of 4*bits bytes).
+template <int BITS>
+__device__ __forceinline__ uint32_t slab_pair(const uint32_t* w, int m) {
+  constexpr int W = 2 * BITS;
+  const int bit = W * m;
+  const int wi = bit >> 5, sh = bit & 31;
+  uint32_t lo = w[wi] >> sh;
+  if (sh + W > 32) lo |= w[wi + 1] << (32 - sh);
+  return lo & ((1u << W) - 1u);
+}
+
+}  // namespace kvq

@@ -1,0 +1,699 @@
+// Quantize-on-append for a prefill block: KVQuantizer.quantize_k / quantize_v
+// (kvquant/quant/kv_quantizer.py:72-122) with dense-and-sparse outliers
+// (kvquant/quant/dense_sparse.py:4-32), writing the packed cache layout.
+//
+// Keys are quantized per channel: outliers are the top-k |n| along tokens of
+// each (batch, channel) column, k = max(1, int((S - sink) * ratio)). Values are
+// quantized per token: scale/zero and the top-k run over all C channels of the
+// token row. Top-k selection is an exact radix select on the fp32 bits of |n|;
+// among values equal to the k-th largest, lower token (keys) / channel
+// (values) indices are taken first.
+#pragma once
+#include "kvq_common.cuh"
+
+namespace kvq {
+
+// Per-column / per-row selection result.
+struct Select {
+  uint32_t thr;     // fp32 bits of the k-th largest |n|
+  int32_t kleft;    // remaining rank inside the current radix prefix
+  int32_t tie_cut;  // |n| == thr is selected iff index <= tie_cut
+  int32_t ties;     // number of entries equal to thr (last radix pass)
+};
+
+__device__ __forceinline__ uint32_t abs_bits(float n) { return __float_as_uint(n) & 0x7fffffffu; }
+
+__device__ __forceinline__ bool selected(uint32_t ab, int32_t idx, const Select& s) {
+  return ab > s.thr || (ab == s.thr && idx <= s.tie_cut);
+}
+
+// ---------------------------------------------------------------------------
+// Keys: radix select along tokens, per (b, channel) column.
+// Columns are numbered col = b * CL + c, CL = n_heads * 128 local channels.
+// ---------------------------------------------------------------------------
+struct KeyShape {
+  const __half* k;
+  int64_t B, S, C_full, c0, CL;  // c0 = first local channel in the full row
+  int64_t off;                   // 1 when token 0 is the sink, else 0
+  const float* scale;            // [C_full]
+  const float* zero;
+};
+
+__device__ __forceinline__ float key_norm(const KeyShape& ks, int64_t b, int64_t t, int64_t c) {
+  const float x = __half2float(ks.k[(b * ks.S + t) * ks.C_full + ks.c0 + c]);
+  return normalize(x, ks.zero[ks.c0 + c], ks.scale[ks.c0 + c]);
+}
+
+constexpr int kHistCols = 32;  // columns per histogram CTA
+
+// Histogram of the radix digit at `shift` of |n| among entries matching the
+// prefix so far. grid = (CL/32 column groups, B, row blocks); block 256.
+__global__ void __launch_bounds__(256) key_hist_kernel(KeyShape ks, int shift,
+                                                       const Select* __restrict__ sel,
+                                                       uint32_t* __restrict__ hist,
+                                                       int64_t rows_per_block) {
+  __shared__ uint32_t h[kHistCols][256];
+  for (int i = threadIdx.x; i < kHistCols * 256; i += blockDim.x) (&h[0][0])[i] = 0;
+  __syncthreads();
+  const int64_t b = blockIdx.y;
+  const int64_t cg = (int64_t)blockIdx.x * kHistCols;
+  const int lc = threadIdx.x & 31;  // column inside the group
+  const int64_t c = cg + lc;
+  const int64_t col = b * ks.CL + c;
+  const uint32_t mask_hi = shift >= 24 ? 0u : (0xffffffffu << (shift + 8));
+  const uint32_t prefix = sel[col].thr & mask_hi;
+  const int64_t n_rest = ks.S - ks.off;
+  const int64_t r0 = (int64_t)blockIdx.z * rows_per_block;
+  const int64_t r1 = min(n_rest, r0 + rows_per_block);
+  for (int64_t r = r0 + (threadIdx.x >> 5); r < r1; r += (blockDim.x >> 5)) {
+    const uint32_t ab = abs_bits(key_norm(ks, b, r + ks.off, c));
+    if ((ab & mask_hi) == prefix) atomicAdd(&h[lc][(ab >> shift) & 0xffu], 1u);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kHistCols * 256; i += blockDim.x) {
+    const uint32_t v = (&h[0][0])[i];
+    if (v) atomicAdd(&hist[(b * ks.CL + cg + i / 256) * 256 + (i & 255)], v);
+  }
+}
+
+// One thread per column: picks the digit holding the k-th largest entry.
+__global__ void key_select_kernel(Select* __restrict__ sel, uint32_t* __restrict__ hist,
+                                  int64_t ncols, int shift) {
+  const int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= ncols) return;
+  uint32_t* hc = hist + col * 256;
+  Select s = sel[col];
+  int32_t k = s.kleft;
+  int d = 255;
+  for (; d > 0; --d) {
+    const int32_t n = (int32_t)hc[d];
+    if (k <= n) break;
+    k -= n;
+  }
+  s.thr |= (uint32_t)d << shift;
+  s.kleft = k;
+  s.ties = (int32_t)hc[d];
+  sel[col] = s;
+  for (int i = 0; i < 256; ++i) hc[i] = 0;  // ready for the next pass
+}
+
+// Columns where only some of the entries equal to thr are taken: one warp per
+// such column walks the tokens in order and records the index of the last tie
+// taken. Other columns take every tie (tie_cut = INT_MAX).
+__global__ void key_ties_kernel(KeyShape ks, Select* __restrict__ sel, int64_t ncols) {
+  const int64_t col = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (col >= ncols) return;
+  Select s = sel[col];
+  if (s.kleft >= s.ties) {
+    if (lane == 0) { s.tie_cut = 0x7fffffff; sel[col] = s; }
+    return;
+  }
+  const int64_t b = col / ks.CL, c = col % ks.CL;
+  const int64_t n_rest = ks.S - ks.off;
+  int32_t need = s.kleft;
+  int32_t cut = -1;
+  for (int64_t r0 = 0; r0 < n_rest && need > 0; r0 += 32) {
+    const int64_t r = r0 + lane;
+    const bool tie = r < n_rest && abs_bits(key_norm(ks, b, r + ks.off, c)) == s.thr;
+    const uint32_t bal = __ballot_sync(0xffffffffu, tie);
+    const int cnt = __popc(bal);
+    if (cnt >= need) {
+      // the need-th set bit of bal
+      uint32_t m = bal;
+      for (int i = 1; i < need; ++i) m &= m - 1;
+      cut = (int32_t)(r0 + (__ffs(m) - 1));
+      need = 0;
+    } else {
+      need -= cnt;
+    }
+  }
+  if (lane == 0) { s.tie_cut = cut; sel[col] = s; }
+}
+
+// ---------------------------------------------------------------------------
+// Values: one CTA per (b, token) row: per-token min/max over all C_full
+// channels, then radix select of the top-k |n| over those channels.
+// ---------------------------------------------------------------------------
+constexpr int kValRowMax = 16384;  // channels per value row held in smem
+
+__global__ void __launch_bounds__(256) value_plan_kernel(
+    const __half* __restrict__ v, int64_t B, int64_t S, int64_t C_full, int64_t off,
+    int64_t kv, float* __restrict__ v_scale, float* __restrict__ v_zero, int64_t ld_stats,
+    Select* __restrict__ sel) {
+  extern __shared__ uint32_t vsm[];  // C_full |n| bits
+  __shared__ uint32_t hist[256];
+  __shared__ float red_min[8], red_max[8];
+  __shared__ int32_t sh_kleft, sh_digit, sh_ties, sh_cut;
+  const int64_t row = blockIdx.x;  // over B * (S - off)
+  const int64_t n_rest = S - off;
+  const int64_t b = row / n_rest, t = row % n_rest + off;
+  const __half* x = v + (b * S + t) * C_full;
+  float mn = INFINITY, mx = -INFINITY;
+  for (int64_t c = threadIdx.x; c < C_full; c += blockDim.x) {
+    const float f = __half2float(x[c]);
+    mn = fminf(mn, f);
+    mx = fmaxf(mx, f);
+  }
+  mn = -warp_max(-mn);
+  mx = warp_max(mx);
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { red_min[w] = mn; red_max[w] = mx; }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float a = lane < (int)(blockDim.x >> 5) ? red_min[lane] : INFINITY;
+    float m2 = lane < (int)(blockDim.x >> 5) ? red_max[lane] : -INFINITY;
+    a = -warp_max(-a);
+    m2 = warp_max(m2);
+    if (lane == 0) { red_min[0] = a; red_max[0] = m2; }
+  }
+  __syncthreads();
+  // kv_quantizer.py:106-107: scale = (max - min) / 2, zero = (max + min) / 2 (fp32).
+  const float scale = __fdiv_rn(__fsub_rn(red_max[0], red_min[0]), 2.0f);
+  const float zero = __fdiv_rn(__fadd_rn(red_max[0], red_min[0]), 2.0f);
+  if (threadIdx.x == 0) {
+    v_scale[b * ld_stats + t] = scale;
+    v_zero[b * ld_stats + t] = zero;
+  }
+  for (int64_t c = threadIdx.x; c < C_full; c += blockDim.x)
+    vsm[c] = abs_bits(normalize(__half2float(x[c]), zero, scale));
+  if (threadIdx.x == 0) sh_kleft = (int32_t)kv;
+  __syncthreads();
+  uint32_t prefix = 0;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    const uint32_t mask_hi = shift >= 24 ? 0u : (0xffffffffu << (shift + 8));
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int64_t c = threadIdx.x; c < C_full; c += blockDim.x) {
+      const uint32_t ab = vsm[c];
+      if ((ab & mask_hi) == prefix) atomicAdd(&hist[(ab >> shift) & 0xffu], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int32_t k = sh_kleft;
+      int d = 255;
+      for (; d > 0; --d) {
+        const int32_t n = (int32_t)hist[d];
+        if (k <= n) break;
+        k -= n;
+      }
+      sh_kleft = k;
+      sh_digit = d;
+      sh_ties = (int32_t)hist[d];
+    }
+    __syncthreads();
+    prefix |= (uint32_t)sh_digit << shift;
+    __syncthreads();
+  }
+  // Tie cut: the channel index of the kleft-th entry equal to the threshold.
+  if (threadIdx.x == 0) sh_cut = 0x7fffffff;
+  __syncthreads();
+  if (sh_kleft < sh_ties) {
+    if (threadIdx.x < 32) {
+      int32_t need = sh_kleft;
+      for (int64_t c0 = 0; c0 < C_full && need > 0; c0 += 32) {
+        const int64_t c = c0 + lane;
+        const bool tie = c < C_full && vsm[c] == prefix;
+        const uint32_t bal = __ballot_sync(0xffffffffu, tie);
+        const int cnt = __popc(bal);
+        if (cnt >= need) {
+          uint32_t m = bal;
+          for (int i = 1; i < need; ++i) m &= m - 1;
+          if (lane == 0) sh_cut = (int32_t)(c0 + (__ffs(m) - 1));
+          need = 0;
+        } else {
+          need -= cnt;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    Select s;
+    s.thr = prefix;
+    s.kleft = sh_kleft;
+    s.ties = sh_ties;
+    s.tie_cut = sh_cut;
+    sel[b * S + t] = s;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Emit: one CTA (128 threads = 4 chunks x 32 tokens) per (b, tile, head).
+// KIND 0 = keys, 1 = values. COUNT_ONLY: write the per-(unit,tile) outlier
+// count into out_ptr[unit*nt_cap + tile + 1] (prefix-summed afterwards).
+// ---------------------------------------------------------------------------
+struct EmitArgs {
+  const __half* x;
+  int64_t B, S, C_full, h0, H, off;
+  const float* k_scale;  // keys: [C_full]
+  const float* k_zero;
+  const float* v_scale;  // values: [B, ld]
+  const float* v_zero;
+  int64_t ld_stats;
+  const Select* sel;     // keys: [B * CL] columns; values: [B * S] rows
+  const float* cb;
+  int bits;
+  uint8_t* codes;
+  int64_t nt_cap;
+  int32_t* out_ptr;
+  __half* out_vals;
+  uint16_t* out_pos;
+  int64_t nnz_cap;
+  __half* sink_out;     // [B, H*128] or null
+  __half* dequant_out;  // [B, S, H*128] or null
+};
+
+// Channel within head of code slot q (0..31) of chunk j.
+template <int KIND>
+__device__ __forceinline__ int slot_channel(int j, int q) {
+  const int m = q >> 1, sec = q & 1;
+  return KIND == 0 ? (16 * j + m + 64 * sec) : (32 * j + 2 * m + sec);
+}
+
+template <int KIND, bool COUNT_ONLY>
+__global__ void __launch_bounds__(128) emit_kernel(EmitArgs a) {
+  __shared__ int32_t cnt[32][8];  // per token, per 16-channel group (channel order)
+  __shared__ float s_cb[16];
+  const int64_t b = blockIdx.y;
+  const int64_t tile = blockIdx.x;
+  const int64_t h = blockIdx.z;  // local head
+  const int j = threadIdx.x >> 5, i = threadIdx.x & 31;
+  const int64_t t = tile * kTileTokens + i;
+  const int64_t unit = b * a.H + h;
+  const int ncb = 1 << a.bits;
+  if (!COUNT_ONLY && threadIdx.x < ncb) s_cb[threadIdx.x] = a.cb[threadIdx.x];
+  const bool is_sink = a.off == 1 && t == 0;
+  const bool live = t < a.S && !is_sink;
+  const int64_t CL = a.H * kHeadDim;
+  float sc_t = 0.f, z_t = 0.f;
+  Select rs;
+  if (KIND == 1 && live) {
+    sc_t = a.v_scale[b * a.ld_stats + t];
+    z_t = a.v_zero[b * a.ld_stats + t];
+    rs = a.sel[b * a.S + t];
+  }
+  __syncthreads();
+  uint32_t slab[4] = {0, 0, 0, 0};  // up to 16 bytes (4-bit)
+  uint32_t omask = 0;                // outlier flag per code slot
+  float nval[32];
+  const __half* xrow = a.x + (b * a.S + (t < a.S ? t : 0)) * a.C_full + (a.h0 + h) * kHeadDim;
+#pragma unroll
+  for (int q = 0; q < 32; ++q) {
+    const int d = slot_channel<KIND>(j, q);
+    float n = 0.f;
+    int code = 0;
+    bool out = false;
+    if (live) {
+      const float xv = __half2float(xrow[d]);
+      if (KIND == 0) {
+        const int64_t cfull = (a.h0 + h) * kHeadDim + d;
+        n = normalize(xv, a.k_zero[cfull], a.k_scale[cfull]);
+        const Select cs = a.sel[b * CL + h * kHeadDim + d];
+        out = a.nnz_cap >= 0 && selected(abs_bits(n), (int32_t)(t - a.off), cs);
+      } else {
+        n = normalize(xv, z_t, sc_t);
+        out = a.nnz_cap >= 0 && selected(abs_bits(n), (int32_t)((a.h0 + h) * kHeadDim + d), rs);
+      }
+      if (!COUNT_ONLY) {
+        const float dense = out ? 0.f : fminf(fmaxf(n, -1.f), 1.f);
+        code = nearest_centroid(dense, s_cb, ncb);
+      }
+    }
+    nval[q] = n;
+    if (out) omask |= 1u << q;
+    if (!COUNT_ONLY) {
+      const int bit = q * a.bits;
+      slab[bit >> 5] |= (uint32_t)code << (bit & 31);
+      if ((bit & 31) + a.bits > 32) slab[(bit >> 5) + 1] |= (uint32_t)code >> (32 - (bit & 31));
+    }
+  }
+  // Outlier counts per (token, 16-channel group in channel order).
+  if (KIND == 0) {
+    cnt[i][j] = __popc(omask & 0x55555555u);      // channels 16j..16j+15
+    cnt[i][4 + j] = __popc(omask & 0xaaaaaaaau);  // channels 64+16j..
+  } else {
+    cnt[i][2 * j] = __popc(omask & 0x0000ffffu);  // channels 32j..32j+15
+    cnt[i][2 * j + 1] = __popc(omask & 0xffff0000u);
+  }
+  __syncthreads();
+  if (COUNT_ONLY) {
+    if (threadIdx.x == 0) {
+      int32_t tot = 0;
+      for (int r = 0; r < 32 * 8; ++r) tot += (&cnt[0][0])[r];
+      a.out_ptr[unit * a.nt_cap + tile + 1] = tot;
+    }
+    return;
+  }
+  // Exclusive prefix over (token, group) in order -> entry offsets.
+  if (threadIdx.x == 0) {
+    int32_t run = 0;
+    for (int r = 0; r < 32 * 8; ++r) {
+      const int32_t v = (&cnt[0][0])[r];
+      (&cnt[0][0])[r] = run;
+      run += v;
+    }
+  }
+  __syncthreads();
+  const int64_t base = a.out_ptr[unit * a.nt_cap + tile];
+  // Slab store.
+  const int sb = slab_bytes(a.bits);
+  uint8_t* dst = a.codes + (unit * a.nt_cap + tile) * (int64_t)tile_bytes(a.bits) +
+                 (int64_t)(j * 32 + i) * sb;
+  for (int w = 0; w < sb / 4; ++w) reinterpret_cast<uint32_t*>(dst)[w] = slab[w];
+  // Outlier entries in (token, channel) order.
+  if (omask) {
+    int32_t o0, o1;
+    if (KIND == 0) { o0 = cnt[i][j]; o1 = cnt[i][4 + j]; }
+    else { o0 = cnt[i][2 * j]; o1 = cnt[i][2 * j + 1]; }
+    // first group: KIND0 even slots (m ascending), KIND1 slots 0..15
+#pragma unroll
+    for (int q = 0; q < 32; ++q) {
+      const bool first = KIND == 0 ? ((q & 1) == 0) : (q < 16);
+      if (!first || !(omask & (1u << q))) continue;
+      const int64_t e = base + o0++;
+      if (e < a.nnz_cap) {
+        a.out_vals[e] = __float2half_rn(nval[q]);
+        a.out_pos[e] = (uint16_t)((i << 7) | slot_channel<KIND>(j, q));
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 32; ++q) {
+      const bool second = KIND == 0 ? ((q & 1) == 1) : (q >= 16);
+      if (!second || !(omask & (1u << q))) continue;
+      const int64_t e = base + o1++;
+      if (e < a.nnz_cap) {
+        a.out_vals[e] = __float2half_rn(nval[q]);
+        a.out_pos[e] = (uint16_t)((i << 7) | slot_channel<KIND>(j, q));
+      }
+    }
+  }
+  // Sink copy and fake-quant output.
+  const int64_t cl0 = h * kHeadDim;
+  if (is_sink && a.sink_out) {
+    for (int q = 0; q < 32; ++q) {
+      const int d = slot_channel<KIND>(j, q);
+      a.sink_out[b * CL + cl0 + d] = xrow[d];
+    }
+  }
+  if (a.dequant_out && t < a.S) {
+    __half* drow = a.dequant_out + (b * a.S + t) * CL + cl0;
+#pragma unroll
+    for (int q = 0; q < 32; ++q) {
+      const int d = slot_channel<KIND>(j, q);
+      if (is_sink) { drow[d] = xrow[d]; continue; }
+      const int bit = q * a.bits;
+      uint32_t code = slab[bit >> 5] >> (bit & 31);
+      if ((bit & 31) + a.bits > 32) code |= slab[(bit >> 5) + 1] << (32 - (bit & 31));
+      code &= (1u << a.bits) - 1u;
+      const bool out = (omask >> q) & 1u;
+      float s, z;
+      if (KIND == 0) {
+        const int64_t cfull = (a.h0 + h) * kHeadDim + d;
+        s = a.k_scale[cfull];
+        z = a.k_zero[cfull];
+      } else {
+        s = sc_t;
+        z = z_t;
+      }
+      drow[d] = __float2half_rn(dequant_ref(s_cb[code], out ? nval[q] : 0.f, s, z));
+    }
+  }
+}
+
+// Single-CTA exclusive scan of counts stored at ptr[1..n] (ptr[0] = 0) and the
+// total nnz. n is U * nt_cap.
+__global__ void __launch_bounds__(1024) scan_counts_kernel(int32_t* __restrict__ ptr, int64_t n,
+                                                           int64_t* __restrict__ nnz_out) {
+  __shared__ int64_t part[1024];
+  const int64_t per = (n + blockDim.x - 1) / blockDim.x;
+  const int64_t s = threadIdx.x * per, e = min(n, s + per);
+  int64_t sum = 0;
+  for (int64_t i = s; i < e; ++i) sum += ptr[i + 1];
+  part[threadIdx.x] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int64_t run = 0;
+    for (int i = 0; i < (int)blockDim.x; ++i) {
+      const int64_t v = part[i];
+      part[i] = run;
+      run += v;
+    }
+    ptr[0] = 0;
+    if (nnz_out) *nnz_out = run;
+  }
+  __syncthreads();
+  int64_t run = part[threadIdx.x];
+  for (int64_t i = s; i < e; ++i) {
+    run += ptr[i + 1];
+    ptr[i + 1] = (int32_t)run;
+  }
+}
+
+__global__ void init_select_kernel(Select* __restrict__ sel, int64_t n, int32_t k) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) {
+    Select s;
+    s.thr = 0;
+    s.kleft = k;
+    s.tie_cut = 0x7fffffff;
+    s.ties = 0;
+    sel[i] = s;
+  }
+}
+
+__global__ void zero_i32_kernel(int32_t* __restrict__ p, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    p[i] = 0;
+}
+
+// Workspace layout.
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+inline size_t key_ws_bytes(int64_t B, int64_t n_heads) {
+  const int64_t ncols = B * n_heads * kHeadDim;
+  return align256(ncols * sizeof(Select)) + align256(ncols * 256 * sizeof(uint32_t));
+}
+inline size_t value_ws_bytes(int64_t B, int64_t S) {
+  return align256((size_t)B * S * sizeof(Select));
+}
+
+inline bool bits_ok(int bits) { return bits >= 2 && bits <= 4; }
+
+}  // namespace kvq
+
+extern "C" size_t kvq_quantize_keys_workspace(int64_t B, int64_t S, int64_t n_heads) {
+  (void)S;
+  return kvq::key_ws_bytes(B, n_heads);
+}
+
+extern "C" size_t kvq_quantize_values_workspace(int64_t B, int64_t S, int64_t n_heads) {
+  (void)n_heads;
+  return kvq::value_ws_bytes(B, S);
+}
+
+namespace kvq {
+
+static int check_block(const char* what, int64_t B, int64_t S, int64_t C_full, int64_t h0,
+                       int64_t n_heads, int64_t nt_cap) {
+  if (B < 1 || S < 1 || n_heads < 1 || h0 < 0 || C_full < (h0 + n_heads) * kHeadDim) {
+    set_error("%s: invalid shape B=%lld S=%lld C_full=%lld heads [%lld, %lld)", what,
+              (long long)B, (long long)S, (long long)C_full, (long long)h0,
+              (long long)(h0 + n_heads));
+    return KVQ_ERR_INVALID;
+  }
+  if (nt_cap * kTileTokens < S) {
+    set_error("%s: nt_cap=%lld tiles cannot hold S=%lld tokens", what, (long long)nt_cap,
+              (long long)S);
+    return KVQ_ERR_INVALID;
+  }
+  if (S > (1LL << 30) || B * n_heads * nt_cap >= (1LL << 31)) {
+    set_error("%s: block too large", what);
+    return KVQ_ERR_INVALID;
+  }
+  return KVQ_OK;
+}
+
+}  // namespace kvq
+
+extern "C" int kvq_quantize_keys_plan(const void* k, int64_t B, int64_t S, int64_t C_full,
+                                      int64_t h0, int64_t n_heads, const float* scale,
+                                      const float* zero, double outlier_ratio, int sink,
+                                      int32_t* out_ptr, int64_t nt_cap, int64_t* nnz_out,
+                                      void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace kvq;
+  clear_error();
+  int rc = check_block("quantize_keys_plan", B, S, C_full, h0, n_heads, nt_cap);
+  if (rc) return rc;
+  if (workspace_bytes < key_ws_bytes(B, n_heads) || !workspace) {
+    set_error("quantize_keys_plan: workspace too small (%zu < %zu)", workspace_bytes,
+              key_ws_bytes(B, n_heads));
+    return KVQ_ERR_INVALID;
+  }
+  cudaStream_t st = as_stream(stream);
+  const int64_t CL = n_heads * kHeadDim, ncols = B * CL;
+  Select* sel = reinterpret_cast<Select*>(workspace);
+  uint32_t* hist = reinterpret_cast<uint32_t*>((char*)workspace + align256(ncols * sizeof(Select)));
+  KeyShape ks{(const __half*)k, B, S, C_full, h0 * kHeadDim, CL, (sink && S > 1) ? 1 : 0,
+              scale, zero};
+  const int64_t n_rest = S - ks.off;
+  const bool outliers = outlier_ratio > 0;
+  const int64_t kk = outliers ? outlier_count(n_rest, outlier_ratio) : 0;
+  init_select_kernel<<<(unsigned)((ncols + 255) / 256), 256, 0, st>>>(sel, ncols, (int32_t)kk);
+  if (outliers) {
+    cudaMemsetAsync(hist, 0, ncols * 256 * sizeof(uint32_t), st);
+    const int64_t rows_per_block = 4096;
+    dim3 hg((unsigned)(CL / kHistCols), (unsigned)B,
+            (unsigned)((n_rest + rows_per_block - 1) / rows_per_block));
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      key_hist_kernel<<<hg, 256, 0, st>>>(ks, shift, sel, hist, rows_per_block);
+      key_select_kernel<<<(unsigned)((ncols + 127) / 128), 128, 0, st>>>(sel, hist, ncols, shift);
+    }
+    key_ties_kernel<<<(unsigned)((ncols + 7) / 8), 256, 0, st>>>(ks, sel, ncols);
+  }
+  // Outlier counts per (unit, tile), then the row pointer.
+  const int64_t nrows = B * n_heads * nt_cap;
+  zero_i32_kernel<<<grid_for(nrows + 1, 256), 256, 0, st>>>(out_ptr, nrows + 1);
+  EmitArgs ea{};
+  ea.x = ks.k; ea.B = B; ea.S = S; ea.C_full = C_full; ea.h0 = h0; ea.H = n_heads;
+  ea.off = ks.off; ea.k_scale = scale; ea.k_zero = zero; ea.sel = sel; ea.bits = 2;
+  ea.nt_cap = nt_cap; ea.out_ptr = out_ptr; ea.nnz_cap = outliers ? 0 : -1;
+  const int64_t nt = (S + kTileTokens - 1) / kTileTokens;
+  ea.cb = nullptr;  // COUNT_ONLY never reads the codebook
+  emit_kernel<0, true><<<dim3((unsigned)nt, (unsigned)B, (unsigned)n_heads), 128, 0, st>>>(ea);
+  scan_counts_kernel<<<1, 1024, 0, st>>>(out_ptr, nrows, nnz_out);
+  return check_launch("quantize_keys_plan");
+}
+
+extern "C" int kvq_quantize_keys_emit(const void* k, int64_t B, int64_t S, int64_t C_full,
+                                      int64_t h0, int64_t n_heads, const float* scale,
+                                      const float* zero, const float* codebook, int bits,
+                                      double outlier_ratio, int sink, uint8_t* codes,
+                                      int64_t nt_cap, const int32_t* out_ptr, void* out_vals,
+                                      uint16_t* out_pos, int64_t nnz_cap, void* sink_out,
+                                      void* dequant_out, const void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+  using namespace kvq;
+  clear_error();
+  int rc = check_block("quantize_keys_emit", B, S, C_full, h0, n_heads, nt_cap);
+  if (rc) return rc;
+  if (!bits_ok(bits)) {
+    set_error("quantize_keys_emit: bits must be 2, 3 or 4 (got %d)", bits);
+    return KVQ_ERR_UNSUPPORTED;
+  }
+  if (workspace_bytes < key_ws_bytes(B, n_heads) || !workspace) {
+    set_error("quantize_keys_emit: workspace too small");
+    return KVQ_ERR_INVALID;
+  }
+  cudaStream_t st = as_stream(stream);
+  const int64_t nt = (S + kTileTokens - 1) / kTileTokens;
+  // Tiles beyond the block are cleared so stale codes never reach the decode kernels.
+  const int64_t tb = tile_bytes(bits);
+  if (nt_cap > nt)
+    for (int64_t u = 0; u < B * n_heads; ++u)
+      cudaMemsetAsync(codes + (u * nt_cap + nt) * tb, 0, (nt_cap - nt) * tb, st);
+  EmitArgs ea{};
+  ea.x = (const __half*)k; ea.B = B; ea.S = S; ea.C_full = C_full; ea.h0 = h0;
+  ea.H = n_heads; ea.off = (sink && S > 1) ? 1 : 0; ea.k_scale = scale; ea.k_zero = zero;
+  ea.sel = reinterpret_cast<const Select*>(workspace); ea.cb = codebook; ea.bits = bits;
+  ea.codes = codes; ea.nt_cap = nt_cap; ea.out_ptr = const_cast<int32_t*>(out_ptr);
+  ea.out_vals = (__half*)out_vals; ea.out_pos = out_pos;
+  ea.nnz_cap = outlier_ratio > 0 ? nnz_cap : -1;
+  ea.sink_out = (__half*)sink_out; ea.dequant_out = (__half*)dequant_out;
+  emit_kernel<0, false><<<dim3((unsigned)nt, (unsigned)B, (unsigned)n_heads), 128, 0, st>>>(ea);
+  return check_launch("quantize_keys_emit");
+}
+
+extern "C" int kvq_quantize_values_plan(const void* v, int64_t B, int64_t S, int64_t C_full,
+                                        int64_t h0, int64_t n_heads, double outlier_ratio,
+                                        int sink, float* v_scale, float* v_zero,
+                                        int64_t ld_stats, int32_t* out_ptr, int64_t nt_cap,
+                                        int64_t* nnz_out, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  using namespace kvq;
+  clear_error();
+  int rc = check_block("quantize_values_plan", B, S, C_full, h0, n_heads, nt_cap);
+  if (rc) return rc;
+  if (C_full > kValRowMax) {
+    set_error("quantize_values_plan: C=%lld channels exceed %d", (long long)C_full, kValRowMax);
+    return KVQ_ERR_UNSUPPORTED;
+  }
+  if (ld_stats < S) {
+    set_error("quantize_values_plan: ld_stats=%lld < S=%lld", (long long)ld_stats, (long long)S);
+    return KVQ_ERR_INVALID;
+  }
+  if (workspace_bytes < value_ws_bytes(B, S) || !workspace) {
+    set_error("quantize_values_plan: workspace too small");
+    return KVQ_ERR_INVALID;
+  }
+  cudaStream_t st = as_stream(stream);
+  Select* sel = reinterpret_cast<Select*>(workspace);
+  const int64_t off = (sink && S > 1) ? 1 : 0;
+  const int64_t n_rest = S - off;
+  const bool outliers = outlier_ratio > 0;
+  const int64_t kv = outliers ? outlier_count(C_full, outlier_ratio) : 0;
+  if (B * n_rest > 0) {
+    const size_t smem = C_full * sizeof(uint32_t);
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(value_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem);
+    value_plan_kernel<<<(unsigned)(B * n_rest), 256, smem, st>>>(
+        (const __half*)v, B, S, C_full, off, kv, v_scale, v_zero, ld_stats, sel);
+  }
+  if (off) {  // the sink token carries no stats
+    for (int64_t b = 0; b < B; ++b) {
+      cudaMemsetAsync(v_scale + b * ld_stats, 0, sizeof(float), st);
+      cudaMemsetAsync(v_zero + b * ld_stats, 0, sizeof(float), st);
+    }
+  }
+  const int64_t nrows = B * n_heads * nt_cap;
+  zero_i32_kernel<<<grid_for(nrows + 1, 256), 256, 0, st>>>(out_ptr, nrows + 1);
+  EmitArgs ea{};
+  ea.x = (const __half*)v; ea.B = B; ea.S = S; ea.C_full = C_full; ea.h0 = h0;
+  ea.H = n_heads; ea.off = off; ea.v_scale = v_scale; ea.v_zero = v_zero;
+  ea.ld_stats = ld_stats; ea.sel = sel; ea.cb = nullptr; ea.bits = 2; ea.nt_cap = nt_cap;
+  ea.out_ptr = out_ptr; ea.nnz_cap = outliers ? 0 : -1;
+  const int64_t nt = (S + kTileTokens - 1) / kTileTokens;
+  emit_kernel<1, true><<<dim3((unsigned)nt, (unsigned)B, (unsigned)n_heads), 128, 0, st>>>(ea);
+  scan_counts_kernel<<<1, 1024, 0, st>>>(out_ptr, nrows, nnz_out);
+  return check_launch("quantize_values_plan");
+}
+
+extern "C" int kvq_quantize_values_emit(const void* v, int64_t B, int64_t S, int64_t C_full,
+                                        int64_t h0, int64_t n_heads, const float* codebook,
+                                        int bits, double outlier_ratio, int sink,
+                                        const float* v_scale, const float* v_zero,
+                                        int64_t ld_stats, uint8_t* codes, int64_t nt_cap,
+                                        const int32_t* out_ptr, void* out_vals,
+                                        uint16_t* out_pos, int64_t nnz_cap, void* sink_out,
+                                        void* dequant_out, const void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  using namespace kvq;
+  clear_error();
+  int rc = check_block("quantize_values_emit", B, S, C_full, h0, n_heads, nt_cap);
+  if (rc) return rc;
+  if (!bits_ok(bits)) {
+    set_error("quantize_values_emit: bits must be 2, 3 or 4 (got %d)", bits);
+    return KVQ_ERR_UNSUPPORTED;
+  }
+  if (workspace_bytes < value_ws_bytes(B, S) || !workspace || ld_stats < S) {
+    set_error("quantize_values_emit: workspace too small or ld_stats < S");
+    return KVQ_ERR_INVALID;
+  }
+  cudaStream_t st = as_stream(stream);
+  const int64_t nt = (S + kTileTokens - 1) / kTileTokens;
+  const int64_t tb = tile_bytes(bits);
+  if (nt_cap > nt)
+    for (int64_t u = 0; u < B * n_heads; ++u)
+      cudaMemsetAsync(codes + (u * nt_cap + nt) * tb, 0, (nt_cap - nt) * tb, st);
+  EmitArgs ea{};
+  ea.x = (const __half*)v; ea.B = B; ea.S = S; ea.C_full = C_full; ea.h0 = h0;
+  ea.H = n_heads; ea.off = (sink && S > 1) ? 1 : 0; ea.v_scale = v_scale; ea.v_zero = v_zero;
+  ea.ld_stats = ld_stats; ea.sel = reinterpret_cast<const Select*>(workspace);
+  ea.cb = codebook; ea.bits = bits; ea.codes = codes; ea.nt_cap = nt_cap;
+  ea.out_ptr = const_cast<int32_t*>(out_ptr); ea.out_vals = (__half*)out_vals;
+  ea.out_pos = out_pos; ea.nnz_cap = outlier_ratio > 0 ? nnz_cap : -1;
+  ea.sink_out = (__half*)sink_out; ea.dequant_out = (__half*)dequant_out;
+  emit_kernel<1, false><<<dim3((unsigned)nt, (unsigned)B, (unsigned)n_heads), 128, 0, st>>>(ea);
+  return check_launch("quantize_values_emit");
+}

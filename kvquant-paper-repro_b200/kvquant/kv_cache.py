@@ -1,0 +1,49 @@
+"""Quantized KV cache container (drop-in for kvquant/kv_cache.py).
+
+Per-layer dict slots as in the reference (kv_cache.py:4-44), filled with the
+packed dicts that kvquant.kernels.quantize_keys / quantize_values return:
+q_idx (bit-packed codes in 32-token tiles), outlier_values (fp16),
+outlier_cols (int16 packed (token_in_tile, channel)), outlier_rowptr (int32
+per (head, tile)), scale and zero, plus the fp16 sink token. memory_bytes
+counts each tensor at its real element size (the reference counts int32
+columns as 2 bytes and fp32 scales as 2 bytes).
+"""
+from __future__ import annotations
+
+
+class QuantizedKVCache:
+    def __init__(self):
+        self.k_cache = []
+        self.v_cache = []
+        self.seq_len = 0
+
+    def append_k(self, layer_idx: int, packed_k: dict):
+        """kv_cache.py:17-20: stores the layer's packed keys (overwrites the slot)."""
+        while len(self.k_cache) <= layer_idx:
+            self.k_cache.append(None)
+        self.k_cache[layer_idx] = packed_k
+        self.seq_len = max(self.seq_len, int(packed_k.get("length", 0)))
+
+    def append_v(self, layer_idx: int, packed_v: dict):
+        """kv_cache.py:22-25."""
+        while len(self.v_cache) <= layer_idx:
+            self.v_cache.append(None)
+        self.v_cache[layer_idx] = packed_v
+
+    def clear(self):
+        self.k_cache = []
+        self.v_cache = []
+        self.seq_len = 0
+
+    def memory_bytes(self) -> int:
+        total = 0
+        for cache in (self.k_cache, self.v_cache):
+            for packed in cache:
+                if packed is None:
+                    continue
+                for key in ("q_idx", "outlier_values", "outlier_cols", "outlier_rowptr",
+                            "scale", "zero", "sink"):
+                    t = packed.get(key)
+                    if t is not None:
+                        total += t.numel() * t.element_size()
+        return total

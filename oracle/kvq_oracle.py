@@ -1,0 +1,494 @@
+"""CPU oracle for KVQuant's decode-time quantized-KV attention path.
+
+TEST INFRASTRUCTURE ONLY. Nothing in the product (the package under
+``kvquant-paper-repro_b200/``) imports this module. It is used by ``tests/`` as
+the checker, by ``__graft_entry__.smoke()`` to check one small GPU run, and by
+``bench.py``'s ``cpu_baseline`` leg / ``--impl reference`` arm as the timed CPU
+port of the reference path.
+
+It restates, in numpy, the reference's algorithm for the path. Every function
+cites the reference file and lines it follows (paths relative to the
+KVQuant-Paper-Repro project root). Parity of this restatement is pinned by
+``tests/test_oracle_golden.py`` against golden vectors produced by running the
+reference's own PyTorch code (``tests/golden/make_golden.py``).
+
+Packed-format helpers (``pack_codes``/``unpack_codes``/``tile_outliers``) define
+this build's HBM layout for the quantized cache; the reference stores one code
+per byte and has no bit packing, so the format is new and is checked here by
+round trips to the reference's indices.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+F16 = np.float16
+F32 = np.float32
+
+TILE_TOKENS = 32     # tokens per code tile
+HEAD_DIM = 128       # channels per head (LLaMA head_dim)
+ROPE_PAIRS = HEAD_DIM // 2
+CHUNKS = 4           # 16-pair slabs per token row
+PAIRS_PER_CHUNK = 16
+EPS = F32(1e-8)      # kv_quantizer.py:82,110 `scale + 1e-8` (fp32 add)
+
+
+# --------------------------------------------------------------------------
+# Nearest-centroid lookup and dense-and-sparse outliers
+# --------------------------------------------------------------------------
+def lut_lookup(x: np.ndarray, codebook: np.ndarray):
+    """Nearest centroid, first minimum wins.
+
+    kvquant/quant/kv_quantizer.py:15-21 (CPU branch) and
+    kvquant/kernels/csrc/kvquant_ops.cu:132-151 (`d < best_d`, strict).
+    Returns (idx int64, dequant fp32) with x's shape.
+    """
+    cb = np.asarray(codebook, dtype=F32).reshape(-1)
+    flat = np.asarray(x, dtype=F32).reshape(-1)
+    idx = np.empty(flat.shape, dtype=np.int64)
+    step = 1 << 20
+    for s in range(0, flat.size, step):
+        d = np.abs(flat[s:s + step, None] - cb[None, :])
+        idx[s:s + step] = d.argmin(axis=1)
+    return idx.reshape(np.shape(x)), cb[idx].reshape(np.shape(x))
+
+
+def outlier_count(n: int, ratio: float) -> int:
+    """k = max(1, min(int(n * ratio), n)) -- kvquant/quant/dense_sparse.py:22-23."""
+    return max(1, min(int(n * ratio), n))
+
+
+def topk_mask(xabs: np.ndarray, k: int, axis: int) -> np.ndarray:
+    """Top-k mask of |x| along `axis` (kvquant/quant/dense_sparse.py:25-28).
+
+    torch.topk leaves the order of equal values unspecified; this build fixes
+    it: among values equal to the k-th largest, lower indices win.
+    """
+    order = np.argsort(-xabs, axis=axis, kind="stable")
+    sel = np.take(order, np.arange(k), axis=axis)
+    mask = np.zeros(xabs.shape, dtype=bool)
+    np.put_along_axis(mask, sel, True, axis=axis)
+    return mask
+
+
+def extract_outliers(x: np.ndarray, outlier_ratio: float = 0.01, dim: int = -1):
+    """kvquant/quant/dense_sparse.py:4-32: (dense with outliers zeroed, outliers, mask)."""
+    x = np.asarray(x, dtype=F32)
+    if outlier_ratio <= 0:
+        return x.copy(), np.zeros_like(x), np.zeros(x.shape, dtype=bool)
+    k = outlier_count(x.shape[dim], outlier_ratio)
+    mask = topk_mask(np.abs(x), k, dim % x.ndim)
+    dense = np.where(mask, F32(0.0), x).astype(F32)
+    outliers = (x - dense).astype(F32)
+    return dense, outliers, mask
+
+
+def pack_csr(x: np.ndarray):
+    """kvquant/quant/dense_sparse.py:79-88: CSR of nonzeros of a [R, C] matrix."""
+    mask = x != 0
+    values = x[mask]
+    cols = np.nonzero(mask)[1].astype(np.int32)
+    row_ptr = np.zeros(x.shape[0] + 1, dtype=np.int32)
+    row_ptr[1:] = np.cumsum(mask.sum(axis=1)).astype(np.int32)
+    return values, cols, row_ptr
+
+
+def unpack_csr(values, cols, row_ptr, R: int, C: int, dtype=F16):
+    """kvquant/quant/dense_sparse.py:91-101."""
+    out = np.zeros((R, C), dtype=dtype)
+    for r in range(R):
+        s, e = int(row_ptr[r]), int(row_ptr[r + 1])
+        if e > s:
+            out[r, cols[s:e]] = values[s:e].astype(dtype)
+    return out
+
+
+# --------------------------------------------------------------------------
+# KVQuantizer.quantize_k / quantize_v (fake quant: quantize then dequantize)
+# --------------------------------------------------------------------------
+def _split_sink(x, sink: bool):
+    """kvquant/quant/kv_quantizer.py:55-58: token 0 stays fp16 when S > 1."""
+    if sink and x.shape[1] > 1:
+        return x[:, :1, :], x[:, 1:, :]
+    return None, x
+
+
+def _split_outliers(x_norm_raw, ratio, dim, use_dense_sparse=True):
+    """kvquant/quant/kv_quantizer.py:60-70: outliers on raw values, then clamp."""
+    if use_dense_sparse and ratio > 0:
+        dense_raw, outliers, mask = extract_outliers(x_norm_raw, ratio, dim)
+    else:
+        dense_raw = x_norm_raw
+        outliers = np.zeros_like(x_norm_raw)
+        mask = np.zeros(x_norm_raw.shape, dtype=bool)
+    return np.clip(dense_raw, F32(-1.0), F32(1.0)).astype(F32), outliers, mask
+
+
+def quantize_k(k: np.ndarray, codebook, scale, zero, outlier_ratio=0.01,
+               sink_token=True, use_dense_sparse=True):
+    """kvquant/quant/kv_quantizer.py:72-94 (pre-RoPE, per-channel keys).
+
+    k: [B, S, C] fp16. scale/zero: [C] fp32. Returns a dict with
+    ``dequant`` ([B,S,C] fp16, the reference's output), ``idx`` ([B,S',C]
+    centroid indices of the quantized tokens), ``mask`` (outlier positions),
+    ``norm`` (normalized raw values) and ``has_sink``.
+    """
+    k = np.asarray(k, dtype=F16)
+    cb = np.asarray(codebook, dtype=F32).reshape(-1)
+    scale = np.asarray(scale, dtype=F32)
+    zero = np.asarray(zero, dtype=F32)
+    k_sink, rest = _split_sink(k, sink_token)
+    if rest.size == 0:
+        return dict(dequant=k.copy(), idx=None, mask=None, norm=None, has_sink=False)
+    n = ((rest.astype(F32) - zero) / (scale + EPS)).astype(F32)
+    dense, outl, mask = _split_outliers(n, outlier_ratio, 1, use_dense_sparse)
+    idx, q = lut_lookup(dense, cb)
+    deq = (((q + outl).astype(F32) * scale).astype(F32) + zero).astype(F32)
+    out = deq.astype(F16)
+    if k_sink is not None:
+        out = np.concatenate([k_sink, out], axis=1)
+    return dict(dequant=out, idx=idx, mask=mask, norm=n, has_sink=k_sink is not None)
+
+
+def value_token_stats(v_rest: np.ndarray):
+    """kvquant/quant/kv_quantizer.py:103-107: per-token scale/zero over all C channels."""
+    vf = v_rest.astype(F32)
+    vmin = vf.min(axis=-1, keepdims=True)
+    vmax = vf.max(axis=-1, keepdims=True)
+    scale = ((vmax - vmin) / F32(2.0)).astype(F32)
+    zero = ((vmax + vmin) / F32(2.0)).astype(F32)
+    return scale, zero
+
+
+def quantize_v(v: np.ndarray, codebook, outlier_ratio=0.01, sink_token=True,
+               use_dense_sparse=True):
+    """kvquant/quant/kv_quantizer.py:96-122 (per-token values)."""
+    v = np.asarray(v, dtype=F16)
+    cb = np.asarray(codebook, dtype=F32).reshape(-1)
+    v_sink, rest = _split_sink(v, sink_token)
+    if rest.size == 0:
+        return dict(dequant=v.copy(), idx=None, mask=None, norm=None, has_sink=False,
+                    scale=None, zero=None)
+    vf = rest.astype(F32)
+    scale, zero = value_token_stats(rest)
+    n = ((vf - zero) / (scale + EPS)).astype(F32)
+    dense, outl, mask = _split_outliers(n, outlier_ratio, -1, use_dense_sparse)
+    idx, q = lut_lookup(dense, cb)
+    deq = (((q + outl).astype(F32) * scale).astype(F32) + zero).astype(F32)
+    out = deq.astype(F16)
+    if v_sink is not None:
+        out = np.concatenate([v_sink, out], axis=1)
+    return dict(dequant=out, idx=idx, mask=mask, norm=n, has_sink=v_sink is not None,
+                scale=scale[..., 0], zero=zero[..., 0])
+
+
+# --------------------------------------------------------------------------
+# RoPE
+# --------------------------------------------------------------------------
+def rope_inv_freq(dim: int, base: float) -> np.ndarray:
+    """kvquant/kernels/rope_fused.py:7-8: 1 / base^(i/half) in fp32.
+
+    The exponent i/half is an fp32 division; the power is the correctly
+    rounded fp32 value (an fp64 power rounded once), which is what torch's fp32
+    pow returns for these arguments (numpy's float32 power is off by up to two
+    ulps); the reciprocal is an IEEE fp32 division.
+    """
+    half = dim // 2
+    e = (np.arange(0, half, dtype=F32) / F32(half)).astype(F32)
+    p = np.power(np.float64(base), e.astype(np.float64)).astype(F32)
+    return (F32(1.0) / p).astype(F32)
+
+
+def rope_cos_sin(seq_len: int, dim: int, base: float = 10000.0, inv_freq=None):
+    """kvquant/kernels/rope_fused.py:6-12: fp32 angles outer(t, inv_freq), fp32 cos/sin."""
+    f = rope_inv_freq(dim, base) if inv_freq is None else np.asarray(inv_freq, F32)
+    t = np.arange(seq_len, dtype=F32)
+    ang = (t[:, None] * f[None, :]).astype(F32)
+    return np.cos(ang).astype(F32), np.sin(ang).astype(F32)
+
+
+def rope_apply(x: np.ndarray, cos: np.ndarray, sin: np.ndarray, pos_offset: int = 0):
+    """kvquant/kernels/csrc/kvquant_ops.cu:27-55 (rotate-half, fp32 tables, fp16 out).
+
+    x: [B, H, S, D] fp16; cos/sin: [S_total, D/2] fp32. Computed in float64 and
+    rounded once to fp16.
+    """
+    x = np.asarray(x, dtype=F16)
+    B, H, S, D = x.shape
+    half = D // 2
+    c = cos[pos_offset:pos_offset + S].astype(np.float64)[None, None]
+    s = sin[pos_offset:pos_offset + S].astype(np.float64)[None, None]
+    x1 = x[..., :half].astype(np.float64)
+    x2 = x[..., half:].astype(np.float64)
+    return np.concatenate([x1 * c - x2 * s, x1 * s + x2 * c], axis=-1).astype(F16)
+
+
+# --------------------------------------------------------------------------
+# The reference's matvec ops
+# --------------------------------------------------------------------------
+def lut_matvec(qmat, lut, scale, zero, vec, per_channel: bool):
+    """kvquant/kernels/csrc/kvquant_ops.cu:62-100 (+ host :184-216).
+
+    out[i] = sum_j (lut[q[i,j]] * scale[s] + zero[s]) * vec[j], s = j if
+    per_channel else i; fp16 tables, exact accumulation, fp16 out.
+    """
+    q = np.asarray(qmat).astype(np.int64) & 0xFF
+    lut = np.asarray(lut, dtype=F16).astype(np.float64)
+    sc = np.asarray(scale, dtype=F16).astype(np.float64)
+    zc = np.asarray(zero, dtype=F16).astype(np.float64)
+    v = np.asarray(vec, dtype=F16).astype(np.float64)
+    deq = lut[q]
+    if per_channel:
+        deq = deq * sc[None, :] + zc[None, :]
+    else:
+        deq = deq * sc[:, None] + zc[:, None]
+    return (deq @ v).astype(F16)
+
+
+def sparse_matvec_csr(row_ptr, col_idx, values, vec):
+    """kvquant/kernels/csrc/kvquant_ops.cu:106-127 (+ host :218-241)."""
+    rp = np.asarray(row_ptr, dtype=np.int64)
+    ci = np.asarray(col_idx, dtype=np.int64)
+    va = np.asarray(values, dtype=F16).astype(np.float64)
+    v = np.asarray(vec, dtype=F16).astype(np.float64)
+    R = rp.size - 1
+    out = np.zeros(R, dtype=np.float64)
+    prod = va * v[ci] if ci.size else np.zeros(0)
+    for r in range(R):
+        out[r] = prod[rp[r]:rp[r + 1]].sum()
+    return out.astype(F16)
+
+
+# --------------------------------------------------------------------------
+# Decode attention restated on the reference's dequantized cache
+# --------------------------------------------------------------------------
+def key_scores(q, k_hat, n_kv_heads: int, inv_freq):
+    """Raw scores s[b,h,t] = q[b,h] . RoPE_t(K_hat[b,t,kvh]) in float64.
+
+    K_hat is the reference's fake-quant output (kv_quantizer.py:72-94, fp16),
+    RoPE uses the fp32 angle tables of rope_fused.py:6-12 (the CUDA-path
+    semantics, rope_fused.py:30-34). GQA: query head h reads KV head
+    h // (Hq // Hkv). q is taken as already position-rotated.
+    """
+    q = np.asarray(q, dtype=F16).astype(np.float64)
+    B, Hq, D = q.shape
+    T = k_hat.shape[1]
+    half = D // 2
+    cos, sin = rope_cos_sin(T, D, inv_freq=inv_freq)
+    c = cos.astype(np.float64)[None, :, None, :]
+    s = sin.astype(np.float64)[None, :, None, :]
+    K = np.asarray(k_hat, dtype=F16).astype(np.float64).reshape(B, T, n_kv_heads, D)
+    k1, k2 = K[..., :half], K[..., half:]
+    Kr = np.concatenate([k1 * c - k2 * s, k1 * s + k2 * c], axis=-1)  # [B,T,Hkv,D]
+    G = Hq // n_kv_heads
+    kv_of = np.arange(Hq) // G
+    return np.einsum("bhd,bthd->bht", q, Kr[:, :, kv_of, :])
+
+
+def softmax_probs(scores, head_dim: int = HEAD_DIM):
+    """p = softmax(s / sqrt(D)) along tokens (float64)."""
+    z = scores / math.sqrt(head_dim)
+    z = z - z.max(axis=-1, keepdims=True)
+    e = np.exp(z)
+    return e / e.sum(axis=-1, keepdims=True)
+
+
+def value_output(p, v_hat, n_kv_heads: int):
+    """o[b,h,:] = sum_t p[b,h,t] V_hat[b,t,kvh,:] (V_hat from kv_quantizer.py:96-122)."""
+    B, Hq, T = p.shape
+    D = v_hat.shape[-1] // n_kv_heads
+    V = np.asarray(v_hat, dtype=F16).astype(np.float64).reshape(B, T, n_kv_heads, D)
+    G = Hq // n_kv_heads
+    kv_of = np.arange(Hq) // G
+    return np.einsum("bht,bthd->bhd", p, V[:, :, kv_of, :])
+
+
+def decode_attention(q, k_hat, v_hat, n_kv_heads: int, inv_freq):
+    s = key_scores(q, k_hat, n_kv_heads, inv_freq)
+    p = softmax_probs(s, q.shape[-1])
+    return s, p, value_output(p, v_hat, n_kv_heads)
+
+
+# --------------------------------------------------------------------------
+# Packed cache format (this build's layout; round-trips to reference indices)
+# --------------------------------------------------------------------------
+def slab_position(d: np.ndarray, kind: str):
+    """Channel d (0..127) -> (chunk j, pair m, second-of-pair flag).
+
+    keys:   pair m of chunk j holds channels (16j+m, 64+16j+m), the RoPE
+            rotate-half partners (rope_fused.py:38-43);
+    values: pair m of chunk j holds channels (32j+2m, 32j+2m+1).
+    """
+    d = np.asarray(d)
+    if kind == "k":
+        p = d % ROPE_PAIRS
+        return p // PAIRS_PER_CHUNK, p % PAIRS_PER_CHUNK, (d >= ROPE_PAIRS).astype(np.int64)
+    j = d // 32
+    return j, (d % 32) // 2, d % 2
+
+
+def tile_bytes(bits: int) -> int:
+    return TILE_TOKENS * HEAD_DIM * bits // 8
+
+
+def pack_codes(idx: np.ndarray, bits: int, kind: str) -> np.ndarray:
+    """Pack codes [U, T, 128] -> [U, ceil(T/32), 512*bits] uint8.
+
+    Tile = 4 slabs-chunks x 32 tokens; the slab of (chunk j, token i) is
+    4*bits bytes at offset (j*32 + i)*4*bits. Inside a slab, pair m occupies
+    bits [2*bits*m, 2*bits*m + 2*bits) of a little-endian bit stream, first
+    channel of the pair in the low `bits` bits.
+    """
+    idx = np.asarray(idx, dtype=np.int64)
+    U, T, D = idx.shape
+    assert D == HEAD_DIM
+    nt = (T + TILE_TOKENS - 1) // TILE_TOKENS
+    codes = np.zeros((U, nt * TILE_TOKENS, D), dtype=np.int64)
+    codes[:, :T] = idx
+    codes = codes.reshape(U, nt, TILE_TOKENS, D)
+    j, m, sec = slab_position(np.arange(D), kind)
+    slot = 2 * m + sec                      # code slot 0..31 inside the slab
+    slab = np.zeros((U, nt, CHUNKS, TILE_TOKENS, 32), dtype=np.int64)
+    for d in range(D):
+        slab[:, :, j[d], :, slot[d]] = codes[:, :, :, d]
+    bitsarr = (slab[..., None] >> np.arange(bits)) & 1          # [..,32,bits]
+    flat = bitsarr.reshape(U, nt, CHUNKS, TILE_TOKENS, 32 * bits).astype(np.uint8)
+    packed = np.packbits(flat, axis=-1, bitorder="little")      # [..,4*bits]
+    return packed.reshape(U, nt, tile_bytes(bits))
+
+
+def unpack_codes(packed: np.ndarray, bits: int, kind: str, T: int) -> np.ndarray:
+    """Inverse of pack_codes: [U, nt, 512*bits] uint8 -> [U, T, 128] int64."""
+    packed = np.asarray(packed, dtype=np.uint8)
+    U, nt, _ = packed.shape
+    slabs = packed.reshape(U, nt, CHUNKS, TILE_TOKENS, 4 * bits)
+    bitsarr = np.unpackbits(slabs, axis=-1, bitorder="little").astype(np.int64)
+    bitsarr = bitsarr.reshape(U, nt, CHUNKS, TILE_TOKENS, 32, bits)
+    vals = (bitsarr << np.arange(bits)).sum(axis=-1)            # [U,nt,4,32,32]
+    j, m, sec = slab_position(np.arange(HEAD_DIM), kind)
+    out = np.empty((U, nt, TILE_TOKENS, HEAD_DIM), dtype=np.int64)
+    for d in range(HEAD_DIM):
+        out[:, :, :, d] = vals[:, :, j[d], :, 2 * m[d] + sec[d]]
+    return out.reshape(U, nt * TILE_TOKENS, HEAD_DIM)[:, :T]
+
+
+def tile_outliers(mask: np.ndarray, values: np.ndarray):
+    """Outliers of [U, T, 128] -> CSR over rows (unit, tile).
+
+    Returns (values fp16 [nnz], pos uint16 [nnz] = (token_in_tile << 7) | d,
+    row_ptr int32 [U*nt + 1]); entries of a row are ordered by (token, d).
+    """
+    U, T, D = mask.shape
+    nt = (T + TILE_TOKENS - 1) // TILE_TOKENS
+    m = np.zeros((U, nt * TILE_TOKENS, D), dtype=bool)
+    m[:, :T] = mask
+    v = np.zeros((U, nt * TILE_TOKENS, D), dtype=F32)
+    v[:, :T] = values
+    m = m.reshape(U * nt, TILE_TOKENS * D)
+    v = v.reshape(U * nt, TILE_TOKENS * D)
+    counts = m.sum(axis=1)
+    row_ptr = np.zeros(U * nt + 1, dtype=np.int32)
+    row_ptr[1:] = np.cumsum(counts)
+    r, flatpos = np.nonzero(m)
+    return v[r, flatpos].astype(F16), flatpos.astype(np.uint16), row_ptr
+
+
+def untile_outliers(vals, pos, row_ptr, U: int, T: int):
+    """Inverse of tile_outliers: dense [U, T, 128] fp32 outlier matrix and mask."""
+    nt = (T + TILE_TOKENS - 1) // TILE_TOKENS
+    dense = np.zeros((U * nt, TILE_TOKENS * HEAD_DIM), dtype=F32)
+    mask = np.zeros_like(dense, dtype=bool)
+    rows = np.repeat(np.arange(U * nt), np.diff(np.asarray(row_ptr, np.int64)))
+    p = np.asarray(pos, dtype=np.int64)
+    dense[rows, p] = np.asarray(vals, dtype=F16).astype(F32)
+    mask[rows, p] = True
+    dense = dense.reshape(U, nt * TILE_TOKENS, HEAD_DIM)[:, :T]
+    mask = mask.reshape(U, nt * TILE_TOKENS, HEAD_DIM)[:, :T]
+    return dense, mask
+
+
+def units_view(x_btc: np.ndarray, n_kv_heads: int) -> np.ndarray:
+    """[B, T, Hkv*D] -> [B*Hkv, T, D] (unit u = b*Hkv + h)."""
+    B, T, C = x_btc.shape
+    D = C // n_kv_heads
+    return np.ascontiguousarray(
+        x_btc.reshape(B, T, n_kv_heads, D).transpose(0, 2, 1, 3).reshape(B * n_kv_heads, T, D))
+
+
+def cache_from_reference_quant(kq: dict, vq: dict, k: np.ndarray, v: np.ndarray,
+                               n_kv_heads: int, bits: int):
+    """Expected packed cache for a prefill block, from quantize_k/quantize_v results.
+
+    Token 0 is the fp16 sink (its code slots hold 0); tokens 1.. hold the
+    reference's centroid indices. Outlier values are the normalized raw
+    values (dense_sparse.py:31) rounded to fp16.
+    """
+    B, S, C = k.shape
+    out = {}
+    for name, qd, x in (("k", kq, k), ("v", vq, v)):
+        idx = np.zeros((B, S, C), dtype=np.int64)
+        mask = np.zeros((B, S, C), dtype=bool)
+        val = np.zeros((B, S, C), dtype=F32)
+        off = 1 if qd["has_sink"] else 0
+        idx[:, off:] = qd["idx"]
+        mask[:, off:] = qd["mask"]
+        val[:, off:] = np.where(qd["mask"], qd["norm"], 0)
+        iu = units_view(idx, n_kv_heads)
+        mu = units_view(mask, n_kv_heads)
+        vu = units_view(val, n_kv_heads)
+        out[name + "_codes"] = pack_codes(iu, bits, name)
+        ov, op, orp = tile_outliers(mu, vu)
+        out[name + "_out_vals"], out[name + "_out_pos"], out[name + "_out_ptr"] = ov, op, orp
+        out[name + "_sink"] = x[:, 0, :].copy() if qd["has_sink"] else None
+    return out
+
+
+# --------------------------------------------------------------------------
+# CPU decode over the packed cache (the timed CPU port of the reference path)
+# --------------------------------------------------------------------------
+def dequant_packed(codes, out_vals, out_pos, out_ptr, scale, zero, codebook, bits: int,
+                   kind: str, T: int, sink=None, head_channels=None):
+    """Packed cache of U units -> K_hat / V_hat [U, T, 128] fp16, the reference's
+    fake-quant dequantization (cb[q] + o) * s + z (kv_quantizer.py:89,117), with
+    the fp16 outlier values the cache stores. Keys: scale/zero [U, 128] per
+    channel; values: scale/zero [U, T] per token. sink: [U, 128] fp16 or None.
+    """
+    U = codes.shape[0]
+    idx = unpack_codes(codes, bits, kind, T)
+    cb = np.asarray(codebook, F32)
+    q = cb[idx]
+    o, _ = untile_outliers(out_vals, out_pos, out_ptr, U, T)
+    s = np.asarray(scale, F32)
+    z = np.asarray(zero, F32)
+    if kind == "k":
+        s, z = s[:, None, :], z[:, None, :]
+    else:
+        s, z = s[:, :T, None], z[:, :T, None]
+    deq = ((((q + o).astype(F32)) * s).astype(F32) + z).astype(F16)
+    if sink is not None:
+        deq[:, 0, :] = np.asarray(sink, F16)
+    return deq
+
+
+def decode_packed(q, k_hat_units, v_hat_units, inv_freq, group: int = 1):
+    """Decode attention per unit (fp32 numpy, BLAS matmuls) on dequantized units.
+
+    q: [U*group, 128] fp16; k_hat_units / v_hat_units: [U, T, 128] fp16.
+    RoPE with fp32 angle tables (rope_fused.py:6-12), softmax(s / sqrt(128)),
+    then p . V. Returns fp32 [U*group, 128].
+    """
+    U, T, D = k_hat_units.shape
+    cos, sin = rope_cos_sin(T, D, inv_freq=inv_freq)
+    out = np.empty((U * group, D), F32)
+    for u in range(U):
+        K = k_hat_units[u].astype(F32)
+        k1, k2 = K[:, :D // 2], K[:, D // 2:]
+        Kr = np.concatenate([k1 * cos - k2 * sin, k1 * sin + k2 * cos], axis=1)
+        qs = q[u * group:(u + 1) * group].astype(F32)
+        sc = (qs @ Kr.T) / np.float32(math.sqrt(D))
+        sc -= sc.max(axis=1, keepdims=True)
+        p = np.exp(sc)
+        p /= p.sum(axis=1, keepdims=True)
+        out[u * group:(u + 1) * group] = p @ v_hat_units[u].astype(F32)
+    return out

@@ -1,0 +1,71 @@
+"""Host-side logic of the kvquant package that needs no GPU."""
+import numpy as np
+import pytest
+import torch
+
+from goldens import load_misc
+
+
+def test_rope_inv_freq_matches_reference_bits():
+    from kvquant.kernels.rope_fused import rope_inv_freq
+    m = load_misc()
+    for base in (10000, 500000):
+        got = rope_inv_freq(128, float(base)).numpy()
+        np.testing.assert_array_equal(got.view(np.uint32), m[f"inv_freq_b{base}"].view(np.uint32))
+
+
+def test_ops_reject_cpu_tensors():
+    from kvquant.kernels import dense_matvec_lut, sparse_matvec_csr, apply_rope_elementwise
+    x = torch.zeros(4, 8)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        dense_matvec_lut(x, torch.zeros(16))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        sparse_matvec_csr(torch.zeros(3, dtype=torch.int32), torch.zeros(0, dtype=torch.int32),
+                          torch.zeros(0, dtype=torch.float16), torch.zeros(4, dtype=torch.float16))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        apply_rope_elementwise(torch.zeros(1, 2, 3, 8, dtype=torch.float16))
+
+
+def test_quantizer_rejects_cpu_tensors():
+    from kvquant import KVQuantizer
+    q = KVQuantizer([torch.zeros(16)], [torch.zeros(16)], [torch.ones(128)], [torch.zeros(128)])
+    with pytest.raises(RuntimeError, match="CUDA"):
+        q.quantize_k(0, torch.zeros(1, 4, 128, dtype=torch.float16))
+
+
+def test_missing_library_raises(monkeypatch, tmp_path):
+    import kvquant.kernels.cuda_ops as co
+    monkeypatch.setattr(co, "_ops", None)
+    monkeypatch.setattr(co, "_lib", None)
+    monkeypatch.setenv("KVQ_B200_LIB", str(tmp_path / "nope.so"))
+    with pytest.raises(RuntimeError, match="not loadable"):
+        co.get_cuda_ops()
+    assert not co.cuda_available()
+
+
+def test_kv_cache_container_bytes():
+    from kvquant import QuantizedKVCache
+    c = QuantizedKVCache()
+    packed = {"q_idx": torch.zeros(2, 3, 2048, dtype=torch.uint8),
+              "outlier_values": torch.zeros(10, dtype=torch.float16),
+              "outlier_cols": torch.zeros(10, dtype=torch.int16),
+              "outlier_rowptr": torch.zeros(7, dtype=torch.int32),
+              "scale": torch.zeros(256), "zero": torch.zeros(256), "sink": None, "length": 70}
+    c.append_k(1, packed)
+    c.append_v(0, packed)
+    assert c.k_cache[0] is None and c.seq_len == 70
+    assert c.memory_bytes() == 2 * (2 * 3 * 2048 + 20 + 20 + 28 + 2048)
+    c.clear()
+    assert c.memory_bytes() == 0
+
+
+def test_dense_sparse_helpers_follow_reference():
+    from kvquant.quant.dense_sparse import extract_outliers, pack_csr, unpack_csr
+    m = load_misc()
+    for dim in (1, -1):
+        _, _, mask = extract_outliers(torch.from_numpy(m["eo_x"]), 0.1, dim)
+        np.testing.assert_array_equal(mask.numpy(), m[f"eo_mask_dim{dim}"])
+    x = torch.tensor([[0, 1.5, 0], [0, 0, 0], [2.0, 0, -1.0]])
+    v, c, rp = pack_csr(x)
+    assert rp.tolist() == [0, 1, 1, 3] and c.tolist() == [1, 0, 2]
+    assert torch.equal(unpack_csr(v, c, rp, 3, 3, dtype=torch.float32), x)

@@ -1,0 +1,171 @@
+"""Pins the CPU oracle (oracle/kvq_oracle.py) to the reference's own outputs.
+
+The golden fixtures were produced by running the reference's PyTorch code
+(tests/golden/make_golden.py). Integer/index results must match exactly; the
+only tolerated difference is the order among equal |n| at the top-k threshold,
+which torch.topk leaves unspecified (the oracle takes lower indices first).
+"""
+import numpy as np
+import pytest
+
+from oracle import kvq_oracle as O
+from goldens import QUANT_CASES, load_misc, load_quant
+
+
+def tie_equivalent(m_ref, m_ora, absx, axis):
+    """Masks agree except for which of the entries equal to the threshold were taken."""
+    m_ref = np.moveaxis(m_ref, axis, -1).reshape(-1, m_ref.shape[axis])
+    m_ora = np.moveaxis(m_ora, axis, -1).reshape(-1, m_ora.shape[axis])
+    a = np.moveaxis(absx, axis, -1).reshape(-1, absx.shape[axis])
+    for r in range(a.shape[0]):
+        if np.array_equal(m_ref[r], m_ora[r]):
+            continue
+        if m_ref[r].sum() != m_ora[r].sum():
+            return False
+        thr = a[r][m_ora[r]].min()
+        diff = m_ref[r] != m_ora[r]
+        if not np.all(a[r][diff] == thr):
+            return False
+    return True
+
+
+@pytest.mark.parametrize("name", QUANT_CASES)
+def test_quantize_matches_reference(name):
+    g = load_quant(name)
+    kq = O.quantize_k(g["k"], g["cb_k"], g["scale"], g["zero"], g["ratio"], g["sink"])
+    vq = O.quantize_v(g["v"], g["cb_v"], g["ratio"], g["sink"])
+    if "k_idx" not in g:  # nothing quantized
+        assert np.array_equal(kq["dequant"], g["k_dequant"])
+        return
+    for tag, q, axis in (("k", kq, 1), ("v", vq, 2)):
+        same = np.array_equal(q["mask"], g[f"{tag}_mask"])
+        if not same:
+            assert name.startswith("ties"), f"{tag} outlier mask differs in {name}"
+            assert tie_equivalent(g[f"{tag}_mask"], q["mask"], np.abs(q["norm"]), axis)
+        ok = q["mask"] == g[f"{tag}_mask"]  # positions whose outlier status agrees
+        assert np.array_equal(q["idx"][ok], g[f"{tag}_idx"][ok])
+        if same:
+            assert np.array_equal(q["idx"], g[f"{tag}_idx"])
+            assert np.array_equal(q["norm"][q["mask"]], g[f"{tag}_norm_at_mask"])
+            assert np.array_equal(q["dequant"].view(np.uint16),
+                                  g[f"{tag}_dequant"].view(np.uint16)), f"{tag} dequant"
+    np.testing.assert_array_equal(vq["scale"], g["v_scale"])
+    np.testing.assert_array_equal(vq["zero"], g["v_zero"])
+
+
+@pytest.mark.parametrize("name", ["cfg0_4bit", "cfg1_3bit"])
+def test_pack_csr_matches_reference(name):
+    g = load_quant(name)
+    kq = O.quantize_k(g["k"], g["cb_k"], g["scale"], g["zero"], g["ratio"], g["sink"])
+    om = np.where(kq["mask"], kq["norm"], 0).astype(np.float32)[0]
+    vals, cols, rp = O.pack_csr(om)
+    np.testing.assert_array_equal(vals, g["csr_vals"])
+    np.testing.assert_array_equal(cols, g["csr_cols"])
+    np.testing.assert_array_equal(rp, g["csr_rowptr"])
+    back = O.unpack_csr(vals, cols, rp, om.shape[0], om.shape[1], dtype=np.float32)
+    np.testing.assert_array_equal(back, om)
+
+
+@pytest.mark.parametrize("name", QUANT_CASES)
+def test_decode_attention_restatement(name):
+    g = load_quant(name)
+    inv = O.rope_inv_freq(128, g["base"])
+    Hkv = g["C"] // 128
+    s, p, o = O.decode_attention(g["q"], g["k_dequant"], g["v_dequant"], Hkv, inv)
+    # numpy and torch fp32 cos/sin can differ in the last bit: ~1e-7 of the key norm
+    np.testing.assert_allclose(s, g["scores"], rtol=1e-5, atol=1e-5 * np.abs(g["scores"]).max())
+    np.testing.assert_allclose(p, g["probs"], rtol=1e-4, atol=1e-9)
+    np.testing.assert_allclose(o, g["attn_out"], rtol=1e-5, atol=1e-6)
+
+
+def test_rope_tables_match_reference():
+    m = load_misc()
+    for base in (10000, 500000):
+        inv = O.rope_inv_freq(128, float(base))
+        np.testing.assert_array_equal(inv.view(np.uint32), m[f"inv_freq_b{base}"].view(np.uint32))
+        rows = m["rope_rows"]
+        ang = (rows.astype(np.float32)[:, None] * inv[None, :]).astype(np.float32)
+        # numpy's and torch's fp32 cos/sin may differ in the last bit
+        np.testing.assert_allclose(np.cos(ang), m[f"cos_b{base}"], rtol=0, atol=2.5e-7)
+        np.testing.assert_allclose(np.sin(ang), m[f"sin_b{base}"], rtol=0, atol=2.5e-7)
+
+
+def test_rope_apply_semantics():
+    m = load_misc()
+    x = m["rope_x"]
+    S = x.shape[2]
+    cos, sin = O.rope_cos_sin(S + 7, 128, 10000.0)
+    out = O.rope_apply(x, cos, sin, pos_offset=7)
+    # the reference's CPU path rounds cos/sin and each product to fp16; the
+    # restated CUDA semantics round once, so allow a few fp16 ulps
+    np.testing.assert_allclose(out.astype(np.float32), m["rope_cpu_out"].astype(np.float32),
+                               rtol=4e-3, atol=4e-3)
+
+
+def test_lut_lookup_matches_reference():
+    m = load_misc()
+    idx, dq = O.lut_lookup(m["lut_x"], m["lut_cb"])
+    np.testing.assert_array_equal(idx, m["lut_idx"])
+    np.testing.assert_array_equal(dq, m["lut_dq"])
+    _, dq2 = O.lut_lookup(m["lut_x"].reshape(-1, 5), m["lut_cb"])
+    np.testing.assert_array_equal(dq2, m["dense_matvec_lut_out"])
+
+
+def test_extract_outliers_matches_reference():
+    m = load_misc()
+    for dim in (1, -1):
+        _, _, mask = O.extract_outliers(m["eo_x"], 0.1, dim)
+        np.testing.assert_array_equal(mask, m[f"eo_mask_dim{dim}"])
+
+
+def test_sparse_matvec_matches_reference():
+    m = load_misc()
+    out = O.sparse_matvec_csr(m["sp_rowptr"], m["sp_cols"], m["sp_vals"], m["sp_vec"])
+    np.testing.assert_allclose(out.astype(np.float32), m["sp_out"].astype(np.float32),
+                               rtol=1e-3, atol=1e-3)
+    assert out[7] == 0
+
+
+@pytest.mark.parametrize("bits", [2, 3, 4])
+@pytest.mark.parametrize("kind", ["k", "v"])
+def test_pack_codes_round_trip(bits, kind):
+    rng = np.random.default_rng(bits)
+    idx = rng.integers(0, 1 << bits, size=(3, 77, 128))
+    packed = O.pack_codes(idx, bits, kind)
+    assert packed.shape == (3, 3, 512 * bits)
+    np.testing.assert_array_equal(O.unpack_codes(packed, bits, kind, 77), idx)
+
+
+def test_pack_codes_layout_spot():
+    # keys, 4-bit: byte m of slab (chunk j, token i) = code(16j+m) | code(64+16j+m) << 4
+    idx = np.zeros((1, 32, 128), dtype=np.int64)
+    idx[0, 5, 16 * 2 + 3] = 7
+    idx[0, 5, 64 + 16 * 2 + 3] = 9
+    p = O.pack_codes(idx, 4, "k")
+    off = (2 * 32 + 5) * 16 + 3
+    assert p[0, 0, off] == 7 | (9 << 4)
+    assert p.sum() == p[0, 0, off]
+    # values, 2-bit: nibble m of slab (j, i) = code(32j+2m) | code(32j+2m+1) << 2
+    idx = np.zeros((1, 32, 128), dtype=np.int64)
+    idx[0, 1, 32 * 3 + 2 * 5] = 2
+    idx[0, 1, 32 * 3 + 2 * 5 + 1] = 3
+    p = O.pack_codes(idx, 2, "v")
+    off = (3 * 32 + 1) * 8 + 5 // 2
+    assert p[0, 0, off] == (2 | (3 << 2)) << 4
+
+
+def test_tile_outliers_round_trip():
+    rng = np.random.default_rng(0)
+    mask = rng.random((4, 70, 128)) < 0.02
+    vals = rng.standard_normal((4, 70, 128)).astype(np.float32)
+    v, pos, rp = O.tile_outliers(mask, np.where(mask, vals, 0))
+    assert rp[-1] == mask.sum() and rp.shape == (4 * 3 + 1,)
+    dense, m2 = O.untile_outliers(v, pos, rp, 4, 70)
+    np.testing.assert_array_equal(m2, mask)
+    np.testing.assert_array_equal(dense[mask], vals[mask].astype(np.float16).astype(np.float32))
+
+
+@pytest.mark.parametrize("n,r", [(4095, 0.01), (8191, 0.01), (32767, 0.005), (1, 0.01),
+                                 (100, 0.07), (1048575, 0.01), (4096, 0.01)])
+def test_outlier_count(n, r):
+    assert O.outlier_count(n, r) == max(1, min(int(n * r), n))
