@@ -46,6 +46,7 @@ def parse():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", default="longctx-1m-4bit")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count")
+    ap.add_argument("--tokens", type=int, default=None, help="override the cached token count")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -190,6 +191,9 @@ def run_gpu(args):
     world, rank, local = setup_dist(args)
     dev = torch.device("cuda", local)
     wl = syn.WORKLOADS[args.workload]
+    if args.tokens:
+        import dataclasses
+        wl = dataclasses.replace(wl, tokens=args.tokens, name=f"{wl.name}@{args.tokens}tok")
     layers = args.layers or wl.layers
     if wl.kv_heads % world:
         raise SystemExit(f"{wl.kv_heads} KV heads do not split over {world} GPUs")
@@ -359,10 +363,10 @@ def run_gpu(args):
 def _cpu_unit(args):
     """One worker: dequantize + decode one unit of the packed sample (fp32 numpy)."""
     from oracle import kvq_oracle as O
-    (kc, kv_, kp, kr, ks, kz, kcb, ksink, vc, vv, vp, vr, vs, vz, vcb, vsink, q, inv, bits, T) = args
+    (kc, ke, kr, ks, kz, kcb, ksink, vc, ve, vr, vs, vz, vcb, vsink, q, inv, bits, T) = args
     t0 = time.perf_counter()
-    kh = O.dequant_packed(kc, kv_, kp, kr, ks, kz, kcb, bits, "k", T, ksink)
-    vh = O.dequant_packed(vc, vv, vp, vr, vs, vz, vcb, bits, "v", T, vsink)
+    kh = O.dequant_packed(kc, ke, kr, ks, kz, kcb, bits, "k", T, ksink)
+    vh = O.dequant_packed(vc, ve, vr, vs, vz, vcb, bits, "v", T, vsink)
     O.decode_packed(q, kh, vh, inv)
     return time.perf_counter() - t0
 
@@ -388,19 +392,18 @@ def make_cpu_sample(wl, dev, units: int, T: int):
     h = lambda x: x.cpu().numpy()  # noqa: E731
     tasks = []
     kr_all, vr_all = h(pk["outlier_rowptr"]), h(pv["outlier_rowptr"])
-    kv_all, kp_all = h(pk["outlier_values"]), h(pk["outlier_cols"]).view(np.uint16)
-    vv_all, vp_all = h(pv["outlier_values"]), h(pv["outlier_cols"]).view(np.uint16)
+    ke_all, ve_all = h(pk["outlier_entries"]).view(np.uint32), h(pv["outlier_entries"]).view(np.uint32)
     for u in range(units):
-        def seg(rp, vals, pos):
+        def seg(rp, ent):
             a, b = int(rp[u * nt]), int(rp[(u + 1) * nt])
             r = (rp[u * nt:(u + 1) * nt + 1] - a).astype(np.int32)
-            return vals[a:b], pos[a:b], r
-        kvals, kpos, krp = seg(kr_all, kv_all, kp_all)
-        vvals, vpos, vrp = seg(vr_all, vv_all, vp_all)
-        tasks.append((h(pk["q_idx"][u:u + 1]), kvals, kpos, krp,
+            return ent[a:b], r
+        kent, krp = seg(kr_all, ke_all)
+        vent, vrp = seg(vr_all, ve_all)
+        tasks.append((h(pk["q_idx"][u:u + 1]), kent, krp,
                       h(pk["scale"])[u * 128:(u + 1) * 128][None], h(pk["zero"])[u * 128:(u + 1) * 128][None],
                       h(pk["codebook"]), h(pk["sink"])[0:1, u * 128:(u + 1) * 128],
-                      h(pv["q_idx"][u:u + 1]), vvals, vpos, vrp, h(pv["scale"]), h(pv["zero"]),
+                      h(pv["q_idx"][u:u + 1]), vent, vrp, h(pv["scale"]), h(pv["zero"]),
                       h(pv["codebook"]), h(pv["sink"])[0:1, u * 128:(u + 1) * 128],
                       q[u:u + 1], inv, wl.bits, T))
     del k, v

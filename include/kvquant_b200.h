@@ -16,9 +16,10 @@
  *                byte (j*32+i)*4*bits; pair m at bits [2*bits*m, +2*bits).
  *                Keys: pair m of chunk j = channels (16j+m, 64+16j+m).
  *                Values: pair m of chunk j = channels (32j+2m, 32j+2m+1).
- *       outliers CSR over rows (u, tile): ptr int32 [U*nt_cap+1],
- *                vals fp16 [nnz] (normalized raw value), pos uint16 [nnz] =
- *                (token_in_tile << 7) | channel_in_head.
+ *       outliers CSR over rows (u, tile): ptr int32 [U*nt_cap+1] and one
+ *                uint32 entry per outlier: low 16 bits = (token_in_tile << 7)
+ *                | channel_in_head, high 16 bits = the fp16 normalized raw
+ *                value; entries of a row are ordered by (token, channel).
  *       sink     fp16 [B, n_heads*128]: token 0 kept unquantized.
  *       keys:    scale/zero fp32 [n_heads*128] (per channel, calibrated).
  *       values:  scale/zero fp32 [B, ld] (per token, over all C channels).
@@ -102,7 +103,7 @@ int kvq_quantize_keys_emit(const void* k, int64_t B, int64_t S, int64_t C_full, 
                            int64_t n_heads, const float* scale, const float* zero,
                            const float* codebook, int bits, double outlier_ratio, int sink,
                            uint8_t* codes, int64_t nt_cap, const int32_t* out_ptr,
-                           void* out_vals, uint16_t* out_pos, int64_t nnz_cap, void* sink_out,
+                           uint32_t* out_ent, int64_t nnz_cap, void* sink_out,
                            void* dequant_out, const void* workspace, size_t workspace_bytes,
                            void* stream);
 
@@ -116,8 +117,8 @@ int kvq_quantize_values_emit(const void* v, int64_t B, int64_t S, int64_t C_full
                              int64_t n_heads, const float* codebook, int bits,
                              double outlier_ratio, int sink, const float* v_scale,
                              const float* v_zero, int64_t ld_stats, uint8_t* codes,
-                             int64_t nt_cap, const int32_t* out_ptr, void* out_vals,
-                             uint16_t* out_pos, int64_t nnz_cap, void* sink_out,
+                             int64_t nt_cap, const int32_t* out_ptr, uint32_t* out_ent,
+                             int64_t nnz_cap, void* sink_out,
                              void* dequant_out, const void* workspace, size_t workspace_bytes,
                              void* stream);
 
@@ -129,7 +130,7 @@ int kvq_quantize_values_emit(const void* v, int64_t B, int64_t S, int64_t C_full
 
 /* Fused key kernel: scores[b,hq,t] = q . RoPE_t(Khat_t) (raw, unscaled) fp32
  * [B, n_heads*group, T]. inv_freq fp32 [64] (rope_fused.py:7-8). */
-int kvq_key_scores(const uint8_t* codes, const void* out_vals, const uint16_t* out_pos,
+int kvq_key_scores(const uint8_t* codes, const uint32_t* out_ent,
                    const int32_t* out_ptr, const float* k_scale, const float* k_zero,
                    const void* k_sink, const float* codebook, int bits, const void* q,
                    const float* inv_freq, int64_t B, int64_t n_heads, int64_t group,
@@ -142,7 +143,7 @@ int kvq_softmax(const float* scores, int64_t rows, int64_t T, float scale, float
 
 /* Value kernel: out[b,hq,:] = sum_t probs[b,hq,t] * Vhat_t (fp16 [B, Hq, 128]). */
 size_t kvq_value_output_workspace(int64_t B, int64_t n_heads, int64_t group, int64_t T);
-int kvq_value_output(const uint8_t* codes, const void* out_vals, const uint16_t* out_pos,
+int kvq_value_output(const uint8_t* codes, const uint32_t* out_ent,
                      const int32_t* out_ptr, const float* v_scale, const float* v_zero,
                      int64_t ld_stats, const void* v_sink, const float* codebook, int bits,
                      const float* probs, int64_t B, int64_t n_heads, int64_t group, int64_t T,
@@ -152,11 +153,11 @@ int kvq_value_output(const uint8_t* codes, const void* out_vals, const uint16_t*
 /* scores -> softmax(scores / sqrt(128)) -> p.V in one call; scores_out and
  * probs_out may be NULL (then they live in the workspace). */
 size_t kvq_decode_attention_workspace(int64_t B, int64_t n_heads, int64_t group, int64_t T);
-int kvq_decode_attention(const uint8_t* k_codes, const void* k_out_vals,
-                         const uint16_t* k_out_pos, const int32_t* k_out_ptr,
+int kvq_decode_attention(const uint8_t* k_codes, const uint32_t* k_out_ent,
+                         const int32_t* k_out_ptr,
                          const float* k_scale, const float* k_zero, const void* k_sink,
                          const float* k_codebook, const uint8_t* v_codes,
-                         const void* v_out_vals, const uint16_t* v_out_pos,
+                         const uint32_t* v_out_ent,
                          const int32_t* v_out_ptr, const float* v_scale, const float* v_zero,
                          int64_t ld_stats, const void* v_sink, const float* v_codebook,
                          int bits, const void* q, const float* inv_freq, int64_t B,

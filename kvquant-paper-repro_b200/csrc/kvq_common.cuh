@@ -84,6 +84,12 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 __device__ __forceinline__ uint32_t lo16(uint32_t w) { return w & 0xffffu; }
 __device__ __forceinline__ uint32_t hi16(uint32_t w) { return w >> 16; }
 
+// Splits a 32-bit register into its two 16-bit halves as a register-level
+// view (no arithmetic), so half-operand instructions can read them in place.
+__device__ __forceinline__ void unpack16(uint32_t w, uint16_t& lo, uint16_t& hi) {
+  asm("mov.b32 {%0, %1}, %2;" : "=h"(lo), "=h"(hi) : "r"(w));
+}
+
 __device__ __forceinline__ uint32_t half2_bits(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);

@@ -257,12 +257,18 @@ struct EmitArgs {
   uint8_t* codes;
   int64_t nt_cap;
   int32_t* out_ptr;
-  __half* out_vals;
-  uint16_t* out_pos;
+  uint32_t* out_ent;    // (fp16 value << 16) | (token_in_tile << 7 | channel)
   int64_t nnz_cap;
   __half* sink_out;     // [B, H*128] or null
   __half* dequant_out;  // [B, S, H*128] or null
 };
+
+// One packed outlier entry: position (token_in_tile << 7 | channel) in the low
+// 16 bits, the fp16 normalized value in the high 16 bits.
+__device__ __forceinline__ uint32_t outlier_entry(int token, int channel, float value) {
+  const __half h = __float2half_rn(value);
+  return (uint32_t)((token << 7) | channel) | ((uint32_t)__half_as_ushort(h) << 16);
+}
 
 // Channel within head of code slot q (0..31) of chunk j.
 template <int KIND>
@@ -372,20 +378,14 @@ __global__ void __launch_bounds__(128) emit_kernel(EmitArgs a) {
       const bool first = KIND == 0 ? ((q & 1) == 0) : (q < 16);
       if (!first || !(omask & (1u << q))) continue;
       const int64_t e = base + o0++;
-      if (e < a.nnz_cap) {
-        a.out_vals[e] = __float2half_rn(nval[q]);
-        a.out_pos[e] = (uint16_t)((i << 7) | slot_channel<KIND>(j, q));
-      }
+      if (e < a.nnz_cap) a.out_ent[e] = outlier_entry(i, slot_channel<KIND>(j, q), nval[q]);
     }
 #pragma unroll
     for (int q = 0; q < 32; ++q) {
       const bool second = KIND == 0 ? ((q & 1) == 1) : (q >= 16);
       if (!second || !(omask & (1u << q))) continue;
       const int64_t e = base + o1++;
-      if (e < a.nnz_cap) {
-        a.out_vals[e] = __float2half_rn(nval[q]);
-        a.out_pos[e] = (uint16_t)((i << 7) | slot_channel<KIND>(j, q));
-      }
+      if (e < a.nnz_cap) a.out_ent[e] = outlier_entry(i, slot_channel<KIND>(j, q), nval[q]);
     }
   }
   // Sink copy and fake-quant output.
@@ -569,8 +569,8 @@ extern "C" int kvq_quantize_keys_emit(const void* k, int64_t B, int64_t S, int64
                                       int64_t h0, int64_t n_heads, const float* scale,
                                       const float* zero, const float* codebook, int bits,
                                       double outlier_ratio, int sink, uint8_t* codes,
-                                      int64_t nt_cap, const int32_t* out_ptr, void* out_vals,
-                                      uint16_t* out_pos, int64_t nnz_cap, void* sink_out,
+                                      int64_t nt_cap, const int32_t* out_ptr, uint32_t* out_ent,
+                                      int64_t nnz_cap, void* sink_out,
                                       void* dequant_out, const void* workspace,
                                       size_t workspace_bytes, void* stream) {
   using namespace kvq;
@@ -597,7 +597,7 @@ extern "C" int kvq_quantize_keys_emit(const void* k, int64_t B, int64_t S, int64
   ea.H = n_heads; ea.off = (sink && S > 1) ? 1 : 0; ea.k_scale = scale; ea.k_zero = zero;
   ea.sel = reinterpret_cast<const Select*>(workspace); ea.cb = codebook; ea.bits = bits;
   ea.codes = codes; ea.nt_cap = nt_cap; ea.out_ptr = const_cast<int32_t*>(out_ptr);
-  ea.out_vals = (__half*)out_vals; ea.out_pos = out_pos;
+  ea.out_ent = out_ent;
   ea.nnz_cap = outlier_ratio > 0 ? nnz_cap : -1;
   ea.sink_out = (__half*)sink_out; ea.dequant_out = (__half*)dequant_out;
   emit_kernel<0, false><<<dim3((unsigned)nt, (unsigned)B, (unsigned)n_heads), 128, 0, st>>>(ea);
@@ -664,8 +664,8 @@ extern "C" int kvq_quantize_values_emit(const void* v, int64_t B, int64_t S, int
                                         int bits, double outlier_ratio, int sink,
                                         const float* v_scale, const float* v_zero,
                                         int64_t ld_stats, uint8_t* codes, int64_t nt_cap,
-                                        const int32_t* out_ptr, void* out_vals,
-                                        uint16_t* out_pos, int64_t nnz_cap, void* sink_out,
+                                        const int32_t* out_ptr, uint32_t* out_ent,
+                                        int64_t nnz_cap, void* sink_out,
                                         void* dequant_out, const void* workspace,
                                         size_t workspace_bytes, void* stream) {
   using namespace kvq;
@@ -691,8 +691,8 @@ extern "C" int kvq_quantize_values_emit(const void* v, int64_t B, int64_t S, int
   ea.H = n_heads; ea.off = (sink && S > 1) ? 1 : 0; ea.v_scale = v_scale; ea.v_zero = v_zero;
   ea.ld_stats = ld_stats; ea.sel = reinterpret_cast<const Select*>(workspace);
   ea.cb = codebook; ea.bits = bits; ea.codes = codes; ea.nt_cap = nt_cap;
-  ea.out_ptr = const_cast<int32_t*>(out_ptr); ea.out_vals = (__half*)out_vals;
-  ea.out_pos = out_pos; ea.nnz_cap = outlier_ratio > 0 ? nnz_cap : -1;
+  ea.out_ptr = const_cast<int32_t*>(out_ptr); ea.out_ent = out_ent;
+  ea.nnz_cap = outlier_ratio > 0 ? nnz_cap : -1;
   ea.sink_out = (__half*)sink_out; ea.dequant_out = (__half*)dequant_out;
   emit_kernel<1, false><<<dim3((unsigned)nt, (unsigned)B, (unsigned)n_heads), 128, 0, st>>>(ea);
   return check_launch("quantize_values_emit");

@@ -48,26 +48,26 @@ _SIGNATURES = {
                                         _c_dbl, _c_int, _c_p, _c_i64, _c_p, _c_p, _c_size, _c_p]),
     "kvq_quantize_keys_emit": (_c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p,
                                         _c_p, _c_int, _c_dbl, _c_int, _c_p, _c_i64, _c_p, _c_p,
-                                        _c_p, _c_i64, _c_p, _c_p, _c_p, _c_size, _c_p]),
+                                        _c_i64, _c_p, _c_p, _c_p, _c_size, _c_p]),
     "kvq_quantize_values_workspace": (_c_size, [_c_i64, _c_i64, _c_i64]),
     "kvq_quantize_values_plan": (_c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_dbl,
                                           _c_int, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p,
                                           _c_size, _c_p]),
     "kvq_quantize_values_emit": (_c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p,
                                           _c_int, _c_dbl, _c_int, _c_p, _c_p, _c_i64, _c_p,
-                                          _c_i64, _c_p, _c_p, _c_p, _c_i64, _c_p, _c_p, _c_p,
+                                          _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_p, _c_p,
                                           _c_size, _c_p]),
-    "kvq_key_scores": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_int, _c_p,
+    "kvq_key_scores": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_int, _c_p,
                                 _c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p]),
     "kvq_softmax_workspace": (_c_size, [_c_i64, _c_i64]),
     "kvq_softmax": (_c_int, [_c_p, _c_i64, _c_i64, _c_flt, _c_p, _c_p, _c_size, _c_p]),
     "kvq_value_output_workspace": (_c_size, [_c_i64, _c_i64, _c_i64, _c_i64]),
-    "kvq_value_output": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p, _c_p, _c_int,
+    "kvq_value_output": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p, _c_p, _c_int,
                                   _c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p,
                                   _c_size, _c_p]),
     "kvq_decode_attention_workspace": (_c_size, [_c_i64, _c_i64, _c_i64, _c_i64]),
-    "kvq_decode_attention": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
-                                      _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p, _c_p, _c_int, _c_p,
+    "kvq_decode_attention": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
+                                      _c_p, _c_p, _c_p, _c_i64, _c_p, _c_p, _c_int, _c_p,
                                       _c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p,
                                       _c_p, _c_p, _c_size, _c_p]),
 }

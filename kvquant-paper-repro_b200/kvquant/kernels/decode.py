@@ -78,13 +78,12 @@ def _quantize(kind: str, x: torch.Tensor, codebook: torch.Tensor, bits: int,
                                               nt_cap, _ptr(nnz_dev), _ptr(ws), ws.numel(), st),
                    lib)
             nnz = int(nnz_dev.item())
-            vals = torch.empty(max(nnz, 1), dtype=torch.float16, device=dev)
-            pos = torch.empty(max(nnz, 1), dtype=torch.int16, device=dev)
+            ent = torch.empty(max(nnz, 1), dtype=torch.int32, device=dev)
             _check(lib.kvq_quantize_keys_emit(_ptr(xc), B, S, C_full, h0, H, _ptr(sc), _ptr(ze),
                                               _ptr(cb), bits, float(outlier_ratio), int(sink),
-                                              _ptr(codes), nt_cap, _ptr(out_ptr), _ptr(vals),
-                                              _ptr(pos), nnz, _ptr(sink_t), _ptr(deq), _ptr(ws),
-                                              ws.numel(), st), lib)
+                                              _ptr(codes), nt_cap, _ptr(out_ptr), _ptr(ent), nnz,
+                                              _ptr(sink_t), _ptr(deq), _ptr(ws), ws.numel(), st),
+                   lib)
             scale_out, zero_out = sc[h0 * HEAD_DIM:(h0 + H) * HEAD_DIM].clone(), \
                 ze[h0 * HEAD_DIM:(h0 + H) * HEAD_DIM].clone()
         else:
@@ -96,19 +95,21 @@ def _quantize(kind: str, x: torch.Tensor, codebook: torch.Tensor, bits: int,
                                                 _ptr(vz), cap, _ptr(out_ptr), nt_cap,
                                                 _ptr(nnz_dev), _ptr(ws), ws.numel(), st), lib)
             nnz = int(nnz_dev.item())
-            vals = torch.empty(max(nnz, 1), dtype=torch.float16, device=dev)
-            pos = torch.empty(max(nnz, 1), dtype=torch.int16, device=dev)
+            ent = torch.empty(max(nnz, 1), dtype=torch.int32, device=dev)
             _check(lib.kvq_quantize_values_emit(_ptr(xc), B, S, C_full, h0, H, _ptr(cb), bits,
                                                 float(outlier_ratio), int(sink), _ptr(vs),
                                                 _ptr(vz), cap, _ptr(codes), nt_cap,
-                                                _ptr(out_ptr), _ptr(vals), _ptr(pos), nnz,
-                                                _ptr(sink_t), _ptr(deq), _ptr(ws), ws.numel(),
-                                                st), lib)
+                                                _ptr(out_ptr), _ptr(ent), nnz, _ptr(sink_t),
+                                                _ptr(deq), _ptr(ws), ws.numel(), st), lib)
             scale_out, zero_out = vs, vz
+    pairs = ent.view(torch.int16).view(-1, 2)
     packed = {
         "q_idx": codes,
-        "outlier_values": vals[:nnz],
-        "outlier_cols": pos[:nnz],
+        # one int32 per outlier: low half = (token_in_tile << 7) | channel, high
+        # half = fp16 value; the two halves are also exposed as strided views
+        "outlier_entries": ent,
+        "outlier_values": pairs[:nnz, 1].view(torch.float16),
+        "outlier_cols": pairs[:nnz, 0],
         "outlier_rowptr": out_ptr,
         "scale": scale_out,
         "zero": zero_out,
@@ -166,8 +167,8 @@ def qk_scores(q: torch.Tensor, packed_k: dict, inv_freq: torch.Tensor,
     scores = out if out is not None else torch.empty((B, Hq, T), dtype=torch.float32,
                                                       device=qc.device)
     with torch.cuda.device(qc.device):
-        _check(lib.kvq_key_scores(_ptr(packed_k["q_idx"]), _ptr(packed_k["outlier_values"]),
-                                  _ptr(packed_k["outlier_cols"]), _ptr(packed_k["outlier_rowptr"]),
+        _check(lib.kvq_key_scores(_ptr(packed_k["q_idx"]), _ptr(packed_k["outlier_entries"]),
+                                  _ptr(packed_k["outlier_rowptr"]),
                                   _ptr(packed_k["scale"]), _ptr(packed_k["zero"]),
                                   _ptr(packed_k["sink"]), _ptr(packed_k["codebook"]),
                                   packed_k["bits"], _ptr(qc), _ptr(f), B, packed_k["n_heads"], G,
@@ -204,8 +205,7 @@ def pv_out(probs: torch.Tensor, packed_v: dict, length: int | None = None) -> to
     out = torch.empty((B, Hq, HEAD_DIM), dtype=torch.float16, device=p.device)
     with torch.cuda.device(p.device):
         ws = _workspace(lib.kvq_value_output_workspace(B, H, G, T), p.device)
-        _check(lib.kvq_value_output(_ptr(packed_v["q_idx"]), _ptr(packed_v["outlier_values"]),
-                                    _ptr(packed_v["outlier_cols"]),
+        _check(lib.kvq_value_output(_ptr(packed_v["q_idx"]), _ptr(packed_v["outlier_entries"]),
                                     _ptr(packed_v["outlier_rowptr"]), _ptr(packed_v["scale"]),
                                     _ptr(packed_v["zero"]), packed_v["scale"].shape[1],
                                     _ptr(packed_v["sink"]), _ptr(packed_v["codebook"]),
@@ -248,11 +248,11 @@ def decode_attention(q: torch.Tensor, packed_k: dict, packed_v: dict, inv_freq: 
     ws = (workspace or DecodeWorkspace()).get(need, qc.device)
     with torch.cuda.device(qc.device):
         _check(lib.kvq_decode_attention(
-            _ptr(packed_k["q_idx"]), _ptr(packed_k["outlier_values"]),
-            _ptr(packed_k["outlier_cols"]), _ptr(packed_k["outlier_rowptr"]),
+            _ptr(packed_k["q_idx"]), _ptr(packed_k["outlier_entries"]),
+            _ptr(packed_k["outlier_rowptr"]),
             _ptr(packed_k["scale"]), _ptr(packed_k["zero"]), _ptr(packed_k["sink"]),
-            _ptr(packed_k["codebook"]), _ptr(packed_v["q_idx"]), _ptr(packed_v["outlier_values"]),
-            _ptr(packed_v["outlier_cols"]), _ptr(packed_v["outlier_rowptr"]),
+            _ptr(packed_k["codebook"]), _ptr(packed_v["q_idx"]), _ptr(packed_v["outlier_entries"]),
+            _ptr(packed_v["outlier_rowptr"]),
             _ptr(packed_v["scale"]), _ptr(packed_v["zero"]), packed_v["scale"].shape[1],
             _ptr(packed_v["sink"]), _ptr(packed_v["codebook"]), packed_k["bits"], _ptr(qc), _ptr(f),
             B, H, G, T, packed_k["q_idx"].shape[1], _ptr(o), _ptr(scores_out), _ptr(probs_out),

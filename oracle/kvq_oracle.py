@@ -394,6 +394,18 @@ def tile_outliers(mask: np.ndarray, values: np.ndarray):
     return v[r, flatpos].astype(F16), flatpos.astype(np.uint16), row_ptr
 
 
+def pack_entries(vals, pos) -> np.ndarray:
+    """One uint32 per outlier: position in the low 16 bits, fp16 value bits high."""
+    v = np.asarray(vals, dtype=F16).view(np.uint16).astype(np.uint32)
+    return (np.asarray(pos, dtype=np.uint32) & 0xFFFF) | (v << 16)
+
+
+def unpack_entries(ent):
+    """Inverse of pack_entries: (fp16 values, uint16 positions)."""
+    e = np.asarray(ent).astype(np.uint32)
+    return (e >> 16).astype(np.uint16).view(F16), (e & 0xFFFF).astype(np.uint16)
+
+
 def untile_outliers(vals, pos, row_ptr, U: int, T: int):
     """Inverse of tile_outliers: dense [U, T, 128] fp32 outlier matrix and mask."""
     nt = (T + TILE_TOKENS - 1) // TILE_TOKENS
@@ -440,6 +452,7 @@ def cache_from_reference_quant(kq: dict, vq: dict, k: np.ndarray, v: np.ndarray,
         out[name + "_codes"] = pack_codes(iu, bits, name)
         ov, op, orp = tile_outliers(mu, vu)
         out[name + "_out_vals"], out[name + "_out_pos"], out[name + "_out_ptr"] = ov, op, orp
+        out[name + "_out_ent"] = pack_entries(ov, op)
         out[name + "_sink"] = x[:, 0, :].copy() if qd["has_sink"] else None
     return out
 
@@ -447,8 +460,8 @@ def cache_from_reference_quant(kq: dict, vq: dict, k: np.ndarray, v: np.ndarray,
 # --------------------------------------------------------------------------
 # CPU decode over the packed cache (the timed CPU port of the reference path)
 # --------------------------------------------------------------------------
-def dequant_packed(codes, out_vals, out_pos, out_ptr, scale, zero, codebook, bits: int,
-                   kind: str, T: int, sink=None, head_channels=None):
+def dequant_packed(codes, out_ent, out_ptr, scale, zero, codebook, bits: int,
+                   kind: str, T: int, sink=None):
     """Packed cache of U units -> K_hat / V_hat [U, T, 128] fp16, the reference's
     fake-quant dequantization (cb[q] + o) * s + z (kv_quantizer.py:89,117), with
     the fp16 outlier values the cache stores. Keys: scale/zero [U, 128] per
@@ -458,6 +471,7 @@ def dequant_packed(codes, out_vals, out_pos, out_ptr, scale, zero, codebook, bit
     idx = unpack_codes(codes, bits, kind, T)
     cb = np.asarray(codebook, F32)
     q = cb[idx]
+    out_vals, out_pos = unpack_entries(out_ent)
     o, _ = untile_outliers(out_vals, out_pos, out_ptr, U, T)
     s = np.asarray(scale, F32)
     z = np.asarray(zero, F32)

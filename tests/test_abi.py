@@ -58,14 +58,14 @@ def test_invalid_arguments_are_rejected_before_any_launch(lib):
     rc = lib.kvq_lut_matvec(None, None, 300, None, None, None, None, 4, 4, 1, None)
     assert rc == 1 and b"lut_size too large" in lib.kvq_last_error()
     # unsupported bit width / group size
-    rc = lib.kvq_key_scores(None, None, None, None, None, None, None, None, 5, None, None,
+    rc = lib.kvq_key_scores(None, None, None, None, None, None, None, 5, None, None,
                             1, 1, 1, 64, 2, None, None)
     assert rc == 3
-    rc = lib.kvq_key_scores(None, None, None, None, None, None, None, None, 4, None, None,
+    rc = lib.kvq_key_scores(None, None, None, None, None, None, None, 4, None, None,
                             1, 1, 3, 64, 2, None, None)
     assert rc == 3
     # capacity too small for T
-    rc = lib.kvq_key_scores(None, None, None, None, None, None, None, None, 4, None, None,
+    rc = lib.kvq_key_scores(None, None, None, None, None, None, None, 4, None, None,
                             1, 1, 1, 65, 2, None, None)
     assert rc == 1
     # workspace too small

@@ -47,6 +47,9 @@ def check_packed(p, exp, tag, nt):
                                   exp[f"{tag}_out_vals"].view(np.uint16))
     np.testing.assert_array_equal(p["outlier_cols"].cpu().numpy().view(np.uint16),
                                   exp[f"{tag}_out_pos"])
+    nnz = p["nnz"]
+    np.testing.assert_array_equal(p["outlier_entries"].cpu().numpy()[:nnz].view(np.uint32),
+                                  exp[f"{tag}_out_ent"])
 
 
 def _compact_rowptr(rp, U, nt_cap, nt):

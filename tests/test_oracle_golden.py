@@ -154,6 +154,16 @@ def test_pack_codes_layout_spot():
     assert p[0, 0, off] == (2 | (3 << 2)) << 4
 
 
+def test_outlier_entry_packing():
+    vals = np.array([1.5, -20.25, 0.0, 65504.0], dtype=np.float16)
+    pos = np.array([0, 4095, (31 << 7) | 5, 127], dtype=np.uint16)
+    ent = O.pack_entries(vals, pos)
+    assert ent.dtype == np.uint32 and ent[1] & 0xFFFF == 4095
+    v2, p2 = O.unpack_entries(ent)
+    np.testing.assert_array_equal(v2.view(np.uint16), vals.view(np.uint16))
+    np.testing.assert_array_equal(p2, pos)
+
+
 def test_tile_outliers_round_trip():
     rng = np.random.default_rng(0)
     mask = rng.random((4, 70, 128)) < 0.02
