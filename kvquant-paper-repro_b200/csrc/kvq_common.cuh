@@ -15,11 +15,8 @@ namespace kvq {
 constexpr int kTileTokens = 32;   // tokens per code tile
 constexpr int kHeadDim = 128;     // channels per head
 constexpr int kPairs = 64;        // RoPE rotate-half pairs per head
-constexpr int kChunks = 4;        // slabs per token row (16 pairs each)
-constexpr int kPairsPerChunk = 16;
 
 __host__ __device__ inline int tile_bytes(int bits) { return kTileTokens * kHeadDim * bits / 8; }
-__host__ __device__ inline int slab_bytes(int bits) { return 4 * bits; }
 
 // Thread-local error message of the last failed entry point.
 void set_error(const char* fmt, ...);
@@ -106,8 +103,8 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// Extracts the 2*bits-wide code pair m (0..15) from a slab held in registers
-// (little-endian bit stream of 4*bits bytes).
+// Extracts the 2*bits-wide code pair m from a slab held in registers
+// (little-endian bit stream; pair m at bits [2*bits*m, 2*bits*(m+1))).
 template <int BITS>
 __device__ __forceinline__ uint32_t slab_pair(const uint32_t* w, int m) {
   constexpr int W = 2 * BITS;

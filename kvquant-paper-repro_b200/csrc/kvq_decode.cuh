@@ -1,4 +1,4 @@
-// Decode attention over the packed quantized cache.
+// Decode attention over the packed quantized cache, on the tensor cores.
 //
 // Key kernel: score[b,hq,t] = q . RoPE_t(Khat_t), Khat = (cb[code] + o) * s + z
 // per channel (kvquant/quant/kv_quantizer.py:89), rotate-half RoPE with fp32
@@ -7,35 +7,23 @@
 //   X = L1*(s1 q1) + L2*(s2 q2) + (z1 q1 + z2 q2)
 //   Y = L1*(s1 q2) - L2*(s2 q1) + (z1 q2 - z2 q1)
 //   score += cos(t th_p) * X + sin(t th_p) * Y
-// The per-(query head, pair) constants are built once per CTA; cos/sin once per
-// (token, pair) per CTA and reused by every head the CTA owns; the code->value
-// LUT is a conflict-free shared-memory pair table; X and Y use the sm_100
-// fp16 x fp16 + fp32 FMA; outliers are added from the tile-CSR.
+// X and Y of 16 tokens x 4 pairs are one m16n8k8 MMA whose A operand is the
+// fp16 code values read from the LUT and whose C operand is the zero-point
+// term; the rotation is an fp32 epilogue; outliers come from the tile-CSR.
 //
 // Value kernel: out[b,hq,:] = sum_t p_t * (s_t * (cb[code] + o) + z_t) with the
-// per-token scale s_t / zero z_t over all channels (kv_quantizer.py:103-117).
+// per-token scale s_t / zero z_t over all channels (kv_quantizer.py:103-117);
+// the code-value x weight sum is an m16n8k16 MMA per 16 tokens x 16 channels.
 //
-// Both kernels stream their codes (and the per-token data and outlier entries
-// they need) through a per-thread cp.async ring in shared memory: every thread
-// copies exactly the bytes it will read itself, so the only synchronisation is
-// cp.async.wait_group, and the copies of several units / tiles stay in flight.
+// The packed tiles are laid out so that each lane's slab already holds the code
+// pairs of its MMA fragments (A-operand order), so a lane turns one slab byte
+// (4-bit) into one LUT address and the LUT word is the fragment register.
+// Both kernels stream codes, per-token data and outlier entries through
+// cp.async rings in shared memory.
 #pragma once
 #include "kvq_common.cuh"
 
 namespace kvq {
-
-// ---------------------------------------------------------------------------
-// cos/sin of the fp32 angle a = fl(t * f): reduction by 2*pi in fp64 (exact to
-// ~1e-9 rad for |a| < 2^24), then the hardware sin/cos on [-pi, pi].
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ void rope_cos_sin(int64_t t, float f, float& c, float& s) {
-  const float a = __fmul_rn((float)t, f);
-  const double ad = (double)a;
-  const double k = rint(ad * 0.15915494309189535);  // 1 / (2 pi)
-  double r = fma(-k, 6.283185307179586, ad);        // 2 pi (high part)
-  r = fma(-k, 2.4492935982947064e-16, r);           // 2 pi - high part
-  __sincosf((float)r, &s, &c);
-}
 
 // Exponent e with m <= 2^e (0 for m == 0), clamped to [-100, 100] so that
 // 2^e and 2^-e stay finite fp32 numbers: a slot whose largest magnitude is
@@ -85,61 +73,107 @@ struct PairLut {
       *reinterpret_cast<uint32_t*>(smem + (v << 8) + (lane << 2)) = h;
     }
   }
-  // Byte address (relative to the table) of pair m of the slab for this lane.
-  __device__ static __forceinline__ uint32_t addr(const uint32_t* slab, int m, uint32_t lane4) {
-    if (BITS == 4) {
-      // byte m of the slab -> bits 8..15; lane*4 -> bits 0..7 (one PRMT)
-      const uint32_t w = slab[m >> 2];
-      const uint32_t sel = 0x1100u | ((4u + (m & 3)) << 4);
-      return prmt(lane4, w, sel);
-    } else {
-      return (slab_pair<BITS>(slab, m) << 8) | lane4;
-    }
-  }
-};
-
-// One thread's code slab (4*BITS bytes), copied into / read from shared memory.
-template <int BITS>
-struct CodeSlab {
-  uint32_t w[4];
-  // Asynchronous copy of the slab at src into the 16-byte smem slot dst.
-  __device__ static __forceinline__ void copy(uint32_t dst, const uint8_t* src, bool valid) {
-    if (BITS == 4) {
-      cp_async16(dst, src, valid ? 16u : 0u);
-    } else if (BITS == 2) {
-      cp_async8(dst, src, valid ? 8u : 0u);
-    } else {
-      cp_async4(dst, src, valid ? 4u : 0u);
-      cp_async4(dst + 4, src + 4, valid ? 4u : 0u);
-      cp_async4(dst + 8, src + 8, valid ? 4u : 0u);
-    }
-  }
-  __device__ __forceinline__ void read(const uint8_t* slot) {
-    if (BITS == 4) {
-      const uint4 v = *reinterpret_cast<const uint4*>(slot);
-      w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
-    } else if (BITS == 2) {
-      const uint2 v = *reinterpret_cast<const uint2*>(slot);
-      w[0] = v.x; w[1] = v.y; w[2] = 0; w[3] = 0;
-    } else {
-      const uint32_t* q = reinterpret_cast<const uint32_t*>(slot);
-      w[0] = q[0]; w[1] = q[1]; w[2] = q[2]; w[3] = 0;
-    }
-  }
 };
 
 __device__ __forceinline__ float entry_value(uint32_t ent) {
   return __half2float(__ushort_as_half((unsigned short)(ent >> 16)));
 }
 
+// ---------------------------------------------------------------------------
+// Angle reduction for RoPE in fp32 only: a = fl(t * f) (the reference's fp32
+// angle), r = a - k * 2pi with the classic three-term Cody-Waite split of 2pi
+// (each step one rounded FMA; |error| < 1e-6 rad for |a| < 2^24), then the
+// hardware sin/cos on [-pi, pi] (abs error < 4e-7).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float rope_reduce(int64_t t, float f) {
+  const float a = __fmul_rn((float)t, f);
+  const float k = rintf(a * 0.15915493667125702f);  // 1 / (2 pi)
+  float r = fmaf(-k, 6.2831854820251465f, a);        // fl(2 pi)
+  r = fmaf(-k, -1.7484555314695172e-07f, r);          // fl(2 pi - C1)
+  r = fmaf(-k, -6.8604980400235275e-15f, r);          // fl(2 pi - C1 - C2)
+  return r;
+}
+
+// mma.sync wrappers (fp16 inputs, fp32 accumulate).
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                          uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_1688(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0,
+                                         float c0, float c1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, "
+      "{%7,%8,%7,%8};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(b0), "f"(c0), "f"(c1));
+}
+
+// Lane slab of one 16-token block (8*BITS bytes = 32 code pairs), staged in
+// shared memory as two 16-byte halves (structure of arrays per stage).
+template <int BITS>
+struct LaneSlab {
+  static constexpr int kBytes = 8 * BITS;
+  uint32_t w[8];
+  __device__ static __forceinline__ void copy(uint32_t dst0, uint32_t dst1, const uint8_t* src,
+                                              bool valid) {
+    const uint32_t n = valid ? 1u : 0u;
+    if (BITS == 4) {
+      cp_async16(dst0, src, 16u * n);
+      cp_async16(dst1, src + 16, 16u * n);
+    } else if (BITS == 2) {
+      cp_async16(dst0, src, 16u * n);
+    } else {  // 24 bytes: 16 + 8
+      cp_async8(dst0, src, 8u * n);
+      cp_async8(dst0 + 8, src + 8, 8u * n);
+      cp_async8(dst1, src + 16, 8u * n);
+    }
+  }
+  __device__ __forceinline__ void read(const uint8_t* s0, const uint8_t* s1) {
+    const uint4 v = *reinterpret_cast<const uint4*>(s0);
+    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+    if (BITS == 4) {
+      const uint4 u = *reinterpret_cast<const uint4*>(s1);
+      w[4] = u.x; w[5] = u.y; w[6] = u.z; w[7] = u.w;
+    } else if (BITS == 3) {
+      const uint2 u = *reinterpret_cast<const uint2*>(s1);
+      w[4] = u.x; w[5] = u.y; w[6] = 0; w[7] = 0;
+    } else {
+      w[4] = w[5] = w[6] = w[7] = 0;
+    }
+  }
+  // LUT byte address of pair slot q for this lane.
+  __device__ __forceinline__ uint32_t addr(int q, uint32_t lane4) const {
+    if (BITS == 4) {
+      const uint32_t sel = 0x1100u | ((4u + (q & 3)) << 4);
+      return prmt(lane4, w[q >> 2], sel);
+    }
+    return (slab_pair<BITS>(w, q) << 8) | lane4;
+  }
+};
+
 // ===========================================================================
-// Key kernel
+// Key kernel (tensor cores as the dot-product engine).
+//
+// Per 16-token block, pair block kb (4 RoPE pairs) and query head, one
+// m16n8k8 MMA computes, for the 16 tokens,
+//   X_p = L1 P1 + L2 P2 + OX   (columns 0..3, pairs 4kb..4kb+3)
+//   Y_p = L1 Q1 + L2 Q2 + OY   (columns 4..7)
+// with A = the fp16 code values straight from the LUT (rows = tokens, k =
+// the two halves of each pair), B = the block-diagonal per-head constants
+// and C = the zero-point terms; the epilogue adds cos * X + sin * Y in fp32
+// with the token's exact-angle cos/sin held in registers.
 // ===========================================================================
-// Per-(slot, pair) key constants, 16 bytes: fp16 {P1, P2} {Q1, Q2}, fp32 OX, OY
-// (all divided by the slot's power-of-two sigma).
+// Per-(slot, kb, c) constants, 16 bytes: B-fragment candidates for pair
+// 4kb + c (X column: half2(P1, P2), Y column: half2(Q1, Q2)) and the two
+// C-fragment values of columns 2c, 2c+1 (OX or OY of two pairs). All divided
+// by the slot's power-of-two sigma.
 struct KeyConst {
-  uint32_t p12, q12;
-  float ox, oy;
+  uint32_t bx, by;
+  float oa, ob;
 };
 
 struct KeyArgs {
@@ -158,39 +192,35 @@ struct KeyArgs {
   int64_t n_items;       // tile quads * groups
 };
 
-// CTA = 8 warps: warp w handles chunk j = w & 3 (16 RoPE pairs) of tiles
-// 2*(w >> 2) and 2*(w >> 2) + 1 of a 4-tile (128-token) work item; every
-// thread keeps cos/sin of its two tokens x 16 pairs in registers.
+// CTA = 8 warps; warp w handles 16-token block w of a 128-token (4-tile) work
+// item for every unit of its group. Lane (g = lane >> 2, c = lane & 3) keeps
+// in registers the cos (c < 2) or sin (c >= 2) of its tokens g and g + 8 for
+// the 32 pairs 4kb + 2(c & 1) + {0, 1}.
 constexpr int kKeyThreads = 256;
 constexpr int kKeyTiles = 4;                     // tiles per work item
 constexpr int kKeyTokens = kKeyTiles * kTileTokens;
 constexpr int kMaxSlots = 32;                    // query heads per group
 constexpr int kKeyStages = 3;                    // units in flight per thread
 
-// Shared-memory layout of the key kernel: pair LUT, per-slot constants, score
-// accumulators, per-slot normalizers, per-unit outlier row pointers and the
-// cp.async ring (per stage: 2 x 16-byte slab slots + one outlier entry per
-// thread). For 4-bit codes the constants live in bytes 128..255 of the LUT's
-// 256-byte rows (32 slots x 64 pairs x 16 B).
 template <int BITS>
 struct KeySmem {
   static constexpr int kLut = PairLut<BITS>::kBytes;
+  // 4-bit: constants in bytes 128..255 of the LUT rows (2048 cells x 16 B)
   static constexpr int kConst = BITS == 4 ? 0 : kLut;
-  static constexpr int kSc = BITS == 4 ? kLut : kConst + kMaxSlots * kPairs * 16;
+  static constexpr int kSc = BITS == 4 ? kLut : kConst + kMaxSlots * 64 * 16;
   static constexpr int kSigma = kSc + kMaxSlots * kKeyTokens * 4;
-  static constexpr int kPtr = kSigma + kMaxSlots * 4;  // [slots][kKeyTiles + 1] int32
+  static constexpr int kPtr = kSigma + kMaxSlots * 4;     // [units][kKeyTiles + 1]
   static constexpr int kRing = kPtr + kMaxSlots * (kKeyTiles + 1) * 4;
-  static constexpr int kRingSlab = kKeyThreads * 32;    // per stage: [2][thread][16 B]
-  static constexpr int kRingEnt = kKeyThreads * 4;      // per stage: [thread] uint32
-  static constexpr int kBytes = kRing + kKeyStages * (kRingSlab + kRingEnt);
+  static constexpr int kStage = kKeyThreads * (16 + 16 + 4);  // [half0][half1][entry]
+  static constexpr int kBytes = kRing + kKeyStages * kStage;
 };
 
 template <int BITS>
 __host__ __device__ constexpr int key_smem_bytes() { return KeySmem<BITS>::kBytes; }
 
 template <int BITS>
-__device__ __forceinline__ KeyConst* key_const(uint8_t* smem, int slot, int p) {
-  const int idx = slot * kPairs + p;  // < 2048 16-byte cells
+__device__ __forceinline__ KeyConst* key_const(uint8_t* smem, int slot, int kb, int c) {
+  const int idx = (slot * 16 + kb) * 4 + c;  // < 2048 16-byte cells
   if (BITS == 4)
     return reinterpret_cast<KeyConst*>(smem + ((idx >> 3) << 8) + 128 + ((idx & 7) << 4));
   return reinterpret_cast<KeyConst*>(smem + KeySmem<BITS>::kConst) + idx;
@@ -210,25 +240,23 @@ __global__ void __launch_bounds__(kKeyThreads, KVQ_KEY_MIN_BLOCKS) key_scores_ke
   int32_t* uptr = reinterpret_cast<int32_t*>(smem + L::kPtr);  // [units][kKeyTiles + 1]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int j = warp & 3, half = warp >> 2;
+  const int g = lane >> 2, c = lane & 3;
   const uint32_t lane4 = (uint32_t)lane << 2;
+  const uint32_t mask_x = (g == c) ? 0xffffffffu : 0u;      // this lane's B column is X of pair c
+  const uint32_t mask_y = (g == c + 4) ? 0xffffffffu : 0u;  // ... or Y of pair c
   PairLut<BITS>::build(lut, a.cb);
-  // This thread's ring slots.
-  uint8_t* ring_slab = smem + L::kRing + threadIdx.x * 16;  // + kKeyThreads*16 for slab 1
-  uint32_t* ring_ent = reinterpret_cast<uint32_t*>(smem + L::kRing + kKeyStages * L::kRingSlab) +
-                       threadIdx.x;
+  uint8_t* ring = smem + L::kRing;
 
   const int64_t nt = (a.T + kTileTokens - 1) / kTileTokens;
   const int64_t n_quads = (nt + kKeyTiles - 1) / kKeyTiles;
   const int UG = a.units_per_group;
   const int slots = UG * G;
-  // Static contiguous split of the (group-major) work list.
   const int64_t w0 = a.n_items * blockIdx.x / gridDim.x;
   const int64_t w1 = a.n_items * (blockIdx.x + 1) / gridDim.x;
   int cur_group = -1;
   const int64_t HG = a.H * G;
   const int64_t tbytes = kTileTokens * kHeadDim * BITS / 8;
-  const int64_t slab_off = (int64_t)(j * 32 + lane) * (4 * BITS);
+  const int64_t slab_off = (int64_t)((warp & 1) * 32 + lane) * (8 * BITS);
 
   for (int64_t w = w0; w < w1; ++w) {
     const int grp = (int)(w / n_quads);
@@ -238,7 +266,6 @@ __global__ void __launch_bounds__(kKeyThreads, KVQ_KEY_MIN_BLOCKS) key_scores_ke
     __syncthreads();  // previous item's readers are done with sc / tables
     if (grp != cur_group) {
       cur_group = grp;
-      // Constants for every slot (unit, g) of the group.
       for (int s = threadIdx.x; s < slots; s += blockDim.x) sigma[s] = 0.f;
       __syncthreads();
       for (int idx = threadIdx.x; idx < nu * G * kPairs; idx += blockDim.x) {
@@ -253,23 +280,35 @@ __global__ void __launch_bounds__(kKeyThreads, KVQ_KEY_MIN_BLOCKS) key_scores_ke
         atomicMax(reinterpret_cast<int*>(sigma + s), __float_as_int(m));
       }
       __syncthreads();
-      for (int idx = threadIdx.x; idx < nu * G * kPairs; idx += blockDim.x) {
-        const int s = idx / kPairs, p = idx % kPairs;
+      // cell (slot, kb, cc): B candidates of pair 4kb + cc, C values of columns 2cc, 2cc + 1
+      for (int idx = threadIdx.x; idx < nu * G * 64; idx += blockDim.x) {
+        const int s = idx / 64, kb = (idx % 64) >> 2, cc = idx & 3;
         const int64_t u = u0 + s / G;
         const int64_t b = u / a.H, h = u % a.H;
         const int64_t hq = h * G + s % G;
         const __half* qv = a.q + (b * HG + hq) * kHeadDim;
-        const float q1 = __half2float(qv[p]), q2 = __half2float(qv[p + 64]);
-        const float s1 = a.k_scale[h * kHeadDim + p], s2 = a.k_scale[h * kHeadDim + p + 64];
-        const float z1 = a.k_zero[h * kHeadDim + p], z2 = a.k_zero[h * kHeadDim + p + 64];
-        // power-of-two normalizer so every fp16 constant is <= 1 in magnitude
+        const float* scl = a.k_scale + h * kHeadDim;
+        const float* zer = a.k_zero + h * kHeadDim;
         const float inv = ldexpf(1.f, -pow2_exponent(sigma[s]));
         KeyConst kc;
-        kc.p12 = half2_bits(s1 * q1 * inv, s2 * q2 * inv);
-        kc.q12 = half2_bits(s1 * q2 * inv, -s2 * q1 * inv);
-        kc.ox = (z1 * q1 + z2 * q2) * inv;
-        kc.oy = (z1 * q2 - z2 * q1) * inv;
-        *key_const<BITS>(smem, s, p) = kc;
+        {
+          const int p = 4 * kb + cc;
+          const float q1 = __half2float(qv[p]), q2 = __half2float(qv[p + 64]);
+          const float s1 = scl[p], s2 = scl[p + 64];
+          kc.bx = half2_bits(s1 * q1 * inv, s2 * q2 * inv);
+          kc.by = half2_bits(s1 * q2 * inv, -s2 * q1 * inv);
+        }
+        float o[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int p = 4 * kb + 2 * (cc & 1) + e;
+          const float q1 = __half2float(qv[p]), q2 = __half2float(qv[p + 64]);
+          const float z1 = zer[p], z2 = zer[p + 64];
+          o[e] = (cc < 2 ? (z1 * q1 + z2 * q2) : (z1 * q2 - z2 * q1)) * inv;
+        }
+        kc.oa = o[0];
+        kc.ob = o[1];
+        *key_const<BITS>(smem, s, kb, cc) = kc;
       }
       __syncthreads();
       if (threadIdx.x < slots) sigma[threadIdx.x] = ldexpf(1.f, pow2_exponent(sigma[threadIdx.x]));
@@ -277,92 +316,87 @@ __global__ void __launch_bounds__(kKeyThreads, KVQ_KEY_MIN_BLOCKS) key_scores_ke
     for (int idx = threadIdx.x; idx < slots * kKeyTokens; idx += blockDim.x) sc[idx] = 0.f;
     const int64_t tile0 = kKeyTiles * tq;
     const int ntiles = (int)min((int64_t)kKeyTiles, nt - tile0);
-    // Outlier row pointers of every unit over the item's tiles.
     for (int idx = threadIdx.x; idx < nu * (kKeyTiles + 1); idx += blockDim.x) {
       const int ui = idx / (kKeyTiles + 1), k = idx % (kKeyTiles + 1);
       uptr[idx] = __ldg(a.out_ptr + (u0 + ui) * a.nt_cap + tile0 + min(k, ntiles));
     }
-    __syncthreads();  // uptr is read by the copy issue below
+    __syncthreads();
 
-    const int64_t my_tile = tile0 + 2 * half;  // this thread's tiles: my_tile, my_tile + 1
-    const bool has0 = my_tile < nt, has1 = my_tile + 1 < nt;
-
-    // Issue the copies of unit ui into ring stage ui % kKeyStages (always one
-    // commit per call so group counting stays uniform).
+    const int64_t my_tile = tile0 + (warp >> 1);
+    const bool has = my_tile < nt;
     auto issue = [&](int ui) {
       if (ui < nu) {
-        const int st = ui % kKeyStages;
+        uint8_t* st = ring + (ui % kKeyStages) * L::kStage;
         const int64_t u = u0 + ui;
-        const uint8_t* base = a.codes + (u * a.nt_cap + (has0 ? my_tile : tile0)) * tbytes + slab_off;
-        const uint32_t dst = smem_u32(ring_slab + st * L::kRingSlab);
-        CodeSlab<BITS>::copy(dst, base, has0);
-        CodeSlab<BITS>::copy(dst + kKeyThreads * 16, has1 ? base + tbytes : base, has1);
+        const uint8_t* src = a.codes + (u * a.nt_cap + (has ? my_tile : tile0)) * tbytes + slab_off;
+        LaneSlab<BITS>::copy(smem_u32(st + threadIdx.x * 16),
+                             smem_u32(st + kKeyThreads * 16 + threadIdx.x * 16), src, has);
         const int32_t e0 = uptr[ui * (kKeyTiles + 1)], e1 = uptr[ui * (kKeyTiles + 1) + ntiles];
         const int32_t e = e0 + (int32_t)threadIdx.x;
-        cp_async4(smem_u32(ring_ent + st * kKeyThreads), a.out_ent + (e < e1 ? e : 0),
+        cp_async4(smem_u32(st + kKeyThreads * 32 + threadIdx.x * 4), a.out_ent + (e < e1 ? e : 0),
                   e < e1 ? 4u : 0u);
       }
       cp_async_commit();
     };
-
-    // cos/sin for this thread's two tokens and the 16 pairs of chunk j
-    // (computed while the first units' copies are in flight).
     for (int ui = 0; ui < kKeyStages - 1; ++ui) issue(ui);
-    float cs[2][16], sn[2][16];
+
+    // cos (c < 2) or sin (c >= 2) of tokens g, g + 8 of this warp's block
+    // for pairs 4kb + 2(c & 1) + {0, 1}.
+    float tw[16][4];
+    {
+      const int64_t tA = tile0 * kTileTokens + 16 * warp + g;
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const int64_t t = (my_tile + r) * kTileTokens + lane;
+      for (int kb = 0; kb < 16; ++kb) {
 #pragma unroll
-      for (int m = 0; m < 16; ++m) rope_cos_sin(t, __ldg(a.inv_freq + 16 * j + m), cs[r][m], sn[r][m]);
+        for (int e = 0; e < 2; ++e) {
+          const float f = __ldg(a.inv_freq + 4 * kb + 2 * (c & 1) + e);
+          const float rA = rope_reduce(tA, f), rB = rope_reduce(tA + 8, f);
+          tw[kb][e] = c < 2 ? __cosf(rA) : __sinf(rA);
+          tw[kb][2 + e] = c < 2 ? __cosf(rB) : __sinf(rB);
+        }
+      }
     }
 
     for (int ui = 0; ui < nu; ++ui) {
       issue(ui + kKeyStages - 1);
       cp_async_wait<kKeyStages - 1>();
-      const int st = ui % kKeyStages;
-      CodeSlab<BITS> s0, s1;
-      s0.read(ring_slab + st * L::kRingSlab);
-      s1.read(ring_slab + st * L::kRingSlab + kKeyThreads * 16);
+      const uint8_t* st = ring + (ui % kKeyStages) * L::kStage;
+      LaneSlab<BITS> sl;
+      sl.read(st + threadIdx.x * 16, st + kKeyThreads * 16 + threadIdx.x * 16);
+      uint32_t ent = *reinterpret_cast<const uint32_t*>(st + kKeyThreads * 32 + threadIdx.x * 4);
       const int32_t e0 = uptr[ui * (kKeyTiles + 1)], e1 = uptr[ui * (kKeyTiles + 1) + ntiles];
       const int32_t e_first = e0 + (int32_t)threadIdx.x;
-      uint32_t ent = ring_ent[st * kKeyThreads];
 
-      float acc[G][2];
+      float accA[G], accB[G];
 #pragma unroll
-      for (int g = 0; g < G; ++g) acc[g][0] = acc[g][1] = 0.f;
+      for (int gg = 0; gg < G; ++gg) accA[gg] = accB[gg] = 0.f;
 #pragma unroll
-      for (int m = 0; m < 16; ++m) {
-        const uint32_t l0 = *reinterpret_cast<const uint32_t*>(lut + PairLut<BITS>::addr(s0.w, m, lane4));
-        const uint32_t l1 = *reinterpret_cast<const uint32_t*>(lut + PairLut<BITS>::addr(s1.w, m, lane4));
-        uint16_t A1, A2, B1, B2;
-        unpack16(l0, A1, A2);
-        unpack16(l1, B1, B2);
+      for (int kb = 0; kb < 16; ++kb) {
+        const uint32_t a0 = *reinterpret_cast<const uint32_t*>(lut + sl.addr(2 * kb, lane4));
+        const uint32_t a1 = *reinterpret_cast<const uint32_t*>(lut + sl.addr(2 * kb + 1, lane4));
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const KeyConst kc = *key_const<BITS>(smem, ui * G + g, 16 * j + m);
-          uint16_t P1, P2, Q1, Q2;
-          unpack16(kc.p12, P1, P2);
-          unpack16(kc.q12, Q1, Q2);
-          {
-            const float X = fma_h(A1, P1, fma_h(A2, P2, kc.ox));
-            const float Y = fma_h(A1, Q1, fma_h(A2, Q2, kc.oy));
-            acc[g][0] = fmaf(cs[0][m], X, fmaf(sn[0][m], Y, acc[g][0]));
-          }
-          {
-            const float X = fma_h(B1, P1, fma_h(B2, P2, kc.ox));
-            const float Y = fma_h(B1, Q1, fma_h(B2, Q2, kc.oy));
-            acc[g][1] = fmaf(cs[1][m], X, fmaf(sn[1][m], Y, acc[g][1]));
-          }
+        for (int gg = 0; gg < G; ++gg) {
+          const KeyConst kc = *key_const<BITS>(smem, ui * G + gg, kb, c);
+          const uint32_t b0 = (kc.bx & mask_x) | (kc.by & mask_y);
+          float d[4];
+          mma_1688(d, a0, a1, b0, kc.oa, kc.ob);
+          accA[gg] = fmaf(tw[kb][0], d[0], fmaf(tw[kb][1], d[1], accA[gg]));
+          accB[gg] = fmaf(tw[kb][2], d[2], fmaf(tw[kb][3], d[3], accB[gg]));
         }
       }
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        atomicAdd(sc + (ui * G + g) * kKeyTokens + (2 * half) * 32 + lane, acc[g][0]);
-        atomicAdd(sc + (ui * G + g) * kKeyTokens + (2 * half + 1) * 32 + lane, acc[g][1]);
+      for (int gg = 0; gg < G; ++gg) {
+        float x = accA[gg], y = accB[gg];
+        x += __shfl_xor_sync(0xffffffffu, x, 1);
+        y += __shfl_xor_sync(0xffffffffu, y, 1);
+        x += __shfl_xor_sync(0xffffffffu, x, 2);
+        y += __shfl_xor_sync(0xffffffffu, y, 2);
+        if (c == 0) {
+          atomicAdd(sc + (ui * G + gg) * kKeyTokens + 16 * warp + g, x);
+          atomicAdd(sc + (ui * G + gg) * kKeyTokens + 16 * warp + g + 8, y);
+        }
       }
-      // Outliers: o * (cos * P + sin * Q) of the channel's half of the pair,
-      // with the exact-angle cos/sin (an fp16 table would cost ~1e-3 on
-      // outlier-heavy scores).
+      // Outliers: o * (cos * P + sin * Q) of the channel's half of the pair.
       if (e_first < e1) {
         int32_t bnd[kKeyTiles - 1];
 #pragma unroll
@@ -371,21 +405,21 @@ __global__ void __launch_bounds__(kKeyThreads, KVQ_KEY_MIN_BLOCKS) key_scores_ke
           if (e != e_first) ent = __ldg(a.out_ent + e);
           int k = 0;
 #pragma unroll
-          for (int q = 0; q < kKeyTiles - 1; ++q) k += e >= bnd[q] ? 1 : 0;
+          for (int qq = 0; qq < kKeyTiles - 1; ++qq) k += e >= bnd[qq] ? 1 : 0;
           const int tok = k * kTileTokens + (int)((ent >> 7) & 31);
           const int ch = (int)(ent & 127);
           const int p = ch & 63, second = ch >> 6;
           const float oval = entry_value(ent);
-          float c, sv;
-          rope_cos_sin(tile0 * kTileTokens + tok, __ldg(a.inv_freq + p), c, sv);
+          float cv, sv;
+          __sincosf(rope_reduce(tile0 * kTileTokens + tok, __ldg(a.inv_freq + p)), &sv, &cv);
 #pragma unroll
-          for (int g = 0; g < G; ++g) {
-            const KeyConst kc = *key_const<BITS>(smem, ui * G + g, p);
-            const __half2 pp = *reinterpret_cast<const __half2*>(&kc.p12);
-            const __half2 qq = *reinterpret_cast<const __half2*>(&kc.q12);
+          for (int gg = 0; gg < G; ++gg) {
+            const KeyConst kc = *key_const<BITS>(smem, ui * G + gg, p >> 2, p & 3);
+            const __half2 pp = *reinterpret_cast<const __half2*>(&kc.bx);
+            const __half2 qq = *reinterpret_cast<const __half2*>(&kc.by);
             const float P = second ? __high2float(pp) : __low2float(pp);
             const float Q = second ? __high2float(qq) : __low2float(qq);
-            atomicAdd(sc + (ui * G + g) * kKeyTokens + tok, oval * fmaf(c, P, sv * Q));
+            atomicAdd(sc + (ui * G + gg) * kKeyTokens + tok, oval * fmaf(cv, P, sv * Q));
           }
         }
       }
@@ -409,7 +443,6 @@ __global__ void __launch_bounds__(kKeyThreads, KVQ_KEY_MIN_BLOCKS) key_scores_ke
       __syncthreads();
     }
 
-    // Write out.
     for (int idx = threadIdx.x; idx < nu * G * kKeyTokens; idx += blockDim.x) {
       const int s = idx / kKeyTokens, tt = idx % kKeyTokens;
       const int64_t t = tile0 * kTileTokens + tt;
@@ -482,10 +515,21 @@ __global__ void __launch_bounds__(256) softmax_write_kernel(const float* __restr
 }
 
 // ===========================================================================
-// Value kernel. One CTA = 8 warps: warp w handles chunk j = w & 3 (32
-// channels) of the tiles of parity w >> 2; a work item is (unit, split of
-// tiles); each thread accumulates its 32 channels over one token per tile for
-// the G query heads of the unit.
+// Value kernel (tensor cores as the weighted-sum engine).
+//
+// For one 16-token block and channel block mb (16 channels), one m16n8k16
+// MMA accumulates D[channel][head] += sum_t cb[code(t, channel)] * w[head][t]
+// with A = the fp16 code values straight from the pair LUT (rows = channels,
+// k = tokens: slot q = 4 mb + i of the lane slab is fragment register a_i),
+// B = the fp16 token weights w = p * s * 2^e (rows = tokens, columns = the
+// query heads of the KV head, zero beyond the group) and fp32 accumulators.
+// The zero-point term sum_t p_t z_t, the outliers (p s o into one channel)
+// and the sink token are added in fp32 beside it.
+//
+// CTA = 16 warps, one CTA per SM; a work item is (unit, split of its tiles)
+// and warp w takes the split's tiles w, w + 16, ...; each warp streams whole
+// tiles (codes, probabilities, scales, zeros, outlier entries) through its
+// own cp.async ring.
 // ===========================================================================
 struct ValueArgs {
   const uint8_t* codes;
@@ -502,9 +546,10 @@ struct ValueArgs {
   float* partial;        // [n_splits, B*H*G, 129]: 128 channels + zero term
 };
 
-constexpr int kValThreads = 256;
-constexpr int kValStages = 4;       // tiles in flight per thread
-constexpr int kValMaxTiles = 4096;  // tiles per CTA (their row pointers sit in shared memory)
+constexpr int kValWarps = 16;
+constexpr int kValThreads = kValWarps * 32;
+constexpr int kValMaxTiles = 2048;     // tiles per work item (row pointers sit in shared memory)
+constexpr int kValSmemLimit = 232448;  // opt-in shared memory per CTA (227 KB)
 
 // max_t v_scale[b, t] for each batch row (bounds every weight p_t * s_t).
 __global__ void row_max_kernel(const float* __restrict__ vs, int64_t T, int64_t ld,
@@ -523,40 +568,48 @@ __global__ void row_max_kernel(const float* __restrict__ vs, int64_t T, int64_t 
   }
 }
 
-// Value-kernel shared memory: LUT (reused for the final lane reduction), the
-// split's outlier row pointers and the cp.async ring (per stage and thread:
-// 16-byte slab slot, G probabilities, scale, zero, one outlier entry).
+// Value-kernel shared memory: pair LUT, fp32 side accumulators [G][129]
+// (outliers + sink per channel, zero term at 128), the item's outlier row
+// pointers and the per-warp cp.async rings. A ring stage of one warp holds one
+// tile: the two blocks' lane slabs (first 16 bytes of every lane, then the
+// rest), probabilities [G][kPRow], scales [32], zeros [32], entries [32].
 template <int BITS, int G>
 struct ValSmem {
-  static constexpr int kRed = 8 * 32 * 33 * 4;
-  static constexpr int kLut = PairLut<BITS>::kBytes > kRed ? PairLut<BITS>::kBytes : kRed;
-  static constexpr int kPtr = kLut;
-  static constexpr int kRing = kPtr + (kValMaxTiles + 1) * 4 + 12;  // 16-byte aligned
-  static constexpr int kPerThread = 16 + 4 * (G + 3);  // slab + G probs + scale + zero + entry
-  static constexpr int kStage = kValThreads * kPerThread;  // [slab][G probs][scale][zero][entry]
-  static constexpr int kBytes = kRing + kValStages * kStage;
+  static constexpr int kLut = PairLut<BITS>::kBytes;
+  static constexpr int kAcc = kLut;
+  static constexpr int kPtr = kAcc + (G * 129 * 4 + 15) / 16 * 16;
+  static constexpr int kRing = kPtr + (kValMaxTiles + 4) * 4;
+  static constexpr int kPRow = 40;  // floats per probability row (conflict-free float2 reads)
+  static constexpr int kBlockSlab = 1024;
+  static constexpr int kFields = 2 * kBlockSlab;
+  static constexpr int kStage = kFields + 4 * (kPRow * G + 3 * 32);
+  static constexpr int kFit = (kValSmemLimit - kRing) / (kValWarps * kStage);
+  static constexpr int kStages = kFit < 4 ? kFit : 4;
+  static constexpr int kBytes = kRing + kStages * kValWarps * kStage;
+  static_assert(kStages >= 2, "value ring needs two stages");
+  static_assert(kStage % 16 == 0 && kRing % 16 == 0, "16-byte aligned stages");
+  static_assert(kStages * kValWarps * kStage >= kValWarps * G * kHeadDim * 4,
+                "the reduction buffer reuses the ring");
 };
 
 template <int BITS, int G>
-__global__ void __launch_bounds__(kValThreads) value_kernel(ValueArgs a, const float* __restrict__ row_max) {
+__global__ void __launch_bounds__(kValThreads, 1)
+    value_kernel(ValueArgs a, const float* __restrict__ row_max) {
   extern __shared__ __align__(16) uint8_t smem[];
   using S = ValSmem<BITS, G>;
-  uint8_t* lut = smem;
-  float* red = reinterpret_cast<float*>(smem);  // after the main loop
+  const uint8_t* lut = smem;
+  float* s_acc = reinterpret_cast<float*>(smem + S::kAcc);
   int32_t* tptr = reinterpret_cast<int32_t*>(smem + S::kPtr);
-  __shared__ float s_acc[G][129];  // outliers + sink (fp32) and the zero term at [128]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int j = warp & 3, par = warp >> 2;
-  const int ptid = threadIdx.x & 127;
+  const int g = lane >> 2, c = lane & 3;
   const uint32_t lane4 = (uint32_t)lane << 2;
-  PairLut<BITS>::build(lut, a.cb);
-  for (int idx = threadIdx.x; idx < G * 129; idx += blockDim.x) (&s_acc[0][0])[idx] = 0.f;
+  PairLut<BITS>::build(smem, a.cb);
+  for (int idx = threadIdx.x; idx < G * 129; idx += blockDim.x) s_acc[idx] = 0.f;
 
   const int64_t nt = (a.T + kTileTokens - 1) / kTileTokens;
   const int64_t U = a.B * a.H;
-  const int64_t item = blockIdx.x;  // over U * n_splits
-  const int64_t u = item / a.n_splits;
-  const int split = (int)(item % a.n_splits);
+  const int64_t u = blockIdx.x / a.n_splits;
+  const int split = (int)(blockIdx.x % a.n_splits);
   const int64_t tpb = (nt + a.n_splits - 1) / a.n_splits;
   const int64_t ta = split * tpb, tb = min(nt, ta + tpb);
   const int64_t b = u / a.H, h = u % a.H;
@@ -573,128 +626,135 @@ __global__ void __launch_bounds__(kValThreads) value_kernel(ValueArgs a, const f
     tptr[k] = __ldg(a.out_ptr + u * a.nt_cap + ta + k);
   __syncthreads();
 
-  float acc[G][32];
+  float d[8][4];
 #pragma unroll
-  for (int g = 0; g < G; ++g)
-#pragma unroll
-    for (int c = 0; c < 32; ++c) acc[g][c] = 0.f;
-  float zsum[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) zsum[g] = 0.f;
+  for (int mb = 0; mb < 8; ++mb) d[mb][0] = d[mb][1] = d[mb][2] = d[mb][3] = 0.f;
+  float zs = 0.f;
 
   const int64_t tbytes = kTileTokens * kHeadDim * BITS / 8;
-  const int64_t slab_off = (int64_t)(j * 32 + lane) * (4 * BITS);
-  const uint8_t* ubase = a.codes + u * a.nt_cap * tbytes + slab_off;
-  // Stage layout (structure of arrays, conflict-free): slabs [thread][16 B],
-  // then 4-byte fields [G + 3][thread].
-  uint8_t* ring = smem + S::kRing;
-  const int fb = kValThreads * 16;  // byte offset of the 4-byte fields in a stage
-
-  // This warp's tiles: ta + par, ta + par + 2, ...; the i-th of them goes to
-  // ring stage i % kValStages.
-  const int64_t t0 = ta + par;
-  const int64_t my_n = t0 < tb ? (tb - t0 + 1) / 2 : 0;
+  const uint8_t* ubase = a.codes + u * a.nt_cap * tbytes + lane * (8 * BITS);
+  uint8_t* wring = smem + S::kRing + warp * S::kStage;
+  constexpr int kStageStride = kValWarps * S::kStage;
+  const int64_t my_n = ta + warp < tb ? (tb - ta - warp + kValWarps - 1) / kValWarps : 0;
   auto issue = [&](int64_t i) {
     if (i < my_n) {
-      const int64_t tile = t0 + 2 * i;
-      uint8_t* stage = ring + (i % kValStages) * S::kStage;
-      CodeSlab<BITS>::copy(smem_u32(stage + threadIdx.x * 16), ubase + tile * tbytes, true);
-      const uint32_t fdst = smem_u32(stage + fb + threadIdx.x * 4);
+      const int64_t tile = ta + warp + i * kValWarps;
+      uint8_t* st = wring + (i % S::kStages) * kStageStride;
+      const uint8_t* src = ubase + tile * tbytes;
+#pragma unroll
+      for (int blk = 0; blk < 2; ++blk)
+        LaneSlab<BITS>::copy(smem_u32(st + blk * S::kBlockSlab + lane * 16),
+                             smem_u32(st + blk * S::kBlockSlab + 512 + lane * 16),
+                             src + blk * (32 * 8 * BITS), true);
       const int64_t t = tile * kTileTokens + lane;
       const bool live = t < a.T && !(sink && t == 0);
       const int64_t tc = live ? t : 0;
+      const uint32_t f = smem_u32(st + S::kFields);
 #pragma unroll
-      for (int g = 0; g < G; ++g)
-        cp_async4(fdst + g * kValThreads * 4, prow + g * a.T + tc, live ? 4u : 0u);
-      cp_async4(fdst + G * kValThreads * 4, vs + tc, live ? 4u : 0u);
-      cp_async4(fdst + (G + 1) * kValThreads * 4, vz + tc, live ? 4u : 0u);
+      for (int hd = 0; hd < G; ++hd)
+        cp_async4(f + (hd * S::kPRow + lane) * 4, prow + hd * a.T + tc, live ? 4u : 0u);
+      cp_async4(f + (G * S::kPRow + lane) * 4, vs + tc, live ? 4u : 0u);
+      cp_async4(f + (G * S::kPRow + 32 + lane) * 4, vz + tc, live ? 4u : 0u);
       const int32_t e0 = tptr[tile - ta], e1 = tptr[tile - ta + 1];
-      const int32_t e = e0 + ptid;
-      cp_async4(fdst + (G + 2) * kValThreads * 4, a.out_ent + (e < e1 ? e : 0), e < e1 ? 4u : 0u);
+      const int32_t e = e0 + lane;
+      cp_async4(f + (G * S::kPRow + 64 + lane) * 4, a.out_ent + (e < e1 ? e : 0),
+                e < e1 ? 4u : 0u);
     }
     cp_async_commit();
   };
 
-  for (int64_t i = 0; i < kValStages - 1; ++i) issue(i);
+  for (int64_t i = 0; i < S::kStages - 1; ++i) issue(i);
+  const int gq = g < G ? g : 0;
   for (int64_t i = 0; i < my_n; ++i) {
-    issue(i + kValStages - 1);
-    cp_async_wait<kValStages - 1>();
-    const int64_t tile = t0 + 2 * i;
-    const uint8_t* stage = ring + (i % kValStages) * S::kStage;
-    CodeSlab<BITS> cw;
-    cw.read(stage + threadIdx.x * 16);
-    const float* f = reinterpret_cast<const float*>(stage + fb) + threadIdx.x;
-    float w32[G];
-    uint16_t w16[G];
-    const float s_t = f[G * kValThreads], z_t = f[(G + 1) * kValThreads];
+    __syncwarp();  // every lane is done with the stage the next copy overwrites
+    issue(i + S::kStages - 1);
+    cp_async_wait<S::kStages - 1>();
+    __syncwarp();  // ... and sees the other lanes' copies of this one
+    const int64_t tile = ta + warp + i * kValWarps;
+    const uint8_t* st = wring + (i % S::kStages) * kStageStride;
+    const float* fp = reinterpret_cast<const float*>(st + S::kFields);
+    const float* fs = fp + G * S::kPRow;
+    const float* fz = fs + 32;
+    const uint32_t* fe = reinterpret_cast<const uint32_t*>(fz + 32);
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float p = f[g * kValThreads];
-      w32[g] = p * s_t;
-      const __half hw = __float2half_rn(w32[g] * e_scale);
-      w16[g] = __half_as_ushort(hw);
-      if (warp == 0 || warp == 4) zsum[g] = fmaf(p, z_t, zsum[g]);
-    }
+    for (int blk = 0; blk < 2; ++blk) {
+      LaneSlab<BITS> sl;
+      sl.read(st + blk * S::kBlockSlab + lane * 16, st + blk * S::kBlockSlab + 512 + lane * 16);
+      const int t0 = 16 * blk + 2 * c;
+      const float2 s01 = *reinterpret_cast<const float2*>(fs + t0);
+      const float2 s89 = *reinterpret_cast<const float2*>(fs + t0 + 8);
+      const float2 p01 = *reinterpret_cast<const float2*>(fp + gq * S::kPRow + t0);
+      const float2 p89 = *reinterpret_cast<const float2*>(fp + gq * S::kPRow + t0 + 8);
+      const float2 z01 = *reinterpret_cast<const float2*>(fz + t0);
+      const float2 z89 = *reinterpret_cast<const float2*>(fz + t0 + 8);
+      uint32_t b0 = half2_bits(p01.x * s01.x * e_scale, p01.y * s01.y * e_scale);
+      uint32_t b1 = half2_bits(p89.x * s89.x * e_scale, p89.y * s89.y * e_scale);
+      if (g < G) {
+        zs = fmaf(p01.x, z01.x, zs);
+        zs = fmaf(p01.y, z01.y, zs);
+        zs = fmaf(p89.x, z89.x, zs);
+        zs = fmaf(p89.y, z89.y, zs);
+      } else {
+        b0 = b1 = 0u;
+      }
 #pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      const uint32_t l = *reinterpret_cast<const uint32_t*>(lut + PairLut<BITS>::addr(cw.w, m, lane4));
-      uint16_t l1, l2;
-      unpack16(l, l1, l2);
+      for (int mb = 0; mb < 8; ++mb) {
+        uint32_t af[4];
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        acc[g][2 * m] = fma_h(l1, w16[g], acc[g][2 * m]);
-        acc[g][2 * m + 1] = fma_h(l2, w16[g], acc[g][2 * m + 1]);
+        for (int ii = 0; ii < 4; ++ii)
+          af[ii] = *reinterpret_cast<const uint32_t*>(lut + sl.addr(4 * mb + ii, lane4));
+        mma_16816(d[mb], af, b0, b1);
       }
     }
-    // Outliers: w_t * o into channel d. Every warp holds the 32 tokens' weights
-    // (lane = token), so the weight of the entry's token is one shuffle away.
+    // Outliers: p s o into channel ch, fp32.
     const int32_t e0 = tptr[tile - ta], e1 = tptr[tile - ta + 1];
-    uint32_t ent = __float_as_uint(f[(G + 2) * kValThreads]);
-    for (int32_t eb = e0; eb < e1; eb += 128) {
-      const int32_t e = eb + ptid;
-      if (eb != e0 && e < e1) ent = __ldg(a.out_ent + e);
-      const int src = (int)((ent >> 7) & 31);
-      const float oval = entry_value(ent);
+    for (int32_t eb = e0; eb < e1; eb += 32) {
+      const int32_t e = eb + lane;
+      if (e < e1) {
+        const uint32_t ent = eb == e0 ? fe[lane] : __ldg(a.out_ent + e);
+        const int tok = (int)((ent >> 7) & 31), ch = (int)(ent & 127);
+        const float so = fs[tok] * entry_value(ent);
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float wt = __shfl_sync(0xffffffffu, w32[g], src);
-        if (e < e1) atomicAdd(&s_acc[g][ent & 127], wt * oval);
+        for (int hd = 0; hd < G; ++hd)
+          atomicAdd(s_acc + hd * 129 + ch, fp[hd * S::kPRow + tok] * so);
       }
     }
   }
   cp_async_wait<0>();
-  // Sink (token 0 in the first split).
-  if (sink && ta == 0 && a.T > 0) {
+  zs += __shfl_xor_sync(0xffffffffu, zs, 1);
+  zs += __shfl_xor_sync(0xffffffffu, zs, 2);
+  if (c == 0 && g < G) atomicAdd(s_acc + g * 129 + 128, zs);
+  // Sink (token 0, in the first split): p_0 * v_sink, fp32.
+  if (sink && ta == 0) {
     for (int idx = threadIdx.x; idx < G * kHeadDim; idx += blockDim.x) {
-      const int g = idx / kHeadDim, d = idx % kHeadDim;
-      const float p0 = prow[g * a.T];
-      atomicAdd(&s_acc[g][d], p0 * __half2float(a.v_sink[(b * a.H + h) * kHeadDim + d]));
+      const int hd = idx / kHeadDim, dd = idx % kHeadDim;
+      atomicAdd(s_acc + hd * 129 + dd,
+                prow[hd * a.T] * __half2float(a.v_sink[(b * a.H + h) * kHeadDim + dd]));
     }
   }
+  __syncthreads();  // all warps are done with their rings
+  float* red = reinterpret_cast<float*>(smem + S::kRing);  // [warp][G][128]
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const float z = warp_sum(zsum[g]);
-    if ((warp == 0 || warp == 4) && lane == 0) atomicAdd(&s_acc[g][128], z);
-  }
-  // Reduce the 64 token lanes (two warps) of each chunk (channels 32j..32j+31).
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    __syncthreads();  // LUT reads (g == 0) / previous reduction reads are done
-    float* r = red + warp * 32 * 33;
-#pragma unroll
-    for (int c = 0; c < 32; ++c) r[lane * 33 + c] = acc[g][c];
-    __syncthreads();
-    if (par == 0) {
-      float sum = 0.f;
-      const float* r0 = red + j * 32 * 33;
-      const float* r1 = red + (j + 4) * 32 * 33;
-#pragma unroll 8
-      for (int l2 = 0; l2 < 32; ++l2) sum += r0[l2 * 33 + lane] + r1[l2 * 33 + lane];
-      const int d = 32 * j + lane;
-      float* dst = a.partial + ((int64_t)split * (U * G) + u * G + g) * 129;
-      dst[d] = sum * inv_e + s_acc[g][d];
-      if (threadIdx.x == 0) dst[128] = s_acc[g][128];
+  for (int mb = 0; mb < 8; ++mb) {
+    const int ch = 16 * mb + g;
+    if (2 * c < G) {
+      red[(warp * G + 2 * c) * kHeadDim + ch] = d[mb][0];
+      red[(warp * G + 2 * c) * kHeadDim + ch + 8] = d[mb][2];
     }
+    if (2 * c + 1 < G) {
+      red[(warp * G + 2 * c + 1) * kHeadDim + ch] = d[mb][1];
+      red[(warp * G + 2 * c + 1) * kHeadDim + ch + 8] = d[mb][3];
+    }
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < G * kHeadDim; idx += blockDim.x) {
+    const int hd = idx / kHeadDim, dd = idx % kHeadDim;
+    float sum = 0.f;
+#pragma unroll
+    for (int w = 0; w < kValWarps; ++w) sum += red[(w * G + hd) * kHeadDim + dd];
+    float* dst = a.partial + ((int64_t)split * (U * G) + u * G + hd) * 129;
+    dst[dd] = fmaf(sum, inv_e, s_acc[hd * 129 + dd]);
+    if (dd == 0) dst[128] = s_acc[hd * 129 + 128];
   }
 }
 
@@ -712,16 +772,27 @@ __global__ void value_combine_kernel(const float* __restrict__ partial, int n_sp
   out[slot * kHeadDim + d] = __float2half_rn(v + z);
 }
 
-inline int value_splits(int64_t U, int64_t nt, int64_t G) {
-  // one full wave: 148 SMs x resident CTAs (2 for G <= 2, 1 above), but at
-  // least 16 tiles per CTA and at most kValMaxTiles
-  int64_t s = (148 * (G <= 2 ? 2 : 1)) / U;
-  const int64_t max_s = (nt + 15) / 16;
-  if (s > max_s) s = max_s;
-  const int64_t min_s = (nt + kValMaxTiles - 1) / kValMaxTiles;
-  if (s < min_s) s = min_s;
-  if (s < 1) s = 1;
-  return (int)s;
+// Splits of each unit's tiles into value work items. The value kernel runs
+// one 16-warp CTA per SM, so the items run in waves of kValSlots; the split
+// count minimises waves x (tile rounds per warp + a pipeline fill of two
+// rounds), subject to at most kValMaxTiles tiles per item. Host-only and
+// independent of the device, so the workspace size is known up front.
+constexpr int kValSlots = 148;  // B200 SMs
+inline int value_splits(int64_t U, int64_t nt, int64_t /*G*/) {
+  if (U < 1 || nt < 1) return 1;
+  const int64_t s_min = (nt + kValMaxTiles - 1) / kValMaxTiles;
+  int64_t s_max = nt / (2 * kValWarps);
+  if (s_max < s_min) s_max = s_min;
+  if (s_max > 4096) s_max = s_min > 4096 ? s_min : 4096;
+  int64_t best = s_min, best_cost = INT64_MAX;
+  for (int64_t s = s_min; s <= s_max; ++s) {
+    const int64_t waves = (U * s + kValSlots - 1) / kValSlots;
+    const int64_t tiles = (nt + s - 1) / s;
+    const int64_t rounds = (tiles + kValWarps - 1) / kValWarps;
+    const int64_t cost = waves * (rounds + 2);
+    if (cost < best_cost) { best_cost = cost; best = s; }
+  }
+  return (int)best;
 }
 
 // ===========================================================================
@@ -796,8 +867,8 @@ static int check_decode_shape(const char* what, int64_t B, int64_t H, int64_t G,
               (long long)G);
     return KVQ_ERR_UNSUPPORTED;
   }
-  if (T >= (1LL << 30)) {
-    set_error("%s: T too large", what);
+  if (T > (1LL << 24)) {  // positions are exact fp32 integers up to 2^24
+    set_error("%s: T=%lld exceeds 2^24 tokens", what, (long long)T);
     return KVQ_ERR_INVALID;
   }
   return KVQ_OK;

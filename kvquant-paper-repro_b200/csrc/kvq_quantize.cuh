@@ -281,6 +281,7 @@ template <int KIND, bool COUNT_ONLY>
 __global__ void __launch_bounds__(128) emit_kernel(EmitArgs a) {
   __shared__ int32_t cnt[32][8];  // per token, per 16-channel group (channel order)
   __shared__ float s_cb[16];
+  __shared__ uint8_t s_code[kTileTokens][kHeadDim];  // codes of the tile (token, channel)
   const int64_t b = blockIdx.y;
   const int64_t tile = blockIdx.x;
   const int64_t h = blockIdx.z;  // local head
@@ -300,7 +301,6 @@ __global__ void __launch_bounds__(128) emit_kernel(EmitArgs a) {
     rs = a.sel[b * a.S + t];
   }
   __syncthreads();
-  uint32_t slab[4] = {0, 0, 0, 0};  // up to 16 bytes (4-bit)
   uint32_t omask = 0;                // outlier flag per code slot
   float nval[32];
   const __half* xrow = a.x + (b * a.S + (t < a.S ? t : 0)) * a.C_full + (a.h0 + h) * kHeadDim;
@@ -328,11 +328,7 @@ __global__ void __launch_bounds__(128) emit_kernel(EmitArgs a) {
     }
     nval[q] = n;
     if (out) omask |= 1u << q;
-    if (!COUNT_ONLY) {
-      const int bit = q * a.bits;
-      slab[bit >> 5] |= (uint32_t)code << (bit & 31);
-      if ((bit & 31) + a.bits > 32) slab[(bit >> 5) + 1] |= (uint32_t)code >> (32 - (bit & 31));
-    }
+    if (!COUNT_ONLY) s_code[i][d] = (uint8_t)code;
   }
   // Outlier counts per (token, 16-channel group in channel order).
   if (KIND == 0) {
@@ -362,11 +358,34 @@ __global__ void __launch_bounds__(128) emit_kernel(EmitArgs a) {
   }
   __syncthreads();
   const int64_t base = a.out_ptr[unit * a.nt_cap + tile];
-  // Slab store.
-  const int sb = slab_bytes(a.bits);
-  uint8_t* dst = a.codes + (unit * a.nt_cap + tile) * (int64_t)tile_bytes(a.bits) +
-                 (int64_t)(j * 32 + i) * sb;
-  for (int w = 0; w < sb / 4; ++w) reinterpret_cast<uint32_t*>(dst)[w] = slab[w];
+  // Slab store: threads 0..63 each pack the slab of (block, lane) = (tid >> 5,
+  // tid & 31) in the fragment-native order of the decode kernels.
+  if (threadIdx.x < 64) {
+    const int blk = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, c = lane & 3;
+    uint32_t slab[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // up to 32 bytes (4-bit)
+#pragma unroll
+    for (int q = 0; q < 32; ++q) {
+      int ta, ca, tb, cb2;
+      if (KIND == 0) {  // keys: token 16*blk + g + 8*(q&1), RoPE pair 4*(q>>1) + c
+        ta = tb = 16 * blk + g + 8 * (q & 1);
+        ca = 4 * (q >> 1) + c;
+        cb2 = ca + 64;
+      } else {          // values: channel 16*(q>>2) + g + 8*(q&1), tokens (t, t+1)
+        ca = cb2 = 16 * (q >> 2) + g + 8 * (q & 1);
+        ta = 16 * blk + 2 * c + 8 * ((q >> 1) & 1);
+        tb = ta + 1;
+      }
+      const uint32_t pair = (uint32_t)s_code[ta][ca] | ((uint32_t)s_code[tb][cb2] << a.bits);
+      const int bit = 2 * a.bits * q;
+      slab[bit >> 5] |= pair << (bit & 31);
+      if ((bit & 31) + 2 * a.bits > 32) slab[(bit >> 5) + 1] |= pair >> (32 - (bit & 31));
+    }
+    const int sb = 8 * a.bits;  // bytes per lane slab
+    uint32_t* dst = reinterpret_cast<uint32_t*>(
+        a.codes + (unit * a.nt_cap + tile) * (int64_t)tile_bytes(a.bits) + (int64_t)threadIdx.x * sb);
+    for (int w = 0; w < sb / 4; ++w) dst[w] = slab[w];
+  }
   // Outlier entries in (token, channel) order.
   if (omask) {
     int32_t o0, o1;
@@ -402,10 +421,7 @@ __global__ void __launch_bounds__(128) emit_kernel(EmitArgs a) {
     for (int q = 0; q < 32; ++q) {
       const int d = slot_channel<KIND>(j, q);
       if (is_sink) { drow[d] = xrow[d]; continue; }
-      const int bit = q * a.bits;
-      uint32_t code = slab[bit >> 5] >> (bit & 31);
-      if ((bit & 31) + a.bits > 32) code |= slab[(bit >> 5) + 1] << (32 - (bit & 31));
-      code &= (1u << a.bits) - 1u;
+      const uint32_t code = s_code[i][d];
       const bool out = (omask >> q) & 1u;
       float s, z;
       if (KIND == 0) {

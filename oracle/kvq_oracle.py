@@ -29,8 +29,6 @@ F32 = np.float32
 TILE_TOKENS = 32     # tokens per code tile
 HEAD_DIM = 128       # channels per head (LLaMA head_dim)
 ROPE_PAIRS = HEAD_DIM // 2
-CHUNKS = 4           # 16-pair slabs per token row
-PAIRS_PER_CHUNK = 16
 EPS = F32(1e-8)      # kv_quantizer.py:82,110 `scale + 1e-8` (fp32 add)
 
 
@@ -313,19 +311,33 @@ def decode_attention(q, k_hat, v_hat, n_kv_heads: int, inv_freq):
 # --------------------------------------------------------------------------
 # Packed cache format (this build's layout; round-trips to reference indices)
 # --------------------------------------------------------------------------
-def slab_position(d: np.ndarray, kind: str):
-    """Channel d (0..127) -> (chunk j, pair m, second-of-pair flag).
+def slab_map(kind: str):
+    """Layout of one 32-token code tile: (block, lane, pair slot) -> elements.
 
-    keys:   pair m of chunk j holds channels (16j+m, 64+16j+m), the RoPE
-            rotate-half partners (rope_fused.py:38-43);
-    values: pair m of chunk j holds channels (32j+2m, 32j+2m+1).
+    A tile is 2 blocks of 16 tokens; each block holds one slab per lane
+    (lane = 4*g + c, g = lane >> 2, c = lane & 3) of 32 code pairs, ordered so
+    that a lane's slab is exactly its share of the tensor-core fragments of
+    the decode kernels. Returns int arrays [2, 32, 32] (block, lane, slot q):
+    (token_a, ch_a, token_b, ch_b) -- the pair's first and second code.
+
+    keys (m16n8k8 A fragments: rows = tokens, k = RoPE pair halves):
+        kb = q >> 1, r = q & 1: token 16*block + g + 8r, pair p = 4*kb + c,
+        first = channel p, second = channel p + 64 (rotate-half partners);
+    values (m16n8k16 A fragments of V^T: rows = channels, k = tokens):
+        mb = q >> 2, i = q & 3: channel 16*mb + g + 8*(i & 1),
+        first = token 16*block + 2c + 8*(i >> 1), second = that token + 1.
     """
-    d = np.asarray(d)
+    blk, lane, q = np.meshgrid(np.arange(2), np.arange(32), np.arange(32), indexing="ij")
+    g, c = lane >> 2, lane & 3
     if kind == "k":
-        p = d % ROPE_PAIRS
-        return p // PAIRS_PER_CHUNK, p % PAIRS_PER_CHUNK, (d >= ROPE_PAIRS).astype(np.int64)
-    j = d // 32
-    return j, (d % 32) // 2, d % 2
+        kb, r = q >> 1, q & 1
+        tok = 16 * blk + g + 8 * r
+        p = 4 * kb + c
+        return tok, p, tok, p + 64
+    mb, i = q >> 2, q & 3
+    ch = 16 * mb + g + 8 * (i & 1)
+    t0 = 16 * blk + 2 * c + 8 * (i >> 1)
+    return t0, ch, t0 + 1, ch
 
 
 def tile_bytes(bits: int) -> int:
@@ -335,10 +347,9 @@ def tile_bytes(bits: int) -> int:
 def pack_codes(idx: np.ndarray, bits: int, kind: str) -> np.ndarray:
     """Pack codes [U, T, 128] -> [U, ceil(T/32), 512*bits] uint8.
 
-    Tile = 4 slabs-chunks x 32 tokens; the slab of (chunk j, token i) is
-    4*bits bytes at offset (j*32 + i)*4*bits. Inside a slab, pair m occupies
-    bits [2*bits*m, 2*bits*m + 2*bits) of a little-endian bit stream, first
-    channel of the pair in the low `bits` bits.
+    Tile = [2 blocks][32 lanes][8*bits bytes]; slot q of a lane's slab is the
+    code pair of slab_map at bits [2*bits*q, 2*bits*q + 2*bits) of a
+    little-endian bit stream, first code in the low `bits` bits.
     """
     idx = np.asarray(idx, dtype=np.int64)
     U, T, D = idx.shape
@@ -347,14 +358,13 @@ def pack_codes(idx: np.ndarray, bits: int, kind: str) -> np.ndarray:
     codes = np.zeros((U, nt * TILE_TOKENS, D), dtype=np.int64)
     codes[:, :T] = idx
     codes = codes.reshape(U, nt, TILE_TOKENS, D)
-    j, m, sec = slab_position(np.arange(D), kind)
-    slot = 2 * m + sec                      # code slot 0..31 inside the slab
-    slab = np.zeros((U, nt, CHUNKS, TILE_TOKENS, 32), dtype=np.int64)
-    for d in range(D):
-        slab[:, :, j[d], :, slot[d]] = codes[:, :, :, d]
-    bitsarr = (slab[..., None] >> np.arange(bits)) & 1          # [..,32,bits]
-    flat = bitsarr.reshape(U, nt, CHUNKS, TILE_TOKENS, 32 * bits).astype(np.uint8)
-    packed = np.packbits(flat, axis=-1, bitorder="little")      # [..,4*bits]
+    ta, ca, tb, cb = slab_map(kind)
+    first = codes[:, :, ta, ca]                                  # [U, nt, 2, 32, 32]
+    second = codes[:, :, tb, cb]
+    slots = np.stack([first, second], axis=-1).reshape(U, nt, 2, 32, 64)
+    bitsarr = (slots[..., None] >> np.arange(bits)) & 1          # [.., 64, bits]
+    flat = bitsarr.reshape(U, nt, 2, 32, 64 * bits).astype(np.uint8)
+    packed = np.packbits(flat, axis=-1, bitorder="little")      # [.., 8*bits]
     return packed.reshape(U, nt, tile_bytes(bits))
 
 
@@ -362,14 +372,14 @@ def unpack_codes(packed: np.ndarray, bits: int, kind: str, T: int) -> np.ndarray
     """Inverse of pack_codes: [U, nt, 512*bits] uint8 -> [U, T, 128] int64."""
     packed = np.asarray(packed, dtype=np.uint8)
     U, nt, _ = packed.shape
-    slabs = packed.reshape(U, nt, CHUNKS, TILE_TOKENS, 4 * bits)
+    slabs = packed.reshape(U, nt, 2, 32, 8 * bits)
     bitsarr = np.unpackbits(slabs, axis=-1, bitorder="little").astype(np.int64)
-    bitsarr = bitsarr.reshape(U, nt, CHUNKS, TILE_TOKENS, 32, bits)
-    vals = (bitsarr << np.arange(bits)).sum(axis=-1)            # [U,nt,4,32,32]
-    j, m, sec = slab_position(np.arange(HEAD_DIM), kind)
+    vals = (bitsarr.reshape(U, nt, 2, 32, 64, bits) << np.arange(bits)).sum(axis=-1)
+    vals = vals.reshape(U, nt, 2, 32, 32, 2)
     out = np.empty((U, nt, TILE_TOKENS, HEAD_DIM), dtype=np.int64)
-    for d in range(HEAD_DIM):
-        out[:, :, :, d] = vals[:, :, j[d], :, 2 * m[d] + sec[d]]
+    ta, ca, tb, cb = slab_map(kind)
+    out[:, :, ta, ca] = vals[..., 0]
+    out[:, :, tb, cb] = vals[..., 1]
     return out.reshape(U, nt * TILE_TOKENS, HEAD_DIM)[:, :T]
 
 

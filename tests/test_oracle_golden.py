@@ -137,21 +137,35 @@ def test_pack_codes_round_trip(bits, kind):
 
 
 def test_pack_codes_layout_spot():
-    # keys, 4-bit: byte m of slab (chunk j, token i) = code(16j+m) | code(64+16j+m) << 4
+    # keys, 4-bit: byte q of the slab of (block, lane) holds the RoPE pair
+    # (4*(q >> 1) + c, +64) of token 16*block + g + 8*(q & 1), low nibble first
     idx = np.zeros((1, 32, 128), dtype=np.int64)
-    idx[0, 5, 16 * 2 + 3] = 7
-    idx[0, 5, 64 + 16 * 2 + 3] = 9
-    p = O.pack_codes(idx, 4, "k")
-    off = (2 * 32 + 5) * 16 + 3
-    assert p[0, 0, off] == 7 | (9 << 4)
-    assert p.sum() == p[0, 0, off]
-    # values, 2-bit: nibble m of slab (j, i) = code(32j+2m) | code(32j+2m+1) << 2
+    blk, lane, q = 1, 4 * 3 + 2, 2 * 5 + 1          # g=3, c=2, kb=5, r=1
+    tok, p = 16 * blk + 3 + 8, 4 * 5 + 2
+    idx[0, tok, p] = 7
+    idx[0, tok, p + 64] = 9
+    packed = O.pack_codes(idx, 4, "k")
+    off = (blk * 32 + lane) * 32 + q
+    assert packed[0, 0, off] == 7 | (9 << 4)
+    assert packed.sum() == packed[0, 0, off]
+    # values, 2-bit: nibble q of the slab holds channel 16*(q>>2) + g + 8*(q&1)
+    # of tokens (t, t+1), t = 16*block + 2c + 8*((q>>1)&1)
     idx = np.zeros((1, 32, 128), dtype=np.int64)
-    idx[0, 1, 32 * 3 + 2 * 5] = 2
-    idx[0, 1, 32 * 3 + 2 * 5 + 1] = 3
-    p = O.pack_codes(idx, 2, "v")
-    off = (3 * 32 + 1) * 8 + 5 // 2
-    assert p[0, 0, off] == (2 | (3 << 2)) << 4
+    blk, lane, q = 0, 4 * 6 + 1, 4 * 2 + 3           # g=6, c=1, mb=2, i=3
+    ch, t = 16 * 2 + 6 + 8, 2 * 1 + 8
+    idx[0, t, ch] = 2
+    idx[0, t + 1, ch] = 3
+    packed = O.pack_codes(idx, 2, "v")
+    off = (blk * 32 + lane) * 16 + q // 2
+    assert packed[0, 0, off] == (2 | (3 << 2)) << (4 * (q & 1))
+    assert packed.sum() == packed[0, 0, off]
+
+
+def test_slab_map_is_a_permutation():
+    for kind in ("k", "v"):
+        ta, ca, tb, cb = O.slab_map(kind)
+        cells = np.concatenate([ta.ravel() * 128 + ca.ravel(), tb.ravel() * 128 + cb.ravel()])
+        assert np.array_equal(np.sort(cells), np.arange(32 * 128))
 
 
 def test_outlier_entry_packing():
