@@ -11,11 +11,15 @@
  *     scratch comes from the caller through (workspace, workspace_bytes),
  *     sized by the matching *_workspace() query.
  *   - Layout of the quantized cache (per layer; unit u = b*n_heads + h):
- *       codes    uint8 [U, nt_cap, 512*bits]: tiles of 32 tokens; tile = 4
- *                chunks x 32 tokens x (4*bits)-byte slabs; slab (j,i) at
- *                byte (j*32+i)*4*bits; pair m at bits [2*bits*m, +2*bits).
- *                Keys: pair m of chunk j = channels (16j+m, 64+16j+m).
- *                Values: pair m of chunk j = channels (32j+2m, 32j+2m+1).
+ *       codes    uint8 [U, nt_cap, 512*bits]: tiles of 32 tokens; tile =
+ *                [2 blocks of 16 tokens][32 lanes][8*bits bytes], lane =
+ *                4g + c; slot q (0..31) of a lane's slab is a code pair at
+ *                bits [2*bits*q, +2*bits), first code in the low bits.
+ *                Keys: kb = q>>1, r = q&1: token 16*blk + g + 8r, channels
+ *                (p, p+64) with p = 4kb + c.
+ *                Values: mb = q>>2, i = q&3: channel 16mb + g + 8(i&1),
+ *                tokens (16blk + 2c + 8(i>>1), that + 1).
+ *                (The order of the decode kernels' tensor-core fragments.)
  *       outliers CSR over rows (u, tile): ptr int32 [U*nt_cap+1] and one
  *                uint32 entry per outlier: low 16 bits = (token_in_tile << 7)
  *                | channel_in_head, high 16 bits = the fp16 normalized raw
