@@ -169,6 +169,30 @@ int kvq_decode_attention(const uint8_t* k_codes, const uint32_t* k_out_ent,
                          float* scores_out, float* probs_out, void* workspace,
                          size_t workspace_bytes, void* stream);
 
+/* No counterpart in the reference. kvq_value_output without a workspace: the
+ * scratch comes from a fixed 4 MiB array owned by the library (one per
+ * device), for callers that cannot hand the library device memory of their
+ * own -- e.g. a host runtime binding this ABI through a plain FFI with no
+ * device allocator, or a decode loop that must not call cudaMalloc (it
+ * synchronizes the device) between steps. Same arguments and result as
+ * kvq_value_output minus (workspace, workspace_bytes).
+ *   - Limit: kvq_value_output_workspace(B, n_heads, group, T) must be at most
+ *     4 MiB (4194304 bytes); larger shapes return KVQ_ERR_INVALID with a
+ *     message and launch nothing.
+ *   - Nothing in the scratch needs to start at zero: the call writes every
+ *     byte of it that it reads.
+ *   - The first call on each device looks the array's address up
+ *     (cudaGetSymbolAddress with that device current) and caches it; make
+ *     that first call before any stream capture begins.
+ *   - All calls on one device share the array: calls whose work overlaps in
+ *     time (other streams, or unordered host threads) race on it; calls in
+ *     order on one stream are safe. */
+int kvq_value_output_noalloc(const uint8_t* codes, const uint32_t* out_ent,
+                             const int32_t* out_ptr, const float* v_scale, const float* v_zero,
+                             int64_t ld_stats, const void* v_sink, const float* codebook,
+                             int bits, const float* probs, int64_t B, int64_t n_heads,
+                             int64_t group, int64_t T, int64_t nt_cap, void* out, void* stream);
+
 /* Reads and clears the device-side error flag set by kernels that skip
  * out-of-range accesses (synchronizes `stream`). */
 int kvq_check_status(void* stream);

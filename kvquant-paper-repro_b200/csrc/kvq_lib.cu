@@ -5,3 +5,4 @@
 #include "kvq_ref_ops.cuh"
 #include "kvq_quantize.cuh"
 #include "kvq_decode.cuh"
+#include "kvq_noalloc.cuh"
