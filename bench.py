@@ -173,9 +173,9 @@ def algorithmic_bytes(wl, pk, pv, hl, T):
     U = B * hl
     nt = -(-T // 32)
     codes = U * T * 16 * bits
-    key = (codes + pk["nnz"] * 4 + U * nt * 4 + 2 * hl * 128 * 4 + B * hl * 128 * 2
+    key = (codes + pk["nnz"] * 4 + U * nt * 8 + 2 * hl * 128 * 4 + B * hl * 128 * 2
            + B * hl * G * 128 * 2 + B * hl * G * T * 4)
-    value = (codes + pv["nnz"] * 4 + U * nt * 4 + B * T * 8 + B * hl * 128 * 2
+    value = (codes + pv["nnz"] * 4 + U * nt * 8 + B * T * 8 + B * hl * 128 * 2
              + B * hl * G * T * 4 + B * hl * G * 128 * 2)
     softmax = 3 * B * hl * G * T * 4
     return {"key_scores": key, "value_output": value, "softmax": softmax}
@@ -395,8 +395,8 @@ def make_cpu_sample(wl, dev, units: int, T: int):
     ke_all, ve_all = h(pk["outlier_entries"]).view(np.uint32), h(pv["outlier_entries"]).view(np.uint32)
     for u in range(units):
         def seg(rp, ent):
-            a, b = int(rp[u * nt]), int(rp[(u + 1) * nt])
-            r = (rp[u * nt:(u + 1) * nt + 1] - a).astype(np.int32)
+            a, b = int(rp[2 * u * nt]), int(rp[2 * (u + 1) * nt])
+            r = (rp[2 * u * nt:2 * (u + 1) * nt + 1] - a).astype(np.int32)
             return ent[a:b], r
         kent, krp = seg(kr_all, ke_all)
         vent, vrp = seg(vr_all, ve_all)

@@ -85,7 +85,7 @@ __device__ __forceinline__ float entry_value(uint32_t ent) {
 // (each step one rounded FMA; |error| < 1e-6 rad for |a| < 2^24), then the
 // hardware sin/cos on [-pi, pi] (abs error < 4e-7).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ float rope_reduce(int64_t t, float f) {
+__device__ __forceinline__ float rope_reduce(int t, float f) {  // 0 <= t < 2^24
   const float a = __fmul_rn((float)t, f);
   const float k = rintf(a * 0.15915493667125702f);  // 1 / (2 pi)
   float r = fmaf(-k, 6.2831854820251465f, a);        // fl(2 pi)
@@ -103,34 +103,22 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
-__device__ __forceinline__ void mma_1688(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0,
-                                         float c0, float c1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, "
-      "{%7,%8,%7,%8};"
-      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-      : "r"(a0), "r"(a1), "r"(b0), "f"(c0), "f"(c1));
-}
-
-// Lane slab of one 16-token block (8*BITS bytes = 32 code pairs), staged in
-// shared memory as two 16-byte halves (structure of arrays per stage).
+// Lane slab of one 16-token block (8*BITS bytes = 32 code pairs). In the
+// cache a block is stored structure-of-arrays: region 0 = bytes 0..15 of the
+// 32 lane slabs (512 B), region 1 = their remaining 8*BITS-16 bytes; in shared
+// memory a slab is staged as two 16-byte slots (the second partly used).
 template <int BITS>
 struct LaneSlab {
   static constexpr int kBytes = 8 * BITS;
+  static constexpr int kRest = 8 * BITS - 16;  // bytes of region 1 per lane
   uint32_t w[8];
-  __device__ static __forceinline__ void copy(uint32_t dst0, uint32_t dst1, const uint8_t* src,
-                                              bool valid) {
+  // Asynchronous copy of lane `lane`'s slab of the block at `blk` (global).
+  __device__ static __forceinline__ void copy(uint32_t dst0, uint32_t dst1, const uint8_t* blk,
+                                              int lane, bool valid) {
     const uint32_t n = valid ? 1u : 0u;
-    if (BITS == 4) {
-      cp_async16(dst0, src, 16u * n);
-      cp_async16(dst1, src + 16, 16u * n);
-    } else if (BITS == 2) {
-      cp_async16(dst0, src, 16u * n);
-    } else {  // 24 bytes: 16 + 8
-      cp_async8(dst0, src, 8u * n);
-      cp_async8(dst0 + 8, src + 8, 8u * n);
-      cp_async8(dst1, src + 16, 8u * n);
-    }
+    cp_async16(dst0, blk + lane * 16, 16u * n);
+    if (BITS == 4) cp_async16(dst1, blk + 512 + lane * 16, 16u * n);
+    if (BITS == 3) cp_async8(dst1, blk + 512 + lane * 8, 8u * n);
   }
   __device__ __forceinline__ void read(const uint8_t* s0, const uint8_t* s1) {
     const uint4 v = *reinterpret_cast<const uint4*>(s0);
@@ -162,210 +150,237 @@ struct LaneSlab {
 // m16n8k8 MMA computes, for the 16 tokens,
 //   X_p = L1 P1 + L2 P2 + OX   (columns 0..3, pairs 4kb..4kb+3)
 //   Y_p = L1 Q1 + L2 Q2 + OY   (columns 4..7)
-// with A = the fp16 code values straight from the LUT (rows = tokens, k =
-// the two halves of each pair), B = the block-diagonal per-head constants
-// and C = the zero-point terms; the epilogue adds cos * X + sin * Y in fp32
-// with the token's exact-angle cos/sin held in registers.
+// with A = the fp16 code values straight from the LUT (rows = tokens, k = the
+// two halves of each pair), B = the block-diagonal per-head constants and C =
+// the zero-point terms, loaded straight into the accumulator registers. The
+// epilogue adds cos * X + sin * Y in fp32 with the token's exact-angle cos/sin
+// held in registers. Outliers add o * (cos P + sin Q) per entry with exact
+// trig; a block's entries (ordered by token) are summed per token with a warp
+// segmented scan, so every score has exactly one writer and no shared-memory
+// float atomics are needed.
+//
+// CTA = 16 warps, one CTA per SM; a work item is (group of up to 32 query-head
+// slots, 8 tiles = 256 tokens); warp w owns 16-token block w of the item for
+// every unit of the group, so the cos/sin registers are computed once per
+// item and reused for every unit.
 // ===========================================================================
-// Per-(slot, kb, c) constants, 16 bytes: B-fragment candidates for pair
-// 4kb + c (X column: half2(P1, P2), Y column: half2(Q1, Q2)) and the two
-// C-fragment values of columns 2c, 2c+1 (OX or OY of two pairs). All divided
-// by the slot's power-of-two sigma.
-struct KeyConst {
-  uint32_t bx, by;
-  float oa, ob;
-};
-
 struct KeyArgs {
   const uint8_t* codes;
   const uint32_t* out_ent;
-  const int32_t* out_ptr;
-  const float* k_scale;  // [H*128] local channels
+  const int32_t* out_ptr;  // CSR rows (unit, tile, 16-token block)
+  const float* k_scale;    // [H*128] local channels
   const float* k_zero;
-  const __half* k_sink;  // [B, H*128] or null
+  const __half* k_sink;    // [B, H*128] or null
   const float* cb;
-  const __half* q;       // [B, H*G, 128]
-  const float* inv_freq; // [64]
+  const __half* q;         // [B, H*G, 128]
+  const float* inv_freq;   // [64]
   int64_t B, H, G, T, nt_cap;
-  float* scores;         // [B, H*G, T]
+  float* scores;           // [B, H*G, T]
   int units_per_group, n_groups;
-  int64_t n_items;       // tile quads * groups
+  int64_t n_items;         // tile octets * groups
 };
 
-// CTA = 8 warps; warp w handles 16-token block w of a 128-token (4-tile) work
-// item for every unit of its group. Lane (g = lane >> 2, c = lane & 3) keeps
-// in registers the cos (c < 2) or sin (c >= 2) of its tokens g and g + 8 for
-// the 32 pairs 4kb + 2(c & 1) + {0, 1}.
-constexpr int kKeyThreads = 256;
-constexpr int kKeyTiles = 4;                     // tiles per work item
-constexpr int kKeyTokens = kKeyTiles * kTileTokens;
-constexpr int kMaxSlots = 32;                    // query heads per group
-constexpr int kKeyStages = 3;                    // units in flight per thread
+constexpr int kKeyWarps = 16;
+constexpr int kKeyThreads = kKeyWarps * 32;
+constexpr int kKeyTiles = kKeyWarps / 2;             // tiles per work item
+constexpr int kKeyTokens = kKeyTiles * kTileTokens;  // 256
+constexpr int kKeyRows = 2 * kKeyTiles;              // CSR rows per unit and item
+constexpr int kMaxSlots = 32;                        // query heads per group
+constexpr int kKeyStages = 3;                        // units in flight per thread
+constexpr int kBRow = 9;  // B words per (slot, kb): half2(P) x4, half2(Q) x4, zero
 
+// Shared memory of the key kernel: pair LUT; C quads {oa, ob, oa, ob} per
+// (slot, kb, c); B words per (slot, kb); scores [slot][256]; per-slot scale
+// sigma; the item's CSR row pointers per unit; the cp.async ring (per stage
+// and thread: the two 16-byte halves of the lane slab and one entry).
 template <int BITS>
 struct KeySmem {
   static constexpr int kLut = PairLut<BITS>::kBytes;
-  // 4-bit: constants in bytes 128..255 of the LUT rows (2048 cells x 16 B)
-  static constexpr int kConst = BITS == 4 ? 0 : kLut;
-  static constexpr int kSc = BITS == 4 ? kLut : kConst + kMaxSlots * 64 * 16;
+  static constexpr int kC = kLut;
+  static constexpr int kB = kC + kMaxSlots * 16 * 4 * 16;
+  static constexpr int kSc = kB + kMaxSlots * 16 * kBRow * 4;
   static constexpr int kSigma = kSc + kMaxSlots * kKeyTokens * 4;
-  static constexpr int kPtr = kSigma + kMaxSlots * 4;     // [units][kKeyTiles + 1]
-  static constexpr int kRing = kPtr + kMaxSlots * (kKeyTiles + 1) * 4;
-  static constexpr int kStage = kKeyThreads * (16 + 16 + 4);  // [half0][half1][entry]
+  static constexpr int kPtr = kSigma + kMaxSlots * 4;
+  static constexpr int kRing = (kPtr + kMaxSlots * (kKeyRows + 1) * 4 + 15) / 16 * 16;
+  static constexpr int kStage = kKeyThreads * (16 + 16 + 4);
   static constexpr int kBytes = kRing + kKeyStages * kStage;
+  static_assert(kC % 16 == 0 && kBytes <= 232448, "key kernel shared memory");
 };
 
 template <int BITS>
 __host__ __device__ constexpr int key_smem_bytes() { return KeySmem<BITS>::kBytes; }
 
-template <int BITS>
-__device__ __forceinline__ KeyConst* key_const(uint8_t* smem, int slot, int kb, int c) {
-  const int idx = (slot * 16 + kb) * 4 + c;  // < 2048 16-byte cells
-  if (BITS == 4)
-    return reinterpret_cast<KeyConst*>(smem + ((idx >> 3) << 8) + 128 + ((idx & 7) << 4));
-  return reinterpret_cast<KeyConst*>(smem + KeySmem<BITS>::kConst) + idx;
+// m16n8k8, fp16 inputs, fp32 accumulator d (= C on entry).
+__device__ __forceinline__ void mma_1688_acc(float& d0, float& d1, float& d2, float& d3,
+                                             uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d0), "+f"(d1), "+f"(d2), "+f"(d3)
+      : "r"(a0), "r"(a1), "r"(b0));
 }
 
-#ifndef KVQ_KEY_MIN_BLOCKS
-#define KVQ_KEY_MIN_BLOCKS 2  // resident CTAs per SM the register budget targets
-#endif
+__device__ __forceinline__ float half_lo(uint32_t w) {
+  return __half2float(__ushort_as_half((unsigned short)(w & 0xffffu)));
+}
+__device__ __forceinline__ float half_hi(uint32_t w) {
+  return __half2float(__ushort_as_half((unsigned short)(w >> 16)));
+}
+
+// Builds the per-slot tables of a group: sigma (power of two >= every |s q|
+// product of the slot), C quads and B words, all divided by sigma.
+template <int BITS, int G>
+__device__ void key_build_tables(const KeyArgs& a, uint8_t* smem, int u0, int nu) {
+  using L = KeySmem<BITS>;
+  float* sigma = reinterpret_cast<float*>(smem + L::kSigma);
+  float4* ct = reinterpret_cast<float4*>(smem + L::kC);
+  uint32_t* bt = reinterpret_cast<uint32_t*>(smem + L::kB);
+  const int64_t HG = a.H * G;
+  for (int s = threadIdx.x; s < kMaxSlots; s += blockDim.x) sigma[s] = 0.f;
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < nu * G * kPairs; idx += blockDim.x) {
+    const int s = idx / kPairs, p = idx % kPairs;
+    const int64_t u = u0 + s / G;
+    const int64_t b = u / a.H, h = u % a.H;
+    const __half* qv = a.q + (b * HG + h * G + s % G) * kHeadDim;
+    const float q1 = __half2float(qv[p]), q2 = __half2float(qv[p + 64]);
+    const float s1 = a.k_scale[h * kHeadDim + p], s2 = a.k_scale[h * kHeadDim + p + 64];
+    const float m = fmaxf(fmaxf(fabsf(s1 * q1), fabsf(s2 * q2)), fmaxf(fabsf(s1 * q2), fabsf(s2 * q1)));
+    atomicMax(reinterpret_cast<int*>(sigma + s), __float_as_int(m));
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < nu * G * 16 * (4 + kBRow); idx += blockDim.x) {
+    const int s = idx / (16 * (4 + kBRow)), r = idx % (16 * (4 + kBRow));
+    const int kb = r / (4 + kBRow), j = r % (4 + kBRow);
+    const int64_t u = u0 + s / G;
+    const int64_t b = u / a.H, h = u % a.H;
+    const __half* qv = a.q + (b * HG + h * G + s % G) * kHeadDim;
+    const float* scl = a.k_scale + h * kHeadDim;
+    const float* zer = a.k_zero + h * kHeadDim;
+    const float inv = ldexpf(1.f, -pow2_exponent(sigma[s]));
+    if (j < 4) {  // C quad of lane column pair c = j: OX (c < 2) or OY of pairs 4kb+2(c&1)+{0,1}
+      float o[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int p = 4 * kb + 2 * (j & 1) + e;
+        const float q1 = __half2float(qv[p]), q2 = __half2float(qv[p + 64]);
+        const float z1 = zer[p], z2 = zer[p + 64];
+        o[e] = (j < 2 ? (z1 * q1 + z2 * q2) : (z1 * q2 - z2 * q1)) * inv;
+      }
+      ct[(s * 16 + kb) * 4 + j] = make_float4(o[0], o[1], o[0], o[1]);
+    } else {      // B word jj: half2(P1, P2) of pair 4kb+jj (jj < 4), half2(Q1, Q2) of 4kb+jj-4
+      const int jj = j - 4;
+      uint32_t w = 0u;
+      if (jj < 8) {
+        const int p = 4 * kb + (jj & 3);
+        const float q1 = __half2float(qv[p]), q2 = __half2float(qv[p + 64]);
+        const float s1 = scl[p], s2 = scl[p + 64];
+        w = jj < 4 ? half2_bits(s1 * q1 * inv, s2 * q2 * inv)
+                   : half2_bits(s1 * q2 * inv, -s2 * q1 * inv);
+      }
+      bt[(s * 16 + kb) * kBRow + jj] = w;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < kMaxSlots) sigma[threadIdx.x] = ldexpf(1.f, pow2_exponent(sigma[threadIdx.x]));
+}
 
 template <int BITS, int G>
-__global__ void __launch_bounds__(kKeyThreads, KVQ_KEY_MIN_BLOCKS) key_scores_kernel(KeyArgs a) {
+__global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
   using L = KeySmem<BITS>;
-  uint8_t* lut = smem;
-  float* sc = reinterpret_cast<float*>(smem + L::kSc);        // [slots][128 tokens]
+  const uint8_t* lut = smem;
+  float* sc = reinterpret_cast<float*>(smem + L::kSc);        // [slots][256 tokens]
   float* sigma = reinterpret_cast<float*>(smem + L::kSigma);  // [slots]
-  int32_t* uptr = reinterpret_cast<int32_t*>(smem + L::kPtr);  // [units][kKeyTiles + 1]
+  int32_t* uptr = reinterpret_cast<int32_t*>(smem + L::kPtr);  // [units][kKeyRows + 1]
+  uint8_t* ring = smem + L::kRing;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const uint32_t lane4 = (uint32_t)lane << 2;
-  const uint32_t mask_x = (g == c) ? 0xffffffffu : 0u;      // this lane's B column is X of pair c
-  const uint32_t mask_y = (g == c + 4) ? 0xffffffffu : 0u;  // ... or Y of pair c
-  PairLut<BITS>::build(lut, a.cb);
-  uint8_t* ring = smem + L::kRing;
+  // B word of this lane: column g of the block-diagonal B is X of pair g
+  // (g < 4) or Y of pair g - 4; lane (g, c) holds rows 2c, 2c+1 of it.
+  const int jl = (g == c) ? c : ((g == c + 4) ? 4 + c : 8);
+  const uint8_t* bbase = smem + L::kB + jl * 4;
+  const uint8_t* cbase = smem + L::kC + c * 16;
+  PairLut<BITS>::build(smem, a.cb);
 
-  const int64_t nt = (a.T + kTileTokens - 1) / kTileTokens;
-  const int64_t n_quads = (nt + kKeyTiles - 1) / kKeyTiles;
+  const int nt = (int)((a.T + kTileTokens - 1) / kTileTokens);
+  const int n_oct = (nt + kKeyTiles - 1) / kKeyTiles;
   const int UG = a.units_per_group;
-  const int slots = UG * G;
   const int64_t w0 = a.n_items * blockIdx.x / gridDim.x;
   const int64_t w1 = a.n_items * (blockIdx.x + 1) / gridDim.x;
-  int cur_group = -1;
   const int64_t HG = a.H * G;
   const int64_t tbytes = kTileTokens * kHeadDim * BITS / 8;
-  const int64_t slab_off = (int64_t)((warp & 1) * 32 + lane) * (8 * BITS);
+  const int64_t ustride = a.nt_cap * tbytes;  // bytes between units
+  const int blk_off = (warp & 1) * (256 * BITS);  // this warp's block within a tile
+  int cur_group = -1;
 
   for (int64_t w = w0; w < w1; ++w) {
-    const int grp = (int)(w / n_quads);
-    const int64_t tq = w % n_quads;
+    const int grp = (int)(w / n_oct);
+    const int tile0 = kKeyTiles * (int)(w % n_oct);
     const int u0 = grp * UG;
     const int nu = (int)min((int64_t)UG, a.B * a.H - u0);
-    __syncthreads();  // previous item's readers are done with sc / tables
+    __syncthreads();  // the previous item's readers are done with sc / tables
     if (grp != cur_group) {
       cur_group = grp;
-      for (int s = threadIdx.x; s < slots; s += blockDim.x) sigma[s] = 0.f;
-      __syncthreads();
-      for (int idx = threadIdx.x; idx < nu * G * kPairs; idx += blockDim.x) {
-        const int s = idx / kPairs, p = idx % kPairs;
-        const int64_t u = u0 + s / G;
-        const int64_t b = u / a.H, h = u % a.H;
-        const int64_t hq = h * G + s % G;
-        const __half* qv = a.q + (b * HG + hq) * kHeadDim;
-        const float q1 = __half2float(qv[p]), q2 = __half2float(qv[p + 64]);
-        const float s1 = a.k_scale[h * kHeadDim + p], s2 = a.k_scale[h * kHeadDim + p + 64];
-        const float m = fmaxf(fmaxf(fabsf(s1 * q1), fabsf(s2 * q2)), fmaxf(fabsf(s1 * q2), fabsf(s2 * q1)));
-        atomicMax(reinterpret_cast<int*>(sigma + s), __float_as_int(m));
-      }
-      __syncthreads();
-      // cell (slot, kb, cc): B candidates of pair 4kb + cc, C values of columns 2cc, 2cc + 1
-      for (int idx = threadIdx.x; idx < nu * G * 64; idx += blockDim.x) {
-        const int s = idx / 64, kb = (idx % 64) >> 2, cc = idx & 3;
-        const int64_t u = u0 + s / G;
-        const int64_t b = u / a.H, h = u % a.H;
-        const int64_t hq = h * G + s % G;
-        const __half* qv = a.q + (b * HG + hq) * kHeadDim;
-        const float* scl = a.k_scale + h * kHeadDim;
-        const float* zer = a.k_zero + h * kHeadDim;
-        const float inv = ldexpf(1.f, -pow2_exponent(sigma[s]));
-        KeyConst kc;
-        {
-          const int p = 4 * kb + cc;
-          const float q1 = __half2float(qv[p]), q2 = __half2float(qv[p + 64]);
-          const float s1 = scl[p], s2 = scl[p + 64];
-          kc.bx = half2_bits(s1 * q1 * inv, s2 * q2 * inv);
-          kc.by = half2_bits(s1 * q2 * inv, -s2 * q1 * inv);
-        }
-        float o[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int p = 4 * kb + 2 * (cc & 1) + e;
-          const float q1 = __half2float(qv[p]), q2 = __half2float(qv[p + 64]);
-          const float z1 = zer[p], z2 = zer[p + 64];
-          o[e] = (cc < 2 ? (z1 * q1 + z2 * q2) : (z1 * q2 - z2 * q1)) * inv;
-        }
-        kc.oa = o[0];
-        kc.ob = o[1];
-        *key_const<BITS>(smem, s, kb, cc) = kc;
-      }
-      __syncthreads();
-      if (threadIdx.x < slots) sigma[threadIdx.x] = ldexpf(1.f, pow2_exponent(sigma[threadIdx.x]));
+      key_build_tables<BITS, G>(a, smem, u0, nu);
     }
-    for (int idx = threadIdx.x; idx < slots * kKeyTokens; idx += blockDim.x) sc[idx] = 0.f;
-    const int64_t tile0 = kKeyTiles * tq;
-    const int ntiles = (int)min((int64_t)kKeyTiles, nt - tile0);
-    for (int idx = threadIdx.x; idx < nu * (kKeyTiles + 1); idx += blockDim.x) {
-      const int ui = idx / (kKeyTiles + 1), k = idx % (kKeyTiles + 1);
-      uptr[idx] = __ldg(a.out_ptr + (u0 + ui) * a.nt_cap + tile0 + min(k, ntiles));
+    for (int idx = threadIdx.x; idx < nu * G * kKeyTokens; idx += blockDim.x) sc[idx] = 0.f;
+    const int ntiles = min(kKeyTiles, nt - tile0);
+    for (int idx = threadIdx.x; idx < nu * (kKeyRows + 1); idx += blockDim.x) {
+      const int ui = idx / (kKeyRows + 1), k = idx % (kKeyRows + 1);
+      uptr[idx] = __ldg(a.out_ptr + 2 * ((int64_t)(u0 + ui) * a.nt_cap + tile0) + min(k, 2 * ntiles));
     }
     __syncthreads();
 
-    const int64_t my_tile = tile0 + (warp >> 1);
+    const int my_tile = tile0 + (warp >> 1);
     const bool has = my_tile < nt;
+    const uint8_t* src = a.codes + ((int64_t)u0 * a.nt_cap + (has ? my_tile : tile0)) * tbytes + blk_off;
+    int wr_stage = 0;
     auto issue = [&](int ui) {
       if (ui < nu) {
-        uint8_t* st = ring + (ui % kKeyStages) * L::kStage;
-        const int64_t u = u0 + ui;
-        const uint8_t* src = a.codes + (u * a.nt_cap + (has ? my_tile : tile0)) * tbytes + slab_off;
+        uint8_t* st = ring + wr_stage * L::kStage;
         LaneSlab<BITS>::copy(smem_u32(st + threadIdx.x * 16),
-                             smem_u32(st + kKeyThreads * 16 + threadIdx.x * 16), src, has);
-        const int32_t e0 = uptr[ui * (kKeyTiles + 1)], e1 = uptr[ui * (kKeyTiles + 1) + ntiles];
-        const int32_t e = e0 + (int32_t)threadIdx.x;
+                             smem_u32(st + kKeyThreads * 16 + threadIdx.x * 16), src, lane, has);
+        src += ustride;
+        const int32_t e0 = uptr[ui * (kKeyRows + 1) + warp], e1 = uptr[ui * (kKeyRows + 1) + warp + 1];
+        const int32_t e = e0 + lane;
         cp_async4(smem_u32(st + kKeyThreads * 32 + threadIdx.x * 4), a.out_ent + (e < e1 ? e : 0),
                   e < e1 ? 4u : 0u);
+        wr_stage = wr_stage == kKeyStages - 1 ? 0 : wr_stage + 1;
       }
       cp_async_commit();
     };
     for (int ui = 0; ui < kKeyStages - 1; ++ui) issue(ui);
 
-    // cos (c < 2) or sin (c >= 2) of tokens g, g + 8 of this warp's block
-    // for pairs 4kb + 2(c & 1) + {0, 1}.
+    // cos (c < 2) or sin (c >= 2) of tokens g, g + 8 of this warp's block for
+    // pairs 4kb + 2(c & 1) + {0, 1}.
+    const int tok0 = tile0 * kTileTokens + 16 * warp;  // first token of the block
     float tw[16][4];
-    {
-      const int64_t tA = tile0 * kTileTokens + 16 * warp + g;
 #pragma unroll
-      for (int kb = 0; kb < 16; ++kb) {
+    for (int kb = 0; kb < 16; ++kb) {
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const float f = __ldg(a.inv_freq + 4 * kb + 2 * (c & 1) + e);
-          const float rA = rope_reduce(tA, f), rB = rope_reduce(tA + 8, f);
-          tw[kb][e] = c < 2 ? __cosf(rA) : __sinf(rA);
-          tw[kb][2 + e] = c < 2 ? __cosf(rB) : __sinf(rB);
-        }
+      for (int e = 0; e < 2; ++e) {
+        const float f = __ldg(a.inv_freq + 4 * kb + 2 * (c & 1) + e);
+        const float rA = rope_reduce(tok0 + g, f), rB = rope_reduce(tok0 + g + 8, f);
+        tw[kb][e] = c < 2 ? __cosf(rA) : __sinf(rA);
+        tw[kb][2 + e] = c < 2 ? __cosf(rB) : __sinf(rB);
       }
     }
 
+    int rd_stage = 0;
     for (int ui = 0; ui < nu; ++ui) {
       issue(ui + kKeyStages - 1);
       cp_async_wait<kKeyStages - 1>();
-      const uint8_t* st = ring + (ui % kKeyStages) * L::kStage;
+      const uint8_t* st = ring + rd_stage * L::kStage;
+      rd_stage = rd_stage == kKeyStages - 1 ? 0 : rd_stage + 1;
       LaneSlab<BITS> sl;
       sl.read(st + threadIdx.x * 16, st + kKeyThreads * 16 + threadIdx.x * 16);
-      uint32_t ent = *reinterpret_cast<const uint32_t*>(st + kKeyThreads * 32 + threadIdx.x * 4);
-      const int32_t e0 = uptr[ui * (kKeyTiles + 1)], e1 = uptr[ui * (kKeyTiles + 1) + ntiles];
-      const int32_t e_first = e0 + (int32_t)threadIdx.x;
+      const uint32_t ent0 = *reinterpret_cast<const uint32_t*>(st + kKeyThreads * 32 + threadIdx.x * 4);
+      const int slot0 = ui * G;
+      const uint8_t* brow = bbase + slot0 * (16 * kBRow * 4);
+      const uint8_t* crow = cbase + slot0 * (16 * 64);
 
       float accA[G], accB[G];
 #pragma unroll
@@ -376,12 +391,12 @@ __global__ void __launch_bounds__(kKeyThreads, KVQ_KEY_MIN_BLOCKS) key_scores_ke
         const uint32_t a1 = *reinterpret_cast<const uint32_t*>(lut + sl.addr(2 * kb + 1, lane4));
 #pragma unroll
         for (int gg = 0; gg < G; ++gg) {
-          const KeyConst kc = *key_const<BITS>(smem, ui * G + gg, kb, c);
-          const uint32_t b0 = (kc.bx & mask_x) | (kc.by & mask_y);
-          float d[4];
-          mma_1688(d, a0, a1, b0, kc.oa, kc.ob);
-          accA[gg] = fmaf(tw[kb][0], d[0], fmaf(tw[kb][1], d[1], accA[gg]));
-          accB[gg] = fmaf(tw[kb][2], d[2], fmaf(tw[kb][3], d[3], accB[gg]));
+          const uint32_t b0 = *reinterpret_cast<const uint32_t*>(brow + (gg * 16 + kb) * (kBRow * 4));
+          const float4 cq = *reinterpret_cast<const float4*>(crow + (gg * 16 + kb) * 64);
+          float d0 = cq.x, d1 = cq.y, d2 = cq.z, d3 = cq.w;
+          mma_1688_acc(d0, d1, d2, d3, a0, a1, b0);
+          accA[gg] = fmaf(tw[kb][0], d0, fmaf(tw[kb][1], d1, accA[gg]));
+          accB[gg] = fmaf(tw[kb][2], d2, fmaf(tw[kb][3], d3, accB[gg]));
         }
       }
 #pragma unroll
@@ -391,36 +406,46 @@ __global__ void __launch_bounds__(kKeyThreads, KVQ_KEY_MIN_BLOCKS) key_scores_ke
         y += __shfl_xor_sync(0xffffffffu, y, 1);
         x += __shfl_xor_sync(0xffffffffu, x, 2);
         y += __shfl_xor_sync(0xffffffffu, y, 2);
-        if (c == 0) {
-          atomicAdd(sc + (ui * G + gg) * kKeyTokens + 16 * warp + g, x);
-          atomicAdd(sc + (ui * G + gg) * kKeyTokens + 16 * warp + g + 8, y);
+        if (c == 0) {  // this warp is the only writer of its block's scores
+          sc[(slot0 + gg) * kKeyTokens + 16 * warp + g] = x;
+          sc[(slot0 + gg) * kKeyTokens + 16 * warp + g + 8] = y;
         }
       }
-      // Outliers: o * (cos * P + sin * Q) of the channel's half of the pair.
-      if (e_first < e1) {
-        int32_t bnd[kKeyTiles - 1];
+      // Outliers of the block: o * (cos P + sin Q) of the channel's half of the pair.
+      const int32_t e0 = uptr[ui * (kKeyRows + 1) + warp], e1 = uptr[ui * (kKeyRows + 1) + warp + 1];
+      if (e0 < e1) {
+        __syncwarp();
+        for (int32_t eb = e0; eb < e1; eb += 32) {
+          const int32_t e = eb + lane;
+          const bool valid = e < e1;
+          uint32_t en = eb == e0 ? ent0 : (valid ? __ldg(a.out_ent + e) : 0u);
+          const int tok = valid ? (int)((en >> 7) & 15) : 16 + lane;  // token within the block
+          const int ch = (int)(en & 127), p = ch & 63;
+          float sv, cv;
+          __sincosf(rope_reduce(tok0 + (tok & 15), __ldg(a.inv_freq + p)), &sv, &cv);
+          const float ov = valid ? entry_value(en) : 0.f;
+          // entries are ordered by token: suffix sums within runs of equal tokens
+          int tn[5];
 #pragma unroll
-        for (int k = 1; k < kKeyTiles; ++k) bnd[k - 1] = uptr[ui * (kKeyTiles + 1) + k];
-        for (int32_t e = e_first; e < e1; e += kKeyThreads) {
-          if (e != e_first) ent = __ldg(a.out_ent + e);
-          int k = 0;
-#pragma unroll
-          for (int qq = 0; qq < kKeyTiles - 1; ++qq) k += e >= bnd[qq] ? 1 : 0;
-          const int tok = k * kTileTokens + (int)((ent >> 7) & 31);
-          const int ch = (int)(ent & 127);
-          const int p = ch & 63, second = ch >> 6;
-          const float oval = entry_value(ent);
-          float cv, sv;
-          __sincosf(rope_reduce(tile0 * kTileTokens + tok, __ldg(a.inv_freq + p)), &sv, &cv);
+          for (int s = 0; s < 5; ++s) tn[s] = __shfl_down_sync(0xffffffffu, tok, 1 << s);
+          const int tprev = __shfl_up_sync(0xffffffffu, tok, 1);  // every lane takes part
+          const bool head = valid && (lane == 0 || tprev != tok);
 #pragma unroll
           for (int gg = 0; gg < G; ++gg) {
-            const KeyConst kc = *key_const<BITS>(smem, ui * G + gg, p >> 2, p & 3);
-            const __half2 pp = *reinterpret_cast<const __half2*>(&kc.bx);
-            const __half2 qq = *reinterpret_cast<const __half2*>(&kc.by);
-            const float P = second ? __high2float(pp) : __low2float(pp);
-            const float Q = second ? __high2float(qq) : __low2float(qq);
-            atomicAdd(sc + (ui * G + gg) * kKeyTokens + tok, oval * fmaf(cv, P, sv * Q));
+            const uint32_t* bw = reinterpret_cast<const uint32_t*>(
+                smem + L::kB + ((slot0 + gg) * 16 + (p >> 2)) * (kBRow * 4));
+            const uint32_t pw = bw[p & 3], qw = bw[4 + (p & 3)];
+            const float P = ch >= 64 ? half_hi(pw) : half_lo(pw);
+            const float Q = ch >= 64 ? half_hi(qw) : half_lo(qw);
+            float v = ov * fmaf(cv, P, sv * Q);
+#pragma unroll
+            for (int s = 0; s < 5; ++s) {
+              const float o = __shfl_down_sync(0xffffffffu, v, 1 << s);
+              if (lane + (1 << s) < 32 && tn[s] == tok) v += o;
+            }
+            if (head) sc[(slot0 + gg) * kKeyTokens + 16 * warp + tok] += v;
           }
+          __syncwarp();
         }
       }
     }
@@ -429,11 +454,10 @@ __global__ void __launch_bounds__(kKeyThreads, KVQ_KEY_MIN_BLOCKS) key_scores_ke
 
     // Sink token (position 0, no rotation): score = q . k_sink, fp32.
     if (tile0 == 0 && a.k_sink) {
-      for (int s = warp; s < nu * G; s += kKeyThreads / 32) {
+      for (int s = warp; s < nu * G; s += kKeyWarps) {
         const int64_t u = u0 + s / G;
         const int64_t b = u / a.H, h = u % a.H;
-        const int64_t hq = h * G + s % G;
-        const __half* qv = a.q + (b * HG + hq) * kHeadDim;
+        const __half* qv = a.q + (b * HG + h * G + s % G) * kHeadDim;
         const __half* kv = a.k_sink + (b * a.H + h) * kHeadDim;
         float v = 0.f;
         for (int dd = lane; dd < kHeadDim; dd += 32) v = fmaf(__half2float(qv[dd]), __half2float(kv[dd]), v);
@@ -445,12 +469,11 @@ __global__ void __launch_bounds__(kKeyThreads, KVQ_KEY_MIN_BLOCKS) key_scores_ke
 
     for (int idx = threadIdx.x; idx < nu * G * kKeyTokens; idx += blockDim.x) {
       const int s = idx / kKeyTokens, tt = idx % kKeyTokens;
-      const int64_t t = tile0 * kTileTokens + tt;
+      const int64_t t = (int64_t)tile0 * kTileTokens + tt;
       if (t >= a.T) continue;
       const int64_t u = u0 + s / G;
       const int64_t b = u / a.H, h = u % a.H;
-      const int64_t hq = h * G + s % G;
-      a.scores[(b * HG + hq) * a.T + t] = sc[idx] * sigma[s];
+      a.scores[(b * HG + h * G + s % G) * a.T + t] = sc[idx] * sigma[s];
     }
   }
 }
@@ -524,26 +547,27 @@ __global__ void __launch_bounds__(256) softmax_write_kernel(const float* __restr
 // B = the fp16 token weights w = p * s * 2^e (rows = tokens, columns = the
 // query heads of the KV head, zero beyond the group) and fp32 accumulators.
 // The zero-point term sum_t p_t z_t, the outliers (p s o into one channel)
-// and the sink token are added in fp32 beside it.
+// and the sink token are added in fp32 beside it; outliers go to per-warp
+// accumulators (groups of up to 4 heads) so that warps do not contend.
 //
 // CTA = 16 warps, one CTA per SM; a work item is (unit, split of its tiles)
 // and warp w takes the split's tiles w, w + 16, ...; each warp streams whole
-// tiles (codes, probabilities, scales, zeros, outlier entries) through its
+// tiles (codes, scale/zero pairs, probabilities, outlier entries) through its
 // own cp.async ring.
 // ===========================================================================
 struct ValueArgs {
   const uint8_t* codes;
   const uint32_t* out_ent;
-  const int32_t* out_ptr;
-  const float* v_scale;  // [B, ld]
+  const int32_t* out_ptr;  // CSR rows (unit, tile, 16-token block)
+  const float* v_scale;    // [B, ld]
   const float* v_zero;
   int64_t ld;
-  const __half* v_sink;  // [B, H*128] or null
+  const __half* v_sink;    // [B, H*128] or null
   const float* cb;
-  const float* probs;    // [B, H*G, T]
+  const float* probs;      // [B, H*G, T]
   int64_t B, H, G, T, nt_cap;
   int n_splits;
-  float* partial;        // [n_splits, B*H*G, 129]: 128 channels + zero term
+  float* partial;          // [n_splits, B*H*G, 129]: 128 channels + zero term
 };
 
 constexpr int kValWarps = 16;
@@ -568,21 +592,27 @@ __global__ void row_max_kernel(const float* __restrict__ vs, int64_t T, int64_t 
   }
 }
 
-// Value-kernel shared memory: pair LUT, fp32 side accumulators [G][129]
-// (outliers + sink per channel, zero term at 128), the item's outlier row
-// pointers and the per-warp cp.async rings. A ring stage of one warp holds one
-// tile: the two blocks' lane slabs (first 16 bytes of every lane, then the
-// rest), probabilities [G][kPRow], scales [32], zeros [32], entries [32].
+// Value-kernel shared memory: pair LUT; fp32 outlier + sink accumulators
+// ([warp][G][128] for G <= 4, else one [G][128]); zero-term sums [G]; the
+// item's tile row pointers; the per-warp cp.async rings. A ring stage of one
+// warp holds one tile: the two blocks' lane slabs (first 16 bytes of every
+// lane, then the rest), (scale, zero) pairs [32], probabilities [G][kPRow],
+// entries [32].
 template <int BITS, int G>
 struct ValSmem {
+  static constexpr bool kWarpAcc = G <= 4;
   static constexpr int kLut = PairLut<BITS>::kBytes;
   static constexpr int kAcc = kLut;
-  static constexpr int kPtr = kAcc + (G * 129 * 4 + 15) / 16 * 16;
+  static constexpr int kAccFloats = (kWarpAcc ? kValWarps : 1) * G * kHeadDim;
+  static constexpr int kZ = kAcc + kAccFloats * 4;
+  static constexpr int kPtr = kZ + 64;
   static constexpr int kRing = kPtr + (kValMaxTiles + 4) * 4;
-  static constexpr int kPRow = 40;  // floats per probability row (conflict-free float2 reads)
   static constexpr int kBlockSlab = 1024;
-  static constexpr int kFields = 2 * kBlockSlab;
-  static constexpr int kStage = kFields + 4 * (kPRow * G + 3 * 32);
+  static constexpr int kSZ = 2 * kBlockSlab;
+  static constexpr int kP = kSZ + 32 * 8;
+  static constexpr int kPRow = 40;  // floats per probability row (conflict-free float2 reads)
+  static constexpr int kE = kP + G * kPRow * 4;
+  static constexpr int kStage = kE + 32 * 4;
   static constexpr int kFit = (kValSmemLimit - kRing) / (kValWarps * kStage);
   static constexpr int kStages = kFit < 4 ? kFit : 4;
   static constexpr int kBytes = kRing + kStages * kValWarps * kStage;
@@ -598,20 +628,24 @@ __global__ void __launch_bounds__(kValThreads, 1)
   extern __shared__ __align__(16) uint8_t smem[];
   using S = ValSmem<BITS, G>;
   const uint8_t* lut = smem;
-  float* s_acc = reinterpret_cast<float*>(smem + S::kAcc);
+  float* acc = reinterpret_cast<float*>(smem + S::kAcc);
+  float* zacc = reinterpret_cast<float*>(smem + S::kZ);
   int32_t* tptr = reinterpret_cast<int32_t*>(smem + S::kPtr);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const uint32_t lane4 = (uint32_t)lane << 2;
+  float* wacc = acc + (S::kWarpAcc ? warp * G * kHeadDim : 0);
   PairLut<BITS>::build(smem, a.cb);
-  for (int idx = threadIdx.x; idx < G * 129; idx += blockDim.x) s_acc[idx] = 0.f;
+  for (int idx = threadIdx.x; idx < S::kAccFloats; idx += blockDim.x) acc[idx] = 0.f;
+  if (threadIdx.x < G) zacc[threadIdx.x] = 0.f;
 
-  const int64_t nt = (a.T + kTileTokens - 1) / kTileTokens;
+  const int nt = (int)((a.T + kTileTokens - 1) / kTileTokens);
+  const int T = (int)a.T;
   const int64_t U = a.B * a.H;
   const int64_t u = blockIdx.x / a.n_splits;
   const int split = (int)(blockIdx.x % a.n_splits);
-  const int64_t tpb = (nt + a.n_splits - 1) / a.n_splits;
-  const int64_t ta = split * tpb, tb = min(nt, ta + tpb);
+  const int tpb = (nt + a.n_splits - 1) / a.n_splits;
+  const int ta = split * tpb, tb = min(nt, ta + tpb);
   const int64_t b = u / a.H, h = u % a.H;
   const int64_t HG = a.H * G;
   const bool sink = a.v_sink != nullptr;
@@ -622,8 +656,8 @@ __global__ void __launch_bounds__(kValThreads, 1)
   // largest possible weight is 2^14 in fp16
   const float e_scale = ldexpf(1.f, 14 - pow2_exponent(row_max[b]));
   const float inv_e = 1.f / e_scale;
-  for (int64_t k = threadIdx.x; k <= tb - ta; k += blockDim.x)
-    tptr[k] = __ldg(a.out_ptr + u * a.nt_cap + ta + k);
+  for (int k = threadIdx.x; k <= tb - ta; k += blockDim.x)
+    tptr[k] = __ldg(a.out_ptr + 2 * (u * a.nt_cap + ta + k));
   __syncthreads();
 
   float d[8][4];
@@ -632,68 +666,69 @@ __global__ void __launch_bounds__(kValThreads, 1)
   float zs = 0.f;
 
   const int64_t tbytes = kTileTokens * kHeadDim * BITS / 8;
-  const uint8_t* ubase = a.codes + u * a.nt_cap * tbytes + lane * (8 * BITS);
+  const uint8_t* src = a.codes + (u * a.nt_cap + ta + warp) * tbytes;
+  int tnext = (ta + warp) * kTileTokens + lane;  // this lane's token of the next tile
   uint8_t* wring = smem + S::kRing + warp * S::kStage;
-  constexpr int kStageStride = kValWarps * S::kStage;
-  const int64_t my_n = ta + warp < tb ? (tb - ta - warp + kValWarps - 1) / kValWarps : 0;
-  auto issue = [&](int64_t i) {
+  constexpr int kStride = kValWarps * S::kStage;
+  const int my_n = ta + warp < tb ? (tb - ta - warp + kValWarps - 1) / kValWarps : 0;
+  int wr = 0;
+  auto issue = [&](int i) {
     if (i < my_n) {
-      const int64_t tile = ta + warp + i * kValWarps;
-      uint8_t* st = wring + (i % S::kStages) * kStageStride;
-      const uint8_t* src = ubase + tile * tbytes;
+      uint8_t* st = wring + wr * kStride;
+      wr = wr == S::kStages - 1 ? 0 : wr + 1;
 #pragma unroll
       for (int blk = 0; blk < 2; ++blk)
         LaneSlab<BITS>::copy(smem_u32(st + blk * S::kBlockSlab + lane * 16),
                              smem_u32(st + blk * S::kBlockSlab + 512 + lane * 16),
-                             src + blk * (32 * 8 * BITS), true);
-      const int64_t t = tile * kTileTokens + lane;
-      const bool live = t < a.T && !(sink && t == 0);
-      const int64_t tc = live ? t : 0;
-      const uint32_t f = smem_u32(st + S::kFields);
+                             src + blk * (256 * BITS), lane, true);
+      src += kValWarps * tbytes;
+      const int t = tnext;
+      tnext += kValWarps * kTileTokens;
+      const bool live = t < T && !(sink && t == 0);
+      const int tc = live ? t : 0;
+      const uint32_t n = live ? 4u : 0u;
+      const uint32_t fsz = smem_u32(st + S::kSZ + lane * 8);
+      cp_async4(fsz, vs + tc, n);
+      cp_async4(fsz + 4, vz + tc, n);
 #pragma unroll
       for (int hd = 0; hd < G; ++hd)
-        cp_async4(f + (hd * S::kPRow + lane) * 4, prow + hd * a.T + tc, live ? 4u : 0u);
-      cp_async4(f + (G * S::kPRow + lane) * 4, vs + tc, live ? 4u : 0u);
-      cp_async4(f + (G * S::kPRow + 32 + lane) * 4, vz + tc, live ? 4u : 0u);
-      const int32_t e0 = tptr[tile - ta], e1 = tptr[tile - ta + 1];
+        cp_async4(smem_u32(st + S::kP + (hd * S::kPRow + lane) * 4), prow + hd * a.T + tc, n);
+      const int k = warp + i * kValWarps;
+      const int32_t e0 = tptr[k], e1 = tptr[k + 1];
       const int32_t e = e0 + lane;
-      cp_async4(f + (G * S::kPRow + 64 + lane) * 4, a.out_ent + (e < e1 ? e : 0),
-                e < e1 ? 4u : 0u);
+      cp_async4(smem_u32(st + S::kE + lane * 4), a.out_ent + (e < e1 ? e : 0), e < e1 ? 4u : 0u);
     }
     cp_async_commit();
   };
 
-  for (int64_t i = 0; i < S::kStages - 1; ++i) issue(i);
+  for (int i = 0; i < S::kStages - 1; ++i) issue(i);
   const int gq = g < G ? g : 0;
-  for (int64_t i = 0; i < my_n; ++i) {
+  int rd = 0;
+  for (int i = 0; i < my_n; ++i) {
     __syncwarp();  // every lane is done with the stage the next copy overwrites
     issue(i + S::kStages - 1);
     cp_async_wait<S::kStages - 1>();
     __syncwarp();  // ... and sees the other lanes' copies of this one
-    const int64_t tile = ta + warp + i * kValWarps;
-    const uint8_t* st = wring + (i % S::kStages) * kStageStride;
-    const float* fp = reinterpret_cast<const float*>(st + S::kFields);
-    const float* fs = fp + G * S::kPRow;
-    const float* fz = fs + 32;
-    const uint32_t* fe = reinterpret_cast<const uint32_t*>(fz + 32);
+    const uint8_t* st = wring + rd * kStride;
+    rd = rd == S::kStages - 1 ? 0 : rd + 1;
+    const float2* sz = reinterpret_cast<const float2*>(st + S::kSZ);
+    const float* fp = reinterpret_cast<const float*>(st + S::kP);
 #pragma unroll
     for (int blk = 0; blk < 2; ++blk) {
       LaneSlab<BITS> sl;
       sl.read(st + blk * S::kBlockSlab + lane * 16, st + blk * S::kBlockSlab + 512 + lane * 16);
       const int t0 = 16 * blk + 2 * c;
-      const float2 s01 = *reinterpret_cast<const float2*>(fs + t0);
-      const float2 s89 = *reinterpret_cast<const float2*>(fs + t0 + 8);
+      const float4 sz01 = *reinterpret_cast<const float4*>(sz + t0);      // s, z of t0, t0+1
+      const float4 sz89 = *reinterpret_cast<const float4*>(sz + t0 + 8);  // ... of t0+8, t0+9
       const float2 p01 = *reinterpret_cast<const float2*>(fp + gq * S::kPRow + t0);
       const float2 p89 = *reinterpret_cast<const float2*>(fp + gq * S::kPRow + t0 + 8);
-      const float2 z01 = *reinterpret_cast<const float2*>(fz + t0);
-      const float2 z89 = *reinterpret_cast<const float2*>(fz + t0 + 8);
-      uint32_t b0 = half2_bits(p01.x * s01.x * e_scale, p01.y * s01.y * e_scale);
-      uint32_t b1 = half2_bits(p89.x * s89.x * e_scale, p89.y * s89.y * e_scale);
+      uint32_t b0 = half2_bits(p01.x * sz01.x * e_scale, p01.y * sz01.z * e_scale);
+      uint32_t b1 = half2_bits(p89.x * sz89.x * e_scale, p89.y * sz89.z * e_scale);
       if (g < G) {
-        zs = fmaf(p01.x, z01.x, zs);
-        zs = fmaf(p01.y, z01.y, zs);
-        zs = fmaf(p89.x, z89.x, zs);
-        zs = fmaf(p89.y, z89.y, zs);
+        zs = fmaf(p01.x, sz01.y, zs);
+        zs = fmaf(p01.y, sz01.w, zs);
+        zs = fmaf(p89.x, sz89.y, zs);
+        zs = fmaf(p89.y, sz89.w, zs);
       } else {
         b0 = b1 = 0u;
       }
@@ -707,32 +742,33 @@ __global__ void __launch_bounds__(kValThreads, 1)
       }
     }
     // Outliers: p s o into channel ch, fp32.
-    const int32_t e0 = tptr[tile - ta], e1 = tptr[tile - ta + 1];
+    const int k = warp + i * kValWarps;
+    const int32_t e0 = tptr[k], e1 = tptr[k + 1];
+    const uint32_t* fe = reinterpret_cast<const uint32_t*>(st + S::kE);
     for (int32_t eb = e0; eb < e1; eb += 32) {
       const int32_t e = eb + lane;
       if (e < e1) {
-        const uint32_t ent = eb == e0 ? fe[lane] : __ldg(a.out_ent + e);
-        const int tok = (int)((ent >> 7) & 31), ch = (int)(ent & 127);
-        const float so = fs[tok] * entry_value(ent);
+        const uint32_t en = eb == e0 ? fe[lane] : __ldg(a.out_ent + e);
+        const int tok = (int)((en >> 7) & 31), ch = (int)(en & 127);
+        const float so = sz[tok].x * entry_value(en);
 #pragma unroll
-        for (int hd = 0; hd < G; ++hd)
-          atomicAdd(s_acc + hd * 129 + ch, fp[hd * S::kPRow + tok] * so);
+        for (int hd = 0; hd < G; ++hd) atomicAdd(wacc + hd * kHeadDim + ch, fp[hd * S::kPRow + tok] * so);
       }
     }
   }
   cp_async_wait<0>();
   zs += __shfl_xor_sync(0xffffffffu, zs, 1);
   zs += __shfl_xor_sync(0xffffffffu, zs, 2);
-  if (c == 0 && g < G) atomicAdd(s_acc + g * 129 + 128, zs);
+  if (c == 0 && g < G) atomicAdd(zacc + g, zs);
   // Sink (token 0, in the first split): p_0 * v_sink, fp32.
   if (sink && ta == 0) {
     for (int idx = threadIdx.x; idx < G * kHeadDim; idx += blockDim.x) {
       const int hd = idx / kHeadDim, dd = idx % kHeadDim;
-      atomicAdd(s_acc + hd * 129 + dd,
+      atomicAdd(acc + hd * kHeadDim + dd,
                 prow[hd * a.T] * __half2float(a.v_sink[(b * a.H + h) * kHeadDim + dd]));
     }
   }
-  __syncthreads();  // all warps are done with their rings
+  __syncthreads();  // all warps are done with their rings and accumulators
   float* red = reinterpret_cast<float*>(smem + S::kRing);  // [warp][G][128]
 #pragma unroll
   for (int mb = 0; mb < 8; ++mb) {
@@ -748,13 +784,19 @@ __global__ void __launch_bounds__(kValThreads, 1)
   }
   __syncthreads();
   for (int idx = threadIdx.x; idx < G * kHeadDim; idx += blockDim.x) {
-    const int hd = idx / kHeadDim, dd = idx % kHeadDim;
-    float sum = 0.f;
+    float sum = 0.f, side = 0.f;
 #pragma unroll
-    for (int w = 0; w < kValWarps; ++w) sum += red[(w * G + hd) * kHeadDim + dd];
+    for (int w = 0; w < kValWarps; ++w) sum += red[w * G * kHeadDim + idx];
+    if (S::kWarpAcc) {
+#pragma unroll
+      for (int w = 0; w < kValWarps; ++w) side += acc[w * G * kHeadDim + idx];
+    } else {
+      side = acc[idx];
+    }
+    const int hd = idx / kHeadDim, dd = idx % kHeadDim;
     float* dst = a.partial + ((int64_t)split * (U * G) + u * G + hd) * 129;
-    dst[dd] = fmaf(sum, inv_e, s_acc[hd * 129 + dd]);
-    if (dd == 0) dst[128] = s_acc[hd * 129 + 128];
+    dst[dd] = fmaf(sum, inv_e, side);
+    if (dd == 0) dst[128] = zacc[hd];
   }
 }
 
@@ -806,8 +848,8 @@ static int launch_key(const KeyArgs& a0, cudaStream_t st) {
   a.units_per_group = UG;
   a.n_groups = (int)((U + UG - 1) / UG);
   const int64_t nt = (a.T + kTileTokens - 1) / kTileTokens;
-  const int64_t n_quads = (nt + kKeyTiles - 1) / kKeyTiles;
-  a.n_items = n_quads * a.n_groups;
+  const int64_t n_oct = (nt + kKeyTiles - 1) / kKeyTiles;
+  a.n_items = n_oct * a.n_groups;
   const int smem = key_smem_bytes<BITS>();
   cudaFuncSetAttribute(key_scores_kernel<BITS, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   int per_sm = 1;

@@ -240,8 +240,9 @@ __global__ void __launch_bounds__(256) value_plan_kernel(
 
 // ---------------------------------------------------------------------------
 // Emit: one CTA (128 threads = 4 chunks x 32 tokens) per (b, tile, head).
-// KIND 0 = keys, 1 = values. COUNT_ONLY: write the per-(unit,tile) outlier
-// count into out_ptr[unit*nt_cap + tile + 1] (prefix-summed afterwards).
+// KIND 0 = keys, 1 = values. COUNT_ONLY: write the outlier counts of the
+// tile's two 16-token blocks into out_ptr[2*(unit*nt_cap + tile) + blk + 1]
+// (prefix-summed afterwards into the CSR row pointer over (unit, tile, blk)).
 // ---------------------------------------------------------------------------
 struct EmitArgs {
   const __half* x;
@@ -340,10 +341,10 @@ __global__ void __launch_bounds__(128) emit_kernel(EmitArgs a) {
   }
   __syncthreads();
   if (COUNT_ONLY) {
-    if (threadIdx.x == 0) {
+    if (threadIdx.x < 2) {  // block threadIdx.x = tokens 16*blk .. 16*blk+15
       int32_t tot = 0;
-      for (int r = 0; r < 32 * 8; ++r) tot += (&cnt[0][0])[r];
-      a.out_ptr[unit * a.nt_cap + tile + 1] = tot;
+      for (int r = 16 * 8 * threadIdx.x; r < 16 * 8 * (threadIdx.x + 1); ++r) tot += (&cnt[0][0])[r];
+      a.out_ptr[2 * (unit * a.nt_cap + tile) + threadIdx.x + 1] = tot;
     }
     return;
   }
@@ -357,7 +358,7 @@ __global__ void __launch_bounds__(128) emit_kernel(EmitArgs a) {
     }
   }
   __syncthreads();
-  const int64_t base = a.out_ptr[unit * a.nt_cap + tile];
+  const int64_t base = a.out_ptr[2 * (unit * a.nt_cap + tile)];  // first entry of the tile
   // Slab store: threads 0..63 each pack the slab of (block, lane) = (tid >> 5,
   // tid & 31) in the fragment-native order of the decode kernels.
   if (threadIdx.x < 64) {
@@ -381,10 +382,16 @@ __global__ void __launch_bounds__(128) emit_kernel(EmitArgs a) {
       slab[bit >> 5] |= pair << (bit & 31);
       if ((bit & 31) + 2 * a.bits > 32) slab[(bit >> 5) + 1] |= pair >> (32 - (bit & 31));
     }
-    const int sb = 8 * a.bits;  // bytes per lane slab
-    uint32_t* dst = reinterpret_cast<uint32_t*>(
-        a.codes + (unit * a.nt_cap + tile) * (int64_t)tile_bytes(a.bits) + (int64_t)threadIdx.x * sb);
-    for (int w = 0; w < sb / 4; ++w) dst[w] = slab[w];
+    // The block is stored structure-of-arrays: bytes 0..15 of every lane's
+    // slab (512 B), then its remaining 8*bits-16 bytes, so that the decode
+    // kernels' per-lane copies are coalesced.
+    uint8_t* blk_base = a.codes + (unit * a.nt_cap + tile) * (int64_t)tile_bytes(a.bits) +
+                        blk * (256 * a.bits);
+    *reinterpret_cast<uint4*>(blk_base + lane * 16) = make_uint4(slab[0], slab[1], slab[2], slab[3]);
+    if (a.bits == 4)
+      *reinterpret_cast<uint4*>(blk_base + 512 + lane * 16) = make_uint4(slab[4], slab[5], slab[6], slab[7]);
+    else if (a.bits == 3)
+      *reinterpret_cast<uint2*>(blk_base + 512 + lane * 8) = make_uint2(slab[4], slab[5]);
   }
   // Outlier entries in (token, channel) order.
   if (omask) {
@@ -438,7 +445,7 @@ __global__ void __launch_bounds__(128) emit_kernel(EmitArgs a) {
 }
 
 // Single-CTA exclusive scan of counts stored at ptr[1..n] (ptr[0] = 0) and the
-// total nnz. n is U * nt_cap.
+// total nnz. n is the number of CSR rows (2 * U * nt_cap).
 __global__ void __launch_bounds__(1024) scan_counts_kernel(int32_t* __restrict__ ptr, int64_t n,
                                                            int64_t* __restrict__ nnz_out) {
   __shared__ int64_t part[1024];
@@ -567,8 +574,8 @@ extern "C" int kvq_quantize_keys_plan(const void* k, int64_t B, int64_t S, int64
     }
     key_ties_kernel<<<(unsigned)((ncols + 7) / 8), 256, 0, st>>>(ks, sel, ncols);
   }
-  // Outlier counts per (unit, tile), then the row pointer.
-  const int64_t nrows = B * n_heads * nt_cap;
+  // Outlier counts per (unit, tile, block), then the row pointer.
+  const int64_t nrows = 2 * B * n_heads * nt_cap;  // (unit, tile, 16-token block)
   zero_i32_kernel<<<grid_for(nrows + 1, 256), 256, 0, st>>>(out_ptr, nrows + 1);
   EmitArgs ea{};
   ea.x = ks.k; ea.B = B; ea.S = S; ea.C_full = C_full; ea.h0 = h0; ea.H = n_heads;
@@ -662,7 +669,7 @@ extern "C" int kvq_quantize_values_plan(const void* v, int64_t B, int64_t S, int
       cudaMemsetAsync(v_zero + b * ld_stats, 0, sizeof(float), st);
     }
   }
-  const int64_t nrows = B * n_heads * nt_cap;
+  const int64_t nrows = 2 * B * n_heads * nt_cap;  // (unit, tile, 16-token block)
   zero_i32_kernel<<<grid_for(nrows + 1, 256), 256, 0, st>>>(out_ptr, nrows + 1);
   EmitArgs ea{};
   ea.x = (const __half*)v; ea.B = B; ea.S = S; ea.C_full = C_full; ea.h0 = h0;

@@ -59,7 +59,8 @@ def _quantize(kind: str, x: torch.Tensor, codebook: torch.Tensor, bits: int,
     if cb.numel() != (1 << bits):
         raise RuntimeError(f"quantize_{kind}: codebook has {cb.numel()} entries, need {1 << bits}")
     U = B * H
-    out_ptr = torch.empty(U * nt_cap + 1, dtype=torch.int32, device=dev)
+    # CSR row pointer over (unit, tile, 16-token block): 2 rows per tile
+    out_ptr = torch.empty(2 * U * nt_cap + 1, dtype=torch.int32, device=dev)
     nnz_dev = torch.zeros(1, dtype=torch.int64, device=dev)
     codes = torch.empty((U, nt_cap, tile_bytes(bits)), dtype=torch.uint8, device=dev)
     sink_t = torch.empty((B, H * HEAD_DIM), dtype=torch.float16, device=dev) \

@@ -344,12 +344,36 @@ def tile_bytes(bits: int) -> int:
     return TILE_TOKENS * HEAD_DIM * bits // 8
 
 
+def _slabs_to_tile(slabs: np.ndarray, bits: int) -> np.ndarray:
+    """Lane slabs [..., 2, 32, 8*bits] -> tile bytes [..., 512*bits].
+
+    Each 16-token block is stored structure-of-arrays: first bytes 0..15 of
+    all 32 lane slabs (512 B), then the remaining 8*bits-16 bytes of all
+    lanes, so that every copy of a lane's bytes is coalesced across the warp.
+    """
+    lead = slabs.shape[:-2]
+    r0 = slabs[..., :16].reshape(*lead[:-1], 2, 32 * 16)
+    r1 = slabs[..., 16:].reshape(*lead[:-1], 2, 32 * (8 * bits - 16))
+    return np.concatenate([r0, r1], axis=-1).reshape(*lead[:-1], 512 * bits)
+
+
+def _tile_to_slabs(tiles: np.ndarray, bits: int) -> np.ndarray:
+    """Inverse of _slabs_to_tile: [..., 512*bits] -> [..., 2, 32, 8*bits]."""
+    lead = tiles.shape[:-1]
+    blocks = tiles.reshape(*lead, 2, 256 * bits)
+    r0 = blocks[..., :512].reshape(*lead, 2, 32, 16)
+    r1 = blocks[..., 512:].reshape(*lead, 2, 32, 8 * bits - 16)
+    return np.concatenate([r0, r1], axis=-1)
+
+
 def pack_codes(idx: np.ndarray, bits: int, kind: str) -> np.ndarray:
     """Pack codes [U, T, 128] -> [U, ceil(T/32), 512*bits] uint8.
 
-    Tile = [2 blocks][32 lanes][8*bits bytes]; slot q of a lane's slab is the
-    code pair of slab_map at bits [2*bits*q, 2*bits*q + 2*bits) of a
-    little-endian bit stream, first code in the low `bits` bits.
+    Tile = 2 blocks of 16 tokens; each block holds one slab per lane of
+    8*bits bytes (stored structure-of-arrays, see _slabs_to_tile). Slot q of a
+    lane's slab is the code pair of slab_map at bits [2*bits*q, 2*bits*q +
+    2*bits) of the slab's little-endian bit stream, first code in the low
+    `bits` bits.
     """
     idx = np.asarray(idx, dtype=np.int64)
     U, T, D = idx.shape
@@ -364,15 +388,15 @@ def pack_codes(idx: np.ndarray, bits: int, kind: str) -> np.ndarray:
     slots = np.stack([first, second], axis=-1).reshape(U, nt, 2, 32, 64)
     bitsarr = (slots[..., None] >> np.arange(bits)) & 1          # [.., 64, bits]
     flat = bitsarr.reshape(U, nt, 2, 32, 64 * bits).astype(np.uint8)
-    packed = np.packbits(flat, axis=-1, bitorder="little")      # [.., 8*bits]
-    return packed.reshape(U, nt, tile_bytes(bits))
+    slabs = np.packbits(flat, axis=-1, bitorder="little")       # [.., 8*bits]
+    return _slabs_to_tile(slabs, bits)
 
 
 def unpack_codes(packed: np.ndarray, bits: int, kind: str, T: int) -> np.ndarray:
     """Inverse of pack_codes: [U, nt, 512*bits] uint8 -> [U, T, 128] int64."""
     packed = np.asarray(packed, dtype=np.uint8)
     U, nt, _ = packed.shape
-    slabs = packed.reshape(U, nt, 2, 32, 8 * bits)
+    slabs = _tile_to_slabs(packed, bits)
     bitsarr = np.unpackbits(slabs, axis=-1, bitorder="little").astype(np.int64)
     vals = (bitsarr.reshape(U, nt, 2, 32, 64, bits) << np.arange(bits)).sum(axis=-1)
     vals = vals.reshape(U, nt, 2, 32, 32, 2)
@@ -384,24 +408,29 @@ def unpack_codes(packed: np.ndarray, bits: int, kind: str, T: int) -> np.ndarray
 
 
 def tile_outliers(mask: np.ndarray, values: np.ndarray):
-    """Outliers of [U, T, 128] -> CSR over rows (unit, tile).
+    """Outliers of [U, T, 128] -> CSR over rows (unit, tile, 16-token block).
 
-    Returns (values fp16 [nnz], pos uint16 [nnz] = (token_in_tile << 7) | d,
-    row_ptr int32 [U*nt + 1]); entries of a row are ordered by (token, d).
+    Row r = 2 * (u * nt + tile) + blk holds the outliers of tokens
+    16*blk .. 16*blk + 15 of the tile, so a tile's entries are rows 2r', 2r'+1
+    back to back. Returns (values fp16 [nnz], pos uint16 [nnz] =
+    (token_in_tile << 7) | d, row_ptr int32 [2*U*nt + 1]); entries of a row are
+    ordered by (token, d).
     """
     U, T, D = mask.shape
     nt = (T + TILE_TOKENS - 1) // TILE_TOKENS
+    half = TILE_TOKENS // 2
     m = np.zeros((U, nt * TILE_TOKENS, D), dtype=bool)
     m[:, :T] = mask
     v = np.zeros((U, nt * TILE_TOKENS, D), dtype=F32)
     v[:, :T] = values
-    m = m.reshape(U * nt, TILE_TOKENS * D)
-    v = v.reshape(U * nt, TILE_TOKENS * D)
+    m = m.reshape(U * nt * 2, half * D)
+    v = v.reshape(U * nt * 2, half * D)
     counts = m.sum(axis=1)
-    row_ptr = np.zeros(U * nt + 1, dtype=np.int32)
+    row_ptr = np.zeros(U * nt * 2 + 1, dtype=np.int32)
     row_ptr[1:] = np.cumsum(counts)
     r, flatpos = np.nonzero(m)
-    return v[r, flatpos].astype(F16), flatpos.astype(np.uint16), row_ptr
+    pos = (r % 2) * (half * D) + flatpos       # position within the 32-token tile
+    return v[r, flatpos].astype(F16), pos.astype(np.uint16), row_ptr
 
 
 def pack_entries(vals, pos) -> np.ndarray:
@@ -421,7 +450,7 @@ def untile_outliers(vals, pos, row_ptr, U: int, T: int):
     nt = (T + TILE_TOKENS - 1) // TILE_TOKENS
     dense = np.zeros((U * nt, TILE_TOKENS * HEAD_DIM), dtype=F32)
     mask = np.zeros_like(dense, dtype=bool)
-    rows = np.repeat(np.arange(U * nt), np.diff(np.asarray(row_ptr, np.int64)))
+    rows = np.repeat(np.arange(U * nt * 2), np.diff(np.asarray(row_ptr, np.int64))) // 2
     p = np.asarray(pos, dtype=np.int64)
     dense[rows, p] = np.asarray(vals, dtype=F16).astype(F32)
     mask[rows, p] = True

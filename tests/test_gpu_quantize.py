@@ -53,11 +53,10 @@ def check_packed(p, exp, tag, nt):
 
 
 def _compact_rowptr(rp, U, nt_cap, nt):
-    """Row pointer over (unit, tile < nt) from one over (unit, tile < nt_cap)."""
+    """Row pointer over (unit, tile < nt, block) from one over (unit, tile < nt_cap, block)."""
     out = [0]
     for u in range(U):
-        for tile in range(nt):
-            r = u * nt_cap + tile
+        for r in range(2 * u * nt_cap, 2 * (u * nt_cap + nt)):
             out.append(out[-1] + rp[r + 1] - rp[r])
     return np.array(out, dtype=np.int32)
 

@@ -49,12 +49,12 @@ def test_kv_cache_container_bytes():
     packed = {"q_idx": torch.zeros(2, 3, 2048, dtype=torch.uint8),
               "outlier_values": torch.zeros(10, dtype=torch.float16),
               "outlier_cols": torch.zeros(10, dtype=torch.int16),
-              "outlier_rowptr": torch.zeros(7, dtype=torch.int32),
+              "outlier_rowptr": torch.zeros(13, dtype=torch.int32),
               "scale": torch.zeros(256), "zero": torch.zeros(256), "sink": None, "length": 70}
     c.append_k(1, packed)
     c.append_v(0, packed)
     assert c.k_cache[0] is None and c.seq_len == 70
-    assert c.memory_bytes() == 2 * (2 * 3 * 2048 + 20 + 20 + 28 + 2048)
+    assert c.memory_bytes() == 2 * (2 * 3 * 2048 + 20 + 20 + 52 + 2048)
     c.clear()
     assert c.memory_bytes() == 0
 

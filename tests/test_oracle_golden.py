@@ -145,8 +145,19 @@ def test_pack_codes_layout_spot():
     idx[0, tok, p] = 7
     idx[0, tok, p + 64] = 9
     packed = O.pack_codes(idx, 4, "k")
-    off = (blk * 32 + lane) * 32 + q
+    # slab byte q < 16 sits in the block's first region: lane * 16 + q
+    off = blk * 1024 + lane * 16 + q
     assert packed[0, 0, off] == 7 | (9 << 4)
+    assert packed.sum() == packed[0, 0, off]
+    # slab byte q >= 16 sits in the second region: 512 + lane * 16 + (q - 16)
+    idx[...] = 0
+    q = 2 * 9 + 0                                     # kb=9, r=0
+    tok, p = 16 * blk + 3, 4 * 9 + 2
+    idx[0, tok, p] = 5
+    idx[0, tok, p + 64] = 12
+    packed = O.pack_codes(idx, 4, "k")
+    off = blk * 1024 + 512 + lane * 16 + (q - 16)
+    assert packed[0, 0, off] == 5 | (12 << 4)
     assert packed.sum() == packed[0, 0, off]
     # values, 2-bit: nibble q of the slab holds channel 16*(q>>2) + g + 8*(q&1)
     # of tokens (t, t+1), t = 16*block + 2c + 8*((q>>1)&1)
@@ -156,7 +167,7 @@ def test_pack_codes_layout_spot():
     idx[0, t, ch] = 2
     idx[0, t + 1, ch] = 3
     packed = O.pack_codes(idx, 2, "v")
-    off = (blk * 32 + lane) * 16 + q // 2
+    off = blk * 512 + lane * 16 + q // 2
     assert packed[0, 0, off] == (2 | (3 << 2)) << (4 * (q & 1))
     assert packed.sum() == packed[0, 0, off]
 
@@ -183,7 +194,16 @@ def test_tile_outliers_round_trip():
     mask = rng.random((4, 70, 128)) < 0.02
     vals = rng.standard_normal((4, 70, 128)).astype(np.float32)
     v, pos, rp = O.tile_outliers(mask, np.where(mask, vals, 0))
-    assert rp[-1] == mask.sum() and rp.shape == (4 * 3 + 1,)
+    assert rp[-1] == mask.sum() and rp.shape == (4 * 3 * 2 + 1,)
+    # row 2*(u*nt + tile) + blk holds tokens 16*blk.. of the tile, in (token, d) order
+    for u in range(4):
+        for tile in range(3):
+            for blk in range(2):
+                r = 2 * (u * 3 + tile) + blk
+                p = pos[rp[r]:rp[r + 1]].astype(np.int64)
+                assert np.all((p >> 11) == blk) and np.all(np.diff(p) > 0)
+                t0 = tile * 32 + 16 * blk
+                assert len(p) == mask[u, t0:t0 + 16].sum()
     dense, m2 = O.untile_outliers(v, pos, rp, 4, 70)
     np.testing.assert_array_equal(m2, mask)
     np.testing.assert_array_equal(dense[mask], vals[mask].astype(np.float16).astype(np.float32))
