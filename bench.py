@@ -167,6 +167,16 @@ def build_cache(wl, layers, h0, hl, dev, log):
     return cache
 
 
+def bench_config(wl, layers, world):
+    """The workload description both arms print (identical for the same run)."""
+    return {"workload": wl.name, "batch": wl.batch, "kv_heads": wl.kv_heads,
+            "q_per_kv": wl.q_per_kv, "tokens": wl.tokens, "layers": layers, "bits": wl.bits,
+            "outlier_ratio": wl.outlier_ratio, "rope_base": wl.rope_base,
+            "sharding": f"kv heads / {world} GPUs",
+            "compute": "fp16 tensor-core MMA on LUT-dequantized codes, fp32 accumulate",
+            "l2": "inputs larger than L2 (each layer's cache is several GB)"}
+
+
 def algorithmic_bytes(wl, pk, pv, hl, T):
     """Bytes each kernel must move per layer (per launch) on this rank."""
     B, G, bits = wl.batch, wl.q_per_kv, wl.bits
@@ -331,13 +341,9 @@ def run_gpu(args):
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic",
-            "config": {"workload": wl.name, "batch": wl.batch, "kv_heads": wl.kv_heads,
-                       "q_per_kv": G, "tokens": T, "layers": layers, "bits": wl.bits,
-                       "outlier_ratio": wl.outlier_ratio, "rope_base": wl.rope_base,
-                       "sharding": f"kv heads / {world} GPUs",
-                       "l2": f"inputs larger than L2 ({step_bytes / world / 1e9:.1f} GB read "
-                             f"per GPU per step)"},
+            "dtype": "f16", "data": "synthetic",
+            "config": bench_config(wl, layers, world),
+            "bytes_read_per_gpu_per_step": step_bytes / world,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
                          "peak_source": peak_src, "unit": "GB/s", "frac": achieved / peak,
                          "traffic": None,
@@ -470,8 +476,7 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": statistics.mean(walls) * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": wl.name, "batch": wl.batch, "kv_heads": wl.kv_heads,
-                   "tokens": wl.tokens, "layers": wl.layers, "bits": wl.bits},
+        "config": bench_config(wl, args.layers or wl.layers, args.gpus),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": min(cores, units), "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

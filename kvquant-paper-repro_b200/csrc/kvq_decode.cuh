@@ -189,15 +189,16 @@ constexpr int kMaxSlots = 32;                        // query heads per group
 constexpr int kKeyStages = 3;                        // units in flight per thread
 constexpr int kBRow = 9;  // B words per (slot, kb): half2(P) x4, half2(Q) x4, zero
 
-// Shared memory of the key kernel: pair LUT; C quads {oa, ob, oa, ob} per
-// (slot, kb, c); B words per (slot, kb); scores [slot][256]; per-slot scale
+// Shared memory of the key kernel: pair LUT; C pairs {oa, ob} per (slot, kb,
+// c) (an 8-byte load: a 16-byte one costs four shared-memory wavefronts even
+// when lanes share the address); B words per (slot, kb); scores [slot][256]; per-slot scale
 // sigma; the item's CSR row pointers per unit; the cp.async ring (per stage
 // and thread: the two 16-byte halves of the lane slab and one entry).
 template <int BITS>
 struct KeySmem {
   static constexpr int kLut = PairLut<BITS>::kBytes;
   static constexpr int kC = kLut;
-  static constexpr int kB = kC + kMaxSlots * 16 * 4 * 16;
+  static constexpr int kB = kC + kMaxSlots * 16 * 4 * 8;
   static constexpr int kSc = kB + kMaxSlots * 16 * kBRow * 4;
   static constexpr int kSigma = kSc + kMaxSlots * kKeyTokens * 4;
   static constexpr int kPtr = kSigma + kMaxSlots * 4;
@@ -228,12 +229,12 @@ __device__ __forceinline__ float half_hi(uint32_t w) {
 }
 
 // Builds the per-slot tables of a group: sigma (power of two >= every |s q|
-// product of the slot), C quads and B words, all divided by sigma.
+// product of the slot), C pairs and B words, all divided by sigma.
 template <int BITS, int G>
 __device__ void key_build_tables(const KeyArgs& a, uint8_t* smem, int u0, int nu) {
   using L = KeySmem<BITS>;
   float* sigma = reinterpret_cast<float*>(smem + L::kSigma);
-  float4* ct = reinterpret_cast<float4*>(smem + L::kC);
+  float2* ct = reinterpret_cast<float2*>(smem + L::kC);
   uint32_t* bt = reinterpret_cast<uint32_t*>(smem + L::kB);
   const int64_t HG = a.H * G;
   for (int s = threadIdx.x; s < kMaxSlots; s += blockDim.x) sigma[s] = 0.f;
@@ -258,7 +259,7 @@ __device__ void key_build_tables(const KeyArgs& a, uint8_t* smem, int u0, int nu
     const float* scl = a.k_scale + h * kHeadDim;
     const float* zer = a.k_zero + h * kHeadDim;
     const float inv = ldexpf(1.f, -pow2_exponent(sigma[s]));
-    if (j < 4) {  // C quad of lane column pair c = j: OX (c < 2) or OY of pairs 4kb+2(c&1)+{0,1}
+    if (j < 4) {  // C pair of lane column pair c = j: OX (c < 2) or OY of pairs 4kb+2(c&1)+{0,1}
       float o[2];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
@@ -267,7 +268,7 @@ __device__ void key_build_tables(const KeyArgs& a, uint8_t* smem, int u0, int nu
         const float z1 = zer[p], z2 = zer[p + 64];
         o[e] = (j < 2 ? (z1 * q1 + z2 * q2) : (z1 * q2 - z2 * q1)) * inv;
       }
-      ct[(s * 16 + kb) * 4 + j] = make_float4(o[0], o[1], o[0], o[1]);
+      ct[(s * 16 + kb) * 4 + j] = make_float2(o[0], o[1]);
     } else {      // B word jj: half2(P1, P2) of pair 4kb+jj (jj < 4), half2(Q1, Q2) of 4kb+jj-4
       const int jj = j - 4;
       uint32_t w = 0u;
@@ -302,7 +303,7 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
   // (g < 4) or Y of pair g - 4; lane (g, c) holds rows 2c, 2c+1 of it.
   const int jl = (g == c) ? c : ((g == c + 4) ? 4 + c : 8);
   const uint8_t* bbase = smem + L::kB + jl * 4;
-  const uint8_t* cbase = smem + L::kC + c * 16;
+  const uint8_t* cbase = smem + L::kC + c * 8;
   PairLut<BITS>::build(smem, a.cb);
 
   const int nt = (int)((a.T + kTileTokens - 1) / kTileTokens);
@@ -380,7 +381,7 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
       const uint32_t ent0 = *reinterpret_cast<const uint32_t*>(st + kKeyThreads * 32 + threadIdx.x * 4);
       const int slot0 = ui * G;
       const uint8_t* brow = bbase + slot0 * (16 * kBRow * 4);
-      const uint8_t* crow = cbase + slot0 * (16 * 64);
+      const uint8_t* crow = cbase + slot0 * (16 * 32);
 
       float accA[G], accB[G];
 #pragma unroll
@@ -392,8 +393,8 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
 #pragma unroll
         for (int gg = 0; gg < G; ++gg) {
           const uint32_t b0 = *reinterpret_cast<const uint32_t*>(brow + (gg * 16 + kb) * (kBRow * 4));
-          const float4 cq = *reinterpret_cast<const float4*>(crow + (gg * 16 + kb) * 64);
-          float d0 = cq.x, d1 = cq.y, d2 = cq.z, d3 = cq.w;
+          const float2 cq = *reinterpret_cast<const float2*>(crow + (gg * 16 + kb) * 32);
+          float d0 = cq.x, d1 = cq.y, d2 = cq.x, d3 = cq.y;
           mma_1688_acc(d0, d1, d2, d3, a0, a1, b0);
           accA[gg] = fmaf(tw[kb][0], d0, fmaf(tw[kb][1], d1, accA[gg]));
           accB[gg] = fmaf(tw[kb][2], d2, fmaf(tw[kb][3], d3, accB[gg]));
@@ -592,12 +593,12 @@ __global__ void row_max_kernel(const float* __restrict__ vs, int64_t T, int64_t 
   }
 }
 
-// Value-kernel shared memory: pair LUT; fp32 outlier + sink accumulators
+// Value-kernel shared memory: pair LUT; fp32 outlier accumulators
 // ([warp][G][128] for G <= 4, else one [G][128]); zero-term sums [G]; the
-// item's tile row pointers; the per-warp cp.async rings. A ring stage of one
-// warp holds one tile: the two blocks' lane slabs (first 16 bytes of every
-// lane, then the rest), (scale, zero) pairs [32], probabilities [G][kPRow],
-// entries [32].
+// warps' fp16 token weights of the current tile; the item's tile row
+// pointers; the per-warp cp.async rings. A ring stage of one warp holds one
+// tile: the two blocks' lane slabs (first 16 bytes of every lane, then the
+// rest), (scale, zero) pairs [32], probabilities [G][kPRow], entries [32].
 template <int BITS, int G>
 struct ValSmem {
   static constexpr bool kWarpAcc = G <= 4;
@@ -605,19 +606,22 @@ struct ValSmem {
   static constexpr int kAcc = kLut;
   static constexpr int kAccFloats = (kWarpAcc ? kValWarps : 1) * G * kHeadDim;
   static constexpr int kZ = kAcc + kAccFloats * 4;
-  static constexpr int kPtr = kZ + 64;
-  static constexpr int kRing = kPtr + (kValMaxTiles + 4) * 4;
+  static constexpr int kW = kZ + 64;  // fp16 token weights [warp][G][32]
+  static constexpr int kPtr = kW + kValWarps * G * 64;
+  // ring and stages on 128-byte boundaries, so that a warp's 512-byte copies
+  // cover whole shared-memory lines
+  static constexpr int kRing = (kPtr + (kValMaxTiles + 4) * 4 + 127) / 128 * 128;
   static constexpr int kBlockSlab = 1024;
   static constexpr int kSZ = 2 * kBlockSlab;
   static constexpr int kP = kSZ + 32 * 8;
-  static constexpr int kPRow = 40;  // floats per probability row (conflict-free float2 reads)
+  static constexpr int kPRow = 32;  // floats per probability row
   static constexpr int kE = kP + G * kPRow * 4;
-  static constexpr int kStage = kE + 32 * 4;
+  static constexpr int kStage = (kE + 32 * 4 + 127) / 128 * 128;
   static constexpr int kFit = (kValSmemLimit - kRing) / (kValWarps * kStage);
   static constexpr int kStages = kFit < 4 ? kFit : 4;
   static constexpr int kBytes = kRing + kStages * kValWarps * kStage;
   static_assert(kStages >= 2, "value ring needs two stages");
-  static_assert(kStage % 16 == 0 && kRing % 16 == 0, "16-byte aligned stages");
+  static_assert(kStage % 128 == 0 && kRing % 128 == 0, "128-byte aligned stages");
   static_assert(kStages * kValWarps * kStage >= kValWarps * G * kHeadDim * 4,
                 "the reduction buffer reuses the ring");
 };
@@ -663,7 +667,10 @@ __global__ void __launch_bounds__(kValThreads, 1)
   float d[8][4];
 #pragma unroll
   for (int mb = 0; mb < 8; ++mb) d[mb][0] = d[mb][1] = d[mb][2] = d[mb][3] = 0.f;
-  float zs = 0.f;
+  float zs[G];
+#pragma unroll
+  for (int hd = 0; hd < G; ++hd) zs[hd] = 0.f;
+  __half* wbuf = reinterpret_cast<__half*>(smem + S::kW) + warp * G * 32;
 
   const int64_t tbytes = kTileTokens * kHeadDim * BITS / 8;
   const uint8_t* src = a.codes + (u * a.nt_cap + ta + warp) * tbytes;
@@ -702,7 +709,6 @@ __global__ void __launch_bounds__(kValThreads, 1)
   };
 
   for (int i = 0; i < S::kStages - 1; ++i) issue(i);
-  const int gq = g < G ? g : 0;
   int rd = 0;
   for (int i = 0; i < my_n; ++i) {
     __syncwarp();  // every lane is done with the stage the next copy overwrites
@@ -713,24 +719,29 @@ __global__ void __launch_bounds__(kValThreads, 1)
     rd = rd == S::kStages - 1 ? 0 : rd + 1;
     const float2* sz = reinterpret_cast<const float2*>(st + S::kSZ);
     const float* fp = reinterpret_cast<const float*>(st + S::kP);
+    // Lane = token of the tile: its weights p * s * 2^e (one per head) go to
+    // the warp's fp16 weight buffer once; its zero-point terms p * z stay in
+    // fp32 registers.
+    {
+      const float2 szl = sz[lane];
+#pragma unroll
+      for (int hd = 0; hd < G; ++hd) {
+        const float p = fp[hd * S::kPRow + lane];
+        zs[hd] = fmaf(p, szl.y, zs[hd]);
+        wbuf[hd * 32 + lane] = __float2half_rn(p * szl.x * e_scale);
+      }
+    }
+    __syncwarp();
 #pragma unroll
     for (int blk = 0; blk < 2; ++blk) {
       LaneSlab<BITS> sl;
       sl.read(st + blk * S::kBlockSlab + lane * 16, st + blk * S::kBlockSlab + 512 + lane * 16);
-      const int t0 = 16 * blk + 2 * c;
-      const float4 sz01 = *reinterpret_cast<const float4*>(sz + t0);      // s, z of t0, t0+1
-      const float4 sz89 = *reinterpret_cast<const float4*>(sz + t0 + 8);  // ... of t0+8, t0+9
-      const float2 p01 = *reinterpret_cast<const float2*>(fp + gq * S::kPRow + t0);
-      const float2 p89 = *reinterpret_cast<const float2*>(fp + gq * S::kPRow + t0 + 8);
-      uint32_t b0 = half2_bits(p01.x * sz01.x * e_scale, p01.y * sz01.z * e_scale);
-      uint32_t b1 = half2_bits(p89.x * sz89.x * e_scale, p89.y * sz89.z * e_scale);
+      // B fragment of head g: weights of tokens 2c, 2c+1 (b0) and 2c+8, 2c+9 (b1)
+      uint32_t b0 = 0u, b1 = 0u;
       if (g < G) {
-        zs = fmaf(p01.x, sz01.y, zs);
-        zs = fmaf(p01.y, sz01.w, zs);
-        zs = fmaf(p89.x, sz89.y, zs);
-        zs = fmaf(p89.y, sz89.w, zs);
-      } else {
-        b0 = b1 = 0u;
+        const __half* wg = wbuf + g * 32 + 16 * blk + 2 * c;
+        b0 = *reinterpret_cast<const uint32_t*>(wg);
+        b1 = *reinterpret_cast<const uint32_t*>(wg + 8);
       }
 #pragma unroll
       for (int mb = 0; mb < 8; ++mb) {
@@ -757,9 +768,11 @@ __global__ void __launch_bounds__(kValThreads, 1)
     }
   }
   cp_async_wait<0>();
-  zs += __shfl_xor_sync(0xffffffffu, zs, 1);
-  zs += __shfl_xor_sync(0xffffffffu, zs, 2);
-  if (c == 0 && g < G) atomicAdd(zacc + g, zs);
+#pragma unroll
+  for (int hd = 0; hd < G; ++hd) {
+    const float z = warp_sum(zs[hd]);
+    if (lane == 0) atomicAdd(zacc + hd, z);
+  }
   // Sink (token 0, in the first split): p_0 * v_sink, fp32.
   if (sink && ta == 0) {
     for (int idx = threadIdx.x; idx < G * kHeadDim; idx += blockDim.x) {
@@ -815,10 +828,11 @@ __global__ void value_combine_kernel(const float* __restrict__ partial, int n_sp
 }
 
 // Splits of each unit's tiles into value work items. The value kernel runs
-// one 16-warp CTA per SM, so the items run in waves of kValSlots; the split
-// count minimises waves x (tile rounds per warp + a pipeline fill of two
-// rounds), subject to at most kValMaxTiles tiles per item. Host-only and
-// independent of the device, so the workspace size is known up front.
+// one 16-warp CTA per SM (16 tiles in flight), so the items run in waves of
+// kValSlots; the split count minimises waves x (tile rounds per warp + a
+// pipeline fill of two rounds), subject to at most kValMaxTiles tiles per
+// item. Host-only and independent of the device, so the workspace size is
+// known up front.
 constexpr int kValSlots = 148;  // B200 SMs
 inline int value_splits(int64_t U, int64_t nt, int64_t /*G*/) {
   if (U < 1 || nt < 1) return 1;
