@@ -577,19 +577,23 @@ constexpr int kValMaxTiles = 2048;     // tiles per work item (row pointers sit 
 constexpr int kValSmemLimit = 232448;  // opt-in shared memory per CTA (227 KB)
 
 // max_t v_scale[b, t] for each batch row (bounds every weight p_t * s_t).
-__global__ void row_max_kernel(const float* __restrict__ vs, int64_t T, int64_t ld,
-                               float* __restrict__ out) {
-  __shared__ float red[32];
-  const int64_t b = blockIdx.x;
+// grid = (chunks of the token axis, B); out[b] starts at 0 and takes the
+// maximum by an integer atomicMax on the float bits (scales are >= 0).
+constexpr int kRowMaxChunk = 16384;
+__global__ void __launch_bounds__(256) row_max_kernel(const float* __restrict__ vs, int64_t T,
+                                                      int64_t ld, float* __restrict__ out) {
+  __shared__ float red[8];
+  const int64_t b = blockIdx.y;
+  const int64_t s0 = (int64_t)blockIdx.x * kRowMaxChunk, s1 = min(T, s0 + kRowMaxChunk);
   float m = 0.f;
-  for (int64_t t = threadIdx.x; t < T; t += blockDim.x) m = fmaxf(m, vs[b * ld + t]);
+  for (int64_t t = s0 + threadIdx.x; t < s1; t += blockDim.x) m = fmaxf(m, vs[b * ld + t]);
   m = warp_max(m);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
   __syncthreads();
   if (threadIdx.x < 32) {
     m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
     m = warp_max(m);
-    if (threadIdx.x == 0) out[b] = m;
+    if (threadIdx.x == 0) atomicMax(reinterpret_cast<int*>(out + b), __float_as_int(m));
   }
 }
 
@@ -913,7 +917,7 @@ static int dispatch_value_bits(int bits, const ValueArgs& a, const float* row_ma
 
 static int check_decode_shape(const char* what, int64_t B, int64_t H, int64_t G, int64_t T,
                               int64_t nt_cap) {
-  if (B < 1 || H < 1 || T < 1 || nt_cap * kTileTokens < T) {
+  if (B < 1 || B > 65535 || H < 1 || T < 1 || nt_cap * kTileTokens < T) {
     set_error("%s: invalid shape B=%lld H=%lld T=%lld nt_cap=%lld", what, (long long)B,
               (long long)H, (long long)T, (long long)nt_cap);
     return KVQ_ERR_INVALID;
@@ -992,7 +996,9 @@ static int value_impl(const uint8_t* codes, const uint32_t* out_ent, const int32
   a.n_splits = n_splits;
   a.partial = reinterpret_cast<float*>(workspace);
   float* row_max = reinterpret_cast<float*>((char*)workspace + part_bytes);
-  row_max_kernel<<<(unsigned)B, 256, 0, st>>>(v_scale, T, ld_stats, row_max);
+  cudaMemsetAsync(row_max, 0, (size_t)B * sizeof(float), st);
+  row_max_kernel<<<dim3((unsigned)((T + kRowMaxChunk - 1) / kRowMaxChunk), (unsigned)B), 256, 0, st>>>(
+      v_scale, T, ld_stats, row_max);
   switch (G) {
     case 1: rc = dispatch_value_bits<1>(bits, a, row_max, st); break;
     case 2: rc = dispatch_value_bits<2>(bits, a, row_max, st); break;
