@@ -147,14 +147,16 @@ struct LaneSlab {
 // Key kernel (tensor cores as the dot-product engine).
 //
 // Per 16-token block, pair block kb (4 RoPE pairs) and query head, one
-// m16n8k8 MMA computes, for the 16 tokens,
+// m16n8k16 MMA computes, for the 16 tokens,
 //   X_p = L1 P1 + L2 P2 + OX   (columns 0..3, pairs 4kb..4kb+3)
 //   Y_p = L1 Q1 + L2 Q2 + OY   (columns 4..7)
-// with A = the fp16 code values straight from the LUT (rows = tokens, k = the
-// two halves of each pair), B = the block-diagonal per-head constants and C =
-// the zero-point terms, loaded straight into the accumulator registers. The
-// epilogue adds cos * X + sin * Y in fp32 with the token's exact-angle cos/sin
-// held in registers. Outliers add o * (cos P + sin Q) per entry with exact
+// with A columns 0..7 = the fp16 code values straight from the LUT (rows =
+// tokens, the two halves of each pair), B rows 0..7 = the block-diagonal
+// per-head constants, and the zero-point terms OX / OY entering as A columns
+// 8, 9 = 256 times B rows 8, 9 = the terms / 256 split into fp16 high and low
+// parts (exact to ~2^-22 relative), so the MMA needs no accumulator input.
+// The epilogue adds cos * X + sin * Y in fp32 with the token's exact-angle
+// cos/sin held in registers. Outliers add o * (cos P + sin Q) per entry with exact
 // trig; a block's entries (ordered by token) are summed per token with a warp
 // segmented scan, so every score has exactly one writer and no shared-memory
 // float atomics are needed.
@@ -188,37 +190,40 @@ constexpr int kKeyRows = 2 * kKeyTiles;              // CSR rows per unit and it
 constexpr int kMaxSlots = 32;                        // query heads per group
 constexpr int kKeyStages = 3;                        // units in flight per thread
 constexpr int kBRow = 9;  // B words per (slot, kb): half2(P) x4, half2(Q) x4, zero
+constexpr int kZRow = 8;  // zero-point words per (slot, kb): half2(hi, lo) of column n's term / 256
+constexpr uint32_t kA256 = 0x5C005C00u;  // half2(256, 256)
 
-// Shared memory of the key kernel: pair LUT; C pairs {oa, ob} per (slot, kb,
-// c) (an 8-byte load: a 16-byte one costs four shared-memory wavefronts even
-// when lanes share the address); B words per (slot, kb); scores [slot][256]; per-slot scale
-// sigma; the item's CSR row pointers per unit; the cp.async ring (per stage
-// and thread: the two 16-byte halves of the lane slab and one entry).
+// Shared memory of the key kernel: pair LUT; zero-point words per (slot, kb,
+// column); B words per (slot, kb); scores [slot][256]; per-slot scale sigma;
+// RoPE inverse frequencies [64]; the item's CSR row pointers per unit; the
+// cp.async ring (per stage and thread: the two 16-byte halves of the lane
+// slab and one entry).
 template <int BITS>
 struct KeySmem {
   static constexpr int kLut = PairLut<BITS>::kBytes;
-  static constexpr int kC = kLut;
-  static constexpr int kB = kC + kMaxSlots * 16 * 4 * 8;
+  static constexpr int kZ = kLut;
+  static constexpr int kB = kZ + kMaxSlots * 16 * kZRow * 4;
   static constexpr int kSc = kB + kMaxSlots * 16 * kBRow * 4;
   static constexpr int kSigma = kSc + kMaxSlots * kKeyTokens * 4;
-  static constexpr int kPtr = kSigma + kMaxSlots * 4;
+  static constexpr int kInv = kSigma + kMaxSlots * 4;
+  static constexpr int kPtr = kInv + kPairs * 4;
   static constexpr int kRing = (kPtr + kMaxSlots * (kKeyRows + 1) * 4 + 15) / 16 * 16;
   static constexpr int kStage = kKeyThreads * (16 + 16 + 4);
   static constexpr int kBytes = kRing + kKeyStages * kStage;
-  static_assert(kC % 16 == 0 && kBytes <= 232448, "key kernel shared memory");
+  static_assert(kBytes <= 232448, "key kernel shared memory");
 };
 
 template <int BITS>
 __host__ __device__ constexpr int key_smem_bytes() { return KeySmem<BITS>::kBytes; }
 
-// m16n8k8, fp16 inputs, fp32 accumulator d (= C on entry).
-__device__ __forceinline__ void mma_1688_acc(float& d0, float& d1, float& d2, float& d3,
-                                             uint32_t a0, uint32_t a1, uint32_t b0) {
+// m16n8k16, fp16 inputs, fp32 result with a zero accumulator input.
+__device__ __forceinline__ void mma_16816_zc(float (&d)[4], uint32_t a0, uint32_t a1,
+                                             uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
   asm volatile(
-      "mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d0), "+f"(d1), "+f"(d2), "+f"(d3)
-      : "r"(a0), "r"(a1), "r"(b0));
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
 }
 
 __device__ __forceinline__ float half_lo(uint32_t w) {
@@ -229,12 +234,12 @@ __device__ __forceinline__ float half_hi(uint32_t w) {
 }
 
 // Builds the per-slot tables of a group: sigma (power of two >= every |s q|
-// product of the slot), C pairs and B words, all divided by sigma.
+// product of the slot), zero-point words and B words, all divided by sigma.
 template <int BITS, int G>
 __device__ void key_build_tables(const KeyArgs& a, uint8_t* smem, int u0, int nu) {
   using L = KeySmem<BITS>;
   float* sigma = reinterpret_cast<float*>(smem + L::kSigma);
-  float2* ct = reinterpret_cast<float2*>(smem + L::kC);
+  uint32_t* zt = reinterpret_cast<uint32_t*>(smem + L::kZ);
   uint32_t* bt = reinterpret_cast<uint32_t*>(smem + L::kB);
   const int64_t HG = a.H * G;
   for (int s = threadIdx.x; s < kMaxSlots; s += blockDim.x) sigma[s] = 0.f;
@@ -250,27 +255,25 @@ __device__ void key_build_tables(const KeyArgs& a, uint8_t* smem, int u0, int nu
     atomicMax(reinterpret_cast<int*>(sigma + s), __float_as_int(m));
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < nu * G * 16 * (4 + kBRow); idx += blockDim.x) {
-    const int s = idx / (16 * (4 + kBRow)), r = idx % (16 * (4 + kBRow));
-    const int kb = r / (4 + kBRow), j = r % (4 + kBRow);
+  for (int idx = threadIdx.x; idx < nu * G * 16 * (kZRow + kBRow); idx += blockDim.x) {
+    const int s = idx / (16 * (kZRow + kBRow)), r = idx % (16 * (kZRow + kBRow));
+    const int kb = r / (kZRow + kBRow), j = r % (kZRow + kBRow);
     const int64_t u = u0 + s / G;
     const int64_t b = u / a.H, h = u % a.H;
     const __half* qv = a.q + (b * HG + h * G + s % G) * kHeadDim;
     const float* scl = a.k_scale + h * kHeadDim;
     const float* zer = a.k_zero + h * kHeadDim;
     const float inv = ldexpf(1.f, -pow2_exponent(sigma[s]));
-    if (j < 4) {  // C pair of lane column pair c = j: OX (c < 2) or OY of pairs 4kb+2(c&1)+{0,1}
-      float o[2];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int p = 4 * kb + 2 * (j & 1) + e;
-        const float q1 = __half2float(qv[p]), q2 = __half2float(qv[p + 64]);
-        const float z1 = zer[p], z2 = zer[p + 64];
-        o[e] = (j < 2 ? (z1 * q1 + z2 * q2) : (z1 * q2 - z2 * q1)) * inv;
-      }
-      ct[(s * 16 + kb) * 4 + j] = make_float2(o[0], o[1]);
+    if (j < kZRow) {  // zero-point word of column j: OX (j < 4) or OY of pair 4kb + (j & 3)
+      const int p = 4 * kb + (j & 3);
+      const float q1 = __half2float(qv[p]), q2 = __half2float(qv[p + 64]);
+      const float z1 = zer[p], z2 = zer[p + 64];
+      const float zt256 = (j < 4 ? (z1 * q1 + z2 * q2) : (z1 * q2 - z2 * q1)) * inv * (1.f / 256.f);
+      const __half hi = __float2half_rn(zt256);
+      const __half lo = __float2half_rn(zt256 - __half2float(hi));
+      zt[(s * 16 + kb) * kZRow + j] = (uint32_t)__half_as_ushort(hi) | ((uint32_t)__half_as_ushort(lo) << 16);
     } else {      // B word jj: half2(P1, P2) of pair 4kb+jj (jj < 4), half2(Q1, Q2) of 4kb+jj-4
-      const int jj = j - 4;
+      const int jj = j - kZRow;
       uint32_t w = 0u;
       if (jj < 8) {
         const int p = 4 * kb + (jj & 3);
@@ -303,8 +306,12 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
   // (g < 4) or Y of pair g - 4; lane (g, c) holds rows 2c, 2c+1 of it.
   const int jl = (g == c) ? c : ((g == c + 4) ? 4 + c : 8);
   const uint8_t* bbase = smem + L::kB + jl * 4;
-  const uint8_t* cbase = smem + L::kC + c * 8;
+  const uint8_t* zbase = smem + L::kZ + g * 4;  // zero-point word of column g
+  // A columns 8, 9 = 256 (lanes c == 0 hold them), columns 10..15 = 0
+  const uint32_t a23 = c == 0 ? kA256 : 0u;
+  float* invf = reinterpret_cast<float*>(smem + L::kInv);
   PairLut<BITS>::build(smem, a.cb);
+  if (threadIdx.x < kPairs) invf[threadIdx.x] = a.inv_freq[threadIdx.x];
 
   const int nt = (int)((a.T + kTileTokens - 1) / kTileTokens);
   const int n_oct = (nt + kKeyTiles - 1) / kKeyTiles;
@@ -358,15 +365,16 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
     // cos (c < 2) or sin (c >= 2) of tokens g, g + 8 of this warp's block for
     // pairs 4kb + 2(c & 1) + {0, 1}.
     const int tok0 = tile0 * kTileTokens + 16 * warp;  // first token of the block
+    const float phase = c < 2 ? 0.f : 1.5707963267948966f;  // cos (c < 2) or sin
     float tw[16][4];
 #pragma unroll
     for (int kb = 0; kb < 16; ++kb) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const float f = __ldg(a.inv_freq + 4 * kb + 2 * (c & 1) + e);
-        const float rA = rope_reduce(tok0 + g, f), rB = rope_reduce(tok0 + g + 8, f);
-        tw[kb][e] = c < 2 ? __cosf(rA) : __sinf(rA);
-        tw[kb][2 + e] = c < 2 ? __cosf(rB) : __sinf(rB);
+        const float f = invf[4 * kb + 2 * (c & 1) + e];
+        // sin r = cos(r - pi/2): one hardware cosine per value
+        tw[kb][e] = __cosf(rope_reduce(tok0 + g, f) - phase);
+        tw[kb][2 + e] = __cosf(rope_reduce(tok0 + g + 8, f) - phase);
       }
     }
 
@@ -381,7 +389,7 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
       const uint32_t ent0 = *reinterpret_cast<const uint32_t*>(st + kKeyThreads * 32 + threadIdx.x * 4);
       const int slot0 = ui * G;
       const uint8_t* brow = bbase + slot0 * (16 * kBRow * 4);
-      const uint8_t* crow = cbase + slot0 * (16 * 32);
+      const uint8_t* zrow = zbase + slot0 * (16 * kZRow * 4);
 
       float accA[G], accB[G];
 #pragma unroll
@@ -393,11 +401,11 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
 #pragma unroll
         for (int gg = 0; gg < G; ++gg) {
           const uint32_t b0 = *reinterpret_cast<const uint32_t*>(brow + (gg * 16 + kb) * (kBRow * 4));
-          const float2 cq = *reinterpret_cast<const float2*>(crow + (gg * 16 + kb) * 32);
-          float d0 = cq.x, d1 = cq.y, d2 = cq.x, d3 = cq.y;
-          mma_1688_acc(d0, d1, d2, d3, a0, a1, b0);
-          accA[gg] = fmaf(tw[kb][0], d0, fmaf(tw[kb][1], d1, accA[gg]));
-          accB[gg] = fmaf(tw[kb][2], d2, fmaf(tw[kb][3], d3, accB[gg]));
+          const uint32_t b1 = *reinterpret_cast<const uint32_t*>(zrow + (gg * 16 + kb) * (kZRow * 4));
+          float d[4];
+          mma_16816_zc(d, a0, a1, a23, a23, b0, b1);
+          accA[gg] = fmaf(tw[kb][0], d[0], fmaf(tw[kb][1], d[1], accA[gg]));
+          accB[gg] = fmaf(tw[kb][2], d[2], fmaf(tw[kb][3], d[3], accB[gg]));
         }
       }
 #pragma unroll
@@ -423,7 +431,7 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
           const int tok = valid ? (int)((en >> 7) & 15) : 16 + lane;  // token within the block
           const int ch = (int)(en & 127), p = ch & 63;
           float sv, cv;
-          __sincosf(rope_reduce(tok0 + (tok & 15), __ldg(a.inv_freq + p)), &sv, &cv);
+          __sincosf(rope_reduce(tok0 + (tok & 15), invf[p]), &sv, &cv);
           const float ov = valid ? entry_value(en) : 0.f;
           // entries are ordered by token: suffix sums within runs of equal tokens
           int tn[5];
