@@ -167,6 +167,13 @@ def build_cache(wl, layers, h0, hl, dev, log):
     return cache
 
 
+# DRAM bytes (ncu dram__bytes_read.sum + dram__bytes_write.sum) per algorithmic
+# byte of each decode kernel, from one capture of the 4-bit 1%-outlier workload
+# at 262144 tokens x 32 KV heads (traffic grows in proportion to the tokens).
+DRAM_PER_ALGORITHMIC_BYTE = {"key_scores": 617608960 / 615514116,
+                             "value_output": 622571776 / 608190336}
+
+
 def bench_config(wl, layers, world):
     """The workload description both arms print (identical for the same run)."""
     return {"workload": wl.name, "batch": wl.batch, "kv_heads": wl.kv_heads,
@@ -224,7 +231,7 @@ def run_gpu(args):
     full = [torch.empty((world, wl.batch, Hq_l, 128), dtype=torch.float16, device=dev)
             for _ in range(layers)] if world > 1 else None
     stream = torch.cuda.current_stream(dev)
-    n_launch_per_layer = 5  # key, softmax x2, value, combine
+    n_launch_per_layer = 6  # key, softmax x2, value row max, value, combine
 
     def step(events=None):
         handles = []
@@ -346,7 +353,7 @@ def run_gpu(args):
             "bytes_read_per_gpu_per_step": step_bytes / world,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
                          "peak_source": peak_src, "unit": "GB/s", "frac": achieved / peak,
-                         "traffic": None,
+                         "traffic": ab[dom] * DRAM_PER_ALGORITHMIC_BYTE[dom],
                          "bytes_per_launch": ab[dom], "launch_ms": dom_ms},
             "step_bandwidth_gbs": step_bytes / (ms_step / 1e3) / 1e9,
             "kernels_ms": {"key_scores": k_avg, "softmax": s_avg, "value_output": v_avg},
