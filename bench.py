@@ -212,10 +212,11 @@ def run_gpu(args):
         import dataclasses
         wl = dataclasses.replace(wl, tokens=args.tokens, name=f"{wl.name}@{args.tokens}tok")
     layers = args.layers or wl.layers
-    if wl.kv_heads % world:
-        raise SystemExit(f"{wl.kv_heads} KV heads do not split over {world} GPUs")
-    hl = wl.kv_heads // world
-    h0 = rank * hl
+    from kvquant.sharding import shard_heads, gather_buffer, gather_head_outputs
+    try:
+        h0, hl = shard_heads(wl.kv_heads, world, rank)
+    except ValueError as e:
+        raise SystemExit(str(e))
     G = wl.q_per_kv
     T = wl.tokens
     log = (lambda m: print(f"[rank {rank}] {m}", file=sys.stderr, flush=True))
@@ -228,8 +229,7 @@ def run_gpu(args):
     scores = torch.empty((wl.batch, Hq_l, T), dtype=torch.float32, device=dev)
     outs = [torch.empty((wl.batch, Hq_l, 128), dtype=torch.float16, device=dev)
             for _ in range(layers)]
-    full = [torch.empty((world, wl.batch, Hq_l, 128), dtype=torch.float16, device=dev)
-            for _ in range(layers)] if world > 1 else None
+    full = [gather_buffer(outs[l], world) for l in range(layers)] if world > 1 else None
     stream = torch.cuda.current_stream(dev)
     n_launch_per_layer = 6  # key, softmax x2, value row max, value, combine
 
@@ -248,7 +248,7 @@ def run_gpu(args):
             if events is not None:
                 events[l][3].record(stream)
             if world > 1:
-                handles.append(dist.all_gather_into_tensor(full[l], outs[l], async_op=True))
+                handles.append(gather_head_outputs(outs[l], full[l], async_op=True))
         for h in handles:
             h.wait()
 
@@ -291,7 +291,7 @@ def run_gpu(args):
     e2e = None
     if not args.no_e2e:
         q_host = [q.cpu().pin_memory() for q in qs]
-        o_host = [torch.empty((world, wl.batch, Hq_l, 128), dtype=torch.float16).pin_memory()
+        o_host = [torch.empty((world * wl.batch, Hq_l, 128), dtype=torch.float16).pin_memory()
                   for _ in range(layers)]
         q_dev = [torch.empty_like(q) for q in qs]
         wsp = DecodeWorkspace()
@@ -302,9 +302,9 @@ def run_gpu(args):
                 q_dev[l].copy_(q_host[l], non_blocking=True)
                 o = decode_attention(q_dev[l], pk, pv, inv, workspace=wsp)
                 if world > 1:
-                    handles.append((l, dist.all_gather_into_tensor(full[l], o, async_op=True)))
+                    handles.append((l, gather_head_outputs(o, full[l], async_op=True)))
                 else:
-                    o_host[l][0].copy_(o, non_blocking=True)
+                    o_host[l].copy_(o, non_blocking=True)
             for l, h in handles:
                 h.wait()
                 o_host[l].copy_(full[l], non_blocking=True)
