@@ -343,7 +343,7 @@ def run_gpu(args):
     if rank == 0:
         cpu = None
         if not args.no_cpu_baseline and world == 1:
-            cpu = cpu_baseline(wl, dev, log)
+            cpu = cpu_baseline(wl, log)
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
@@ -384,43 +384,50 @@ def _cpu_unit(args):
     return time.perf_counter() - t0
 
 
-def make_cpu_sample(wl, dev, units: int, T: int):
-    """Packed cache of `units` KV heads (one layer, T tokens) copied to host arrays."""
-    import numpy as np
-    import torch
-    from kvquant import synthetic as syn
-    from kvquant.kernels import quantize_keys, quantize_values, rope_inv_freq
+def make_cpu_sample(wl, units: int, T: int):
+    """Packed cache of `units` KV heads (one layer, T tokens) built on the CPU.
 
-    C = wl.channels
-    k = torch.empty((1, T, C), dtype=torch.float16, device=dev)
-    v = torch.empty((1, T, C), dtype=torch.float16, device=dev)
-    syn.fill_layer(k, v, 0, seed=0)
-    ks, kz = syn.key_calibration(k)
-    cbk, cbv = syn.fit_codebooks(k, v, ks, kz, wl.bits)
-    pk = quantize_keys(k, ks, kz, cbk, wl.bits, wl.outlier_ratio, True, n_heads=units)
-    pv = quantize_values(v, cbv, wl.bits, wl.outlier_ratio, True, n_heads=units)
-    q = syn.make_query(1, wl.kv_heads * wl.q_per_kv, 0, 0, dev)[0, :units].cpu().numpy()
-    inv = rope_inv_freq(128, wl.rope_base).numpy()
+    Seeded synthetic K/V with the workload's distributions, quantized by the
+    oracle's restatement of KVQuantizer.quantize_k / quantize_v and packed into
+    the cache layout (nothing of the GPU path is involved). The codebooks are a
+    uniform grid on [-1, 1]: the timed CPU decode does not depend on their values.
+    """
+    import numpy as np
+    from oracle import kvq_oracle as O
+
+    rng = np.random.default_rng(1234)
+    C = units * 128
+    ch_scale = np.exp(rng.uniform(np.log(0.1), np.log(10.0), size=C)).astype(np.float32)
+    k = rng.standard_normal((1, T, C), dtype=np.float32) * ch_scale
+    v = rng.standard_normal((1, T, C), dtype=np.float32)
+    for x in (k, v):
+        x[rng.random(x.shape) < 0.01] *= 20.0
+    k, v = k.astype(np.float16), v.astype(np.float16)
+    kr = k[:, 1:].astype(np.float32).reshape(-1, C)
+    kmin, kmax = kr.min(axis=0), kr.max(axis=0)
+    scale = ((kmax - kmin) / np.float32(2)).astype(np.float32)
+    zero = ((kmax + kmin) / np.float32(2)).astype(np.float32)
+    cb = np.linspace(-1, 1, 1 << wl.bits).astype(np.float32)
+    kq = O.quantize_k(k, cb, scale, zero, wl.outlier_ratio, True)
+    vq = O.quantize_v(v, cb, wl.outlier_ratio, True)
+    packed = O.cache_from_reference_quant(kq, vq, k, v, units, wl.bits)
+    q = rng.standard_normal((units, 128), dtype=np.float32).astype(np.float16)
+    inv = O.rope_inv_freq(128, wl.rope_base)
+    vs = np.concatenate([[0.0], vq["scale"][0]]).astype(np.float32)[None]
+    vz = np.concatenate([[0.0], vq["zero"][0]]).astype(np.float32)[None]
     nt = -(-T // 32)
-    h = lambda x: x.cpu().numpy()  # noqa: E731
     tasks = []
-    kr_all, vr_all = h(pk["outlier_rowptr"]), h(pv["outlier_rowptr"])
-    ke_all, ve_all = h(pk["outlier_entries"]).view(np.uint32), h(pv["outlier_entries"]).view(np.uint32)
     for u in range(units):
         def seg(rp, ent):
-            a, b = int(rp[2 * u * nt]), int(rp[2 * (u + 1) * nt])
-            r = (rp[2 * u * nt:2 * (u + 1) * nt + 1] - a).astype(np.int32)
-            return ent[a:b], r
-        kent, krp = seg(kr_all, ke_all)
-        vent, vrp = seg(vr_all, ve_all)
-        tasks.append((h(pk["q_idx"][u:u + 1]), kent, krp,
-                      h(pk["scale"])[u * 128:(u + 1) * 128][None], h(pk["zero"])[u * 128:(u + 1) * 128][None],
-                      h(pk["codebook"]), h(pk["sink"])[0:1, u * 128:(u + 1) * 128],
-                      h(pv["q_idx"][u:u + 1]), vent, vrp, h(pv["scale"]), h(pv["zero"]),
-                      h(pv["codebook"]), h(pv["sink"])[0:1, u * 128:(u + 1) * 128],
-                      q[u:u + 1], inv, wl.bits, T))
-    del k, v
-    torch.cuda.empty_cache()
+            lo, hi = int(rp[2 * u * nt]), int(rp[2 * (u + 1) * nt])
+            r = (rp[2 * u * nt:2 * (u + 1) * nt + 1] - lo).astype(np.int32)
+            return ent[lo:hi], r
+        kent, krp = seg(packed["k_out_ptr"], packed["k_out_ent"])
+        vent, vrp = seg(packed["v_out_ptr"], packed["v_out_ent"])
+        cs = slice(u * 128, (u + 1) * 128)
+        tasks.append((packed["k_codes"][u:u + 1], kent, krp, scale[cs][None], zero[cs][None], cb,
+                      packed["k_sink"][0:1, cs], packed["v_codes"][u:u + 1], vent, vrp, vs, vz, cb,
+                      packed["v_sink"][0:1, cs], q[u:u + 1], inv, wl.bits, T))
     return tasks
 
 
@@ -439,11 +446,11 @@ def cpu_measure(tasks, pool, wl):
     return (T * units / wl.kv_heads) / wall, wall
 
 
-def cpu_baseline(wl, dev, log):
+def cpu_baseline(wl, log):
     cores = os.cpu_count() or 1
     units = min(wl.kv_heads, max(2, cores))
     T = min(wl.tokens, 1 << 16)
-    tasks = make_cpu_sample(wl, dev, units, T)
+    tasks = make_cpu_sample(wl, units, T)
     with _pool(min(cores, units)) as pool:
         cpu_measure(tasks[:1], pool, wl)  # warm the workers
         val, wall = cpu_measure(tasks, pool, wl)
@@ -457,16 +464,14 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import torch
     from kvquant import synthetic as syn
 
     wl = syn.WORKLOADS[args.workload]
     cores = os.cpu_count() or 1
     units = min(wl.kv_heads, max(2, cores))
     T = min(wl.tokens, 1 << 15)
-    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
-    with _pool(min(cores, units)) as pool:  # started before the first GPU call
-        tasks = make_cpu_sample(wl, dev, units, T)
+    with _pool(min(cores, units)) as pool:
+        tasks = make_cpu_sample(wl, units, T)
         for _ in range(args.warmup):
             cpu_measure(tasks, pool, wl)
         vals, walls = [], []
