@@ -350,7 +350,7 @@ def run_gpu(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f16", "data": "synthetic",
             "config": bench_config(wl, layers, world),
-            "bytes_read_per_gpu_per_step": step_bytes / world,
+            "bytes_read_per_gpu_per_step": step_bytes,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
                          "peak_source": peak_src, "unit": "GB/s", "frac": achieved / peak,
                          "traffic": ab[dom] * DRAM_PER_ALGORITHMIC_BYTE[dom],
