@@ -226,6 +226,22 @@ __device__ __forceinline__ void mma_16816_zc(float (&d)[4], uint32_t a0, uint32_
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
 }
 
+// Packed fp32 pairs (one 64-bit register pair) and the sm_100 paired FMA,
+// which issues once for two fp32 FMAs.
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float f2sum(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return lo + hi;
+}
+__device__ __forceinline__ void ffma2(uint64_t& acc, uint64_t a, uint64_t b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
+}
+
 __device__ __forceinline__ float half_lo(uint32_t w) {
   return __half2float(__ushort_as_half((unsigned short)(w & 0xffffu)));
 }
@@ -366,16 +382,20 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
     // pairs 4kb + 2(c & 1) + {0, 1}.
     const int tok0 = tile0 * kTileTokens + 16 * warp;  // first token of the block
     const float phase = c < 2 ? 0.f : 1.5707963267948966f;  // cos (c < 2) or sin
-    float tw[16][4];
+    // tw[kb][0] = the pair (e = 0, 1) for token g, tw[kb][1] for token g + 8
+    uint64_t tw[16][2];
 #pragma unroll
     for (int kb = 0; kb < 16; ++kb) {
+      float v[4];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const float f = invf[4 * kb + 2 * (c & 1) + e];
         // sin r = cos(r - pi/2): one hardware cosine per value
-        tw[kb][e] = __cosf(rope_reduce(tok0 + g, f) - phase);
-        tw[kb][2 + e] = __cosf(rope_reduce(tok0 + g + 8, f) - phase);
+        v[e] = __cosf(rope_reduce(tok0 + g, f) - phase);
+        v[2 + e] = __cosf(rope_reduce(tok0 + g + 8, f) - phase);
       }
+      tw[kb][0] = f2pack(v[0], v[1]);
+      tw[kb][1] = f2pack(v[2], v[3]);
     }
 
     int rd_stage = 0;
@@ -391,9 +411,9 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
       const uint8_t* brow = bbase + slot0 * (16 * kBRow * 4);
       const uint8_t* zrow = zbase + slot0 * (16 * kZRow * 4);
 
-      float accA[G], accB[G];
+      uint64_t accA[G], accB[G];  // pairs of partial sums, token g / g + 8
 #pragma unroll
-      for (int gg = 0; gg < G; ++gg) accA[gg] = accB[gg] = 0.f;
+      for (int gg = 0; gg < G; ++gg) accA[gg] = accB[gg] = 0ull;
 #pragma unroll
       for (int kb = 0; kb < 16; ++kb) {
         const uint32_t a0 = *reinterpret_cast<const uint32_t*>(lut + sl.addr(2 * kb, lane4));
@@ -404,13 +424,13 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
           const uint32_t b1 = *reinterpret_cast<const uint32_t*>(zrow + (gg * 16 + kb) * (kZRow * 4));
           float d[4];
           mma_16816_zc(d, a0, a1, a23, a23, b0, b1);
-          accA[gg] = fmaf(tw[kb][0], d[0], fmaf(tw[kb][1], d[1], accA[gg]));
-          accB[gg] = fmaf(tw[kb][2], d[2], fmaf(tw[kb][3], d[3], accB[gg]));
+          ffma2(accA[gg], tw[kb][0], f2pack(d[0], d[1]));
+          ffma2(accB[gg], tw[kb][1], f2pack(d[2], d[3]));
         }
       }
 #pragma unroll
       for (int gg = 0; gg < G; ++gg) {
-        float x = accA[gg], y = accB[gg];
+        float x = f2sum(accA[gg]), y = f2sum(accB[gg]);
         x += __shfl_xor_sync(0xffffffffu, x, 1);
         y += __shfl_xor_sync(0xffffffffu, y, 1);
         x += __shfl_xor_sync(0xffffffffu, x, 2);
