@@ -453,24 +453,36 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
           float sv, cv;
           __sincosf(rope_reduce(tok0 + (tok & 15), invf[p]), &sv, &cv);
           const float ov = valid ? entry_value(en) : 0.f;
-          // entries are ordered by token: suffix sums within runs of equal tokens
-          int tn[5];
-#pragma unroll
-          for (int s = 0; s < 5; ++s) tn[s] = __shfl_down_sync(0xffffffffu, tok, 1 << s);
+          // Entries are ordered by token: suffix sums within runs of equal
+          // tokens; runs are almost always at most 4 long (two steps), longer
+          // ones take the remaining steps.
+          const int tn1 = __shfl_down_sync(0xffffffffu, tok, 1);
+          const int tn2 = __shfl_down_sync(0xffffffffu, tok, 2);
+          const int tn4 = __shfl_down_sync(0xffffffffu, tok, 4);
           const int tprev = __shfl_up_sync(0xffffffffu, tok, 1);  // every lane takes part
           const bool head = valid && (lane == 0 || tprev != tok);
+          const bool longer = __any_sync(0xffffffffu, head && lane + 4 < 32 && tn4 == tok);
 #pragma unroll
           for (int gg = 0; gg < G; ++gg) {
+            // the fp16 constants of the MMA (the reference rounds each
+            // dequantized key to fp16; fp16 constants track it more closely)
             const uint32_t* bw = reinterpret_cast<const uint32_t*>(
                 smem + L::kB + ((slot0 + gg) * 16 + (p >> 2)) * (kBRow * 4));
             const uint32_t pw = bw[p & 3], qw = bw[4 + (p & 3)];
             const float P = ch >= 64 ? half_hi(pw) : half_lo(pw);
             const float Q = ch >= 64 ? half_hi(qw) : half_lo(qw);
             float v = ov * fmaf(cv, P, sv * Q);
+            float o = __shfl_down_sync(0xffffffffu, v, 1);
+            if (lane + 1 < 32 && tn1 == tok) v += o;
+            o = __shfl_down_sync(0xffffffffu, v, 2);
+            if (lane + 2 < 32 && tn2 == tok) v += o;
+            if (longer) {
 #pragma unroll
-            for (int s = 0; s < 5; ++s) {
-              const float o = __shfl_down_sync(0xffffffffu, v, 1 << s);
-              if (lane + (1 << s) < 32 && tn[s] == tok) v += o;
+              for (int sh = 4; sh < 32; sh <<= 1) {
+                const int tn = __shfl_down_sync(0xffffffffu, tok, sh);
+                o = __shfl_down_sync(0xffffffffu, v, sh);
+                if (lane + sh < 32 && tn == tok) v += o;
+              }
             }
             if (head) sc[(slot0 + gg) * kKeyTokens + 16 * warp + tok] += v;
           }
