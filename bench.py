@@ -148,15 +148,22 @@ def build_cache(wl, layers, h0, hl, dev, log):
     cache = []
     cbk = cbv = None
     t0 = time.time()
+    q_ms = []  # quantize-on-append time of the whole prefill block, per layer (after the first)
     for layer in range(layers):
         syn.fill_layer(k, v, layer, seed=0)
         ks, kz = syn.key_calibration(k)
         if cbk is None:  # one codebook pair for the synthetic model (same distribution per layer)
             cbk, cbv = syn.fit_codebooks(k, v, ks, kz, wl.bits)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
         pk = quantize_keys(k, ks, kz, cbk, wl.bits, wl.outlier_ratio, True, h0=h0, n_heads=hl,
                            capacity=T)
         pv = quantize_values(v, cbv, wl.bits, wl.outlier_ratio, True, h0=h0, n_heads=hl,
                              capacity=T)
+        e1.record()
+        if 1 <= layer <= 3:
+            e1.synchronize()
+            q_ms.append(e0.elapsed_time(e1))
         cache.append((pk, pv))
         if layer == 0 or (layer + 1) % 8 == 0:
             torch.cuda.synchronize()
@@ -164,7 +171,16 @@ def build_cache(wl, layers, h0, hl, dev, log):
                 f"{torch.cuda.memory_allocated(dev) / 2**30:.1f} GiB)")
     del k, v
     torch.cuda.empty_cache()
-    return cache
+    qstat = None
+    if q_ms:
+        ms = statistics.mean(q_ms)
+        # fp16 input read: the rank's key channels, the full value rows (per-token stats)
+        in_bytes = B * T * (hl * 128 + C) * 2
+        qstat = {"ms_per_layer": ms, "tokens": T, "input_bytes": in_bytes,
+                 "input_GBps": in_bytes / (ms / 1e3) / 1e9,
+                 "what": "quantize_keys + quantize_values of one layer's prefill block "
+                         "(plan + emit, outliers, packing), CUDA events"}
+    return cache, qstat
 
 
 # DRAM bytes (ncu dram__bytes_read.sum + dram__bytes_write.sum) per algorithmic
@@ -221,7 +237,7 @@ def run_gpu(args):
     T = wl.tokens
     log = (lambda m: print(f"[rank {rank}] {m}", file=sys.stderr, flush=True))
 
-    cache = build_cache(wl, layers, h0, hl, dev, log)
+    cache, qstat = build_cache(wl, layers, h0, hl, dev, log)
     inv = rope_inv_freq(128, wl.rope_base).to(dev)
     qs = [syn.make_query(wl.batch, wl.kv_heads * G, l, 0, dev)[:, h0 * G:(h0 + hl) * G].contiguous()
           for l in range(layers)]
@@ -358,6 +374,7 @@ def run_gpu(args):
             "step_bandwidth_gbs": step_bytes / (ms_step / 1e3) / 1e9,
             "kernels_ms": {"key_scores": k_avg, "softmax": s_avg, "value_output": v_avg},
             "cpu_baseline": cpu,
+            "quantize_append": qstat,
             "e2e": e2e,
             "gpu_launches": n_launch_per_layer * layers * args.steps,
             "clocks": clk,
