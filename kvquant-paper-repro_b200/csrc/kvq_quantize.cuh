@@ -271,87 +271,109 @@ __device__ __forceinline__ uint32_t outlier_entry(int token, int channel, float 
   return (uint32_t)((token << 7) | channel) | ((uint32_t)__half_as_ushort(h) << 16);
 }
 
-// Channel within head of code slot q (0..31) of chunk j.
-template <int KIND>
-__device__ __forceinline__ int slot_channel(int j, int q) {
-  const int m = q >> 1, sec = q & 1;
-  return KIND == 0 ? (16 * j + m + 64 * sec) : (32 * j + 2 * m + sec);
-}
-
+// One CTA of 128 threads per (tile, b, head); thread c owns channel c of the
+// head and walks the tile's 32 tokens, so every shared-memory access of a
+// warp is to consecutive channels. The tile's fp16 block (32 x 128) is staged
+// once with coalesced 16-byte loads; a key channel's zero / scale / selection
+// live in registers, a value token's in shared memory.
 template <int KIND, bool COUNT_ONLY>
 __global__ void __launch_bounds__(128) emit_kernel(EmitArgs a) {
-  __shared__ int32_t cnt[32][8];  // per token, per 16-channel group (channel order)
+  __shared__ __align__(16) __half xs[kTileTokens][kHeadDim];  // the tile's inputs
+  __shared__ int32_t cnt[kTileTokens][8];  // outliers per (token, 16-channel group)
   __shared__ float s_cb[16];
   __shared__ uint8_t s_code[kTileTokens][kHeadDim];  // codes of the tile (token, channel)
+  __shared__ float s_vs[kTileTokens], s_vz[kTileTokens];  // values: per-token scale / zero
+  __shared__ Select s_rs[kTileTokens];                   // values: per-token selection
   const int64_t b = blockIdx.y;
   const int64_t tile = blockIdx.x;
   const int64_t h = blockIdx.z;  // local head
-  const int j = threadIdx.x >> 5, i = threadIdx.x & 31;
-  const int64_t t = tile * kTileTokens + i;
+  const int c = threadIdx.x;     // channel within the head
+  const int lane = c & 31, w = c >> 5;
   const int64_t unit = b * a.H + h;
   const int ncb = 1 << a.bits;
-  if (!COUNT_ONLY && threadIdx.x < ncb) s_cb[threadIdx.x] = a.cb[threadIdx.x];
-  const bool is_sink = a.off == 1 && t == 0;
-  const bool live = t < a.S && !is_sink;
   const int64_t CL = a.H * kHeadDim;
-  float sc_t = 0.f, z_t = 0.f;
-  Select rs;
-  if (KIND == 1 && live) {
-    sc_t = a.v_scale[b * a.ld_stats + t];
-    z_t = a.v_zero[b * a.ld_stats + t];
-    rs = a.sel[b * a.S + t];
+  const int64_t cfull = (a.h0 + h) * kHeadDim + c;
+  const int64_t t0 = tile * kTileTokens;
+  if (!COUNT_ONLY && c < ncb) s_cb[c] = a.cb[c];
+  // stage x[t0 .. t0+31][head channels] (rows beyond S read as 0)
+  for (int k = c; k < kTileTokens * (kHeadDim / 8); k += 128) {
+    const int i = k >> 4, ch8 = (k & 15) * 8;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (t0 + i < a.S)
+      v = *reinterpret_cast<const uint4*>(a.x + (b * a.S + t0 + i) * a.C_full + (a.h0 + h) * kHeadDim + ch8);
+    *reinterpret_cast<uint4*>(&xs[i][ch8]) = v;
+  }
+  float kz = 0.f, ks = 0.f;
+  Select cs{};
+  if (KIND == 0) {
+    kz = a.k_zero[cfull];
+    ks = a.k_scale[cfull];
+    cs = a.sel[b * CL + h * kHeadDim + c];
+  } else if (c < kTileTokens) {
+    const int64_t t = t0 + c;
+    const bool live = t < a.S && !(a.off == 1 && t == 0);
+    s_vs[c] = live ? a.v_scale[b * a.ld_stats + t] : 0.f;
+    s_vz[c] = live ? a.v_zero[b * a.ld_stats + t] : 0.f;
+    if (live) s_rs[c] = a.sel[b * a.S + t];
   }
   __syncthreads();
-  uint32_t omask = 0;                // outlier flag per code slot
-  float nval[32];
-  const __half* xrow = a.x + (b * a.S + (t < a.S ? t : 0)) * a.C_full + (a.h0 + h) * kHeadDim;
+
+  uint32_t omask = 0;  // outlier flag per token i
+  float nval[kTileTokens];
 #pragma unroll
-  for (int q = 0; q < 32; ++q) {
-    const int d = slot_channel<KIND>(j, q);
+  for (int i = 0; i < kTileTokens; ++i) {
+    const int64_t t = t0 + i;
+    const bool is_sink = a.off == 1 && t == 0;
+    const bool live = t < a.S && !is_sink;
     float n = 0.f;
     int code = 0;
     bool out = false;
     if (live) {
-      const float xv = __half2float(xrow[d]);
+      const float xv = __half2float(xs[i][c]);
       if (KIND == 0) {
-        const int64_t cfull = (a.h0 + h) * kHeadDim + d;
-        n = normalize(xv, a.k_zero[cfull], a.k_scale[cfull]);
-        const Select cs = a.sel[b * CL + h * kHeadDim + d];
+        n = normalize(xv, kz, ks);
         out = a.nnz_cap >= 0 && selected(abs_bits(n), (int32_t)(t - a.off), cs);
       } else {
-        n = normalize(xv, z_t, sc_t);
-        out = a.nnz_cap >= 0 && selected(abs_bits(n), (int32_t)((a.h0 + h) * kHeadDim + d), rs);
+        n = normalize(xv, s_vz[i], s_vs[i]);
+        out = a.nnz_cap >= 0 && selected(abs_bits(n), (int32_t)cfull, s_rs[i]);
       }
       if (!COUNT_ONLY) {
         const float dense = out ? 0.f : fminf(fmaxf(n, -1.f), 1.f);
         code = nearest_centroid(dense, s_cb, ncb);
       }
     }
-    nval[q] = n;
-    if (out) omask |= 1u << q;
-    if (!COUNT_ONLY) s_code[i][d] = (uint8_t)code;
+    nval[i] = n;
+    if (out) omask |= 1u << i;
+    const uint32_t bal = __ballot_sync(0xffffffffu, out);
+    if (lane == 0) {
+      cnt[i][2 * w] = __popc(bal & 0xffffu);  // channels 32w .. 32w+15
+      cnt[i][2 * w + 1] = __popc(bal >> 16);  // channels 32w+16 .. 32w+31
+    }
+    if (!COUNT_ONLY) {
+      s_code[i][c] = (uint8_t)code;
+      if (a.dequant_out && t < a.S) {
+        __half* drow = a.dequant_out + (b * a.S + t) * CL + h * kHeadDim;
+        drow[c] = is_sink ? xs[i][c]
+                          : __float2half_rn(dequant_ref(s_cb[code], out ? n : 0.f,
+                                                        KIND == 0 ? ks : s_vs[i],
+                                                        KIND == 0 ? kz : s_vz[i]));
+      }
+    }
   }
-  // Outlier counts per (token, 16-channel group in channel order).
-  if (KIND == 0) {
-    cnt[i][j] = __popc(omask & 0x55555555u);      // channels 16j..16j+15
-    cnt[i][4 + j] = __popc(omask & 0xaaaaaaaau);  // channels 64+16j..
-  } else {
-    cnt[i][2 * j] = __popc(omask & 0x0000ffffu);  // channels 32j..32j+15
-    cnt[i][2 * j + 1] = __popc(omask & 0xffff0000u);
-  }
+  if (!COUNT_ONLY && a.sink_out && a.off == 1 && tile == 0) a.sink_out[b * CL + h * kHeadDim + c] = xs[0][c];
   __syncthreads();
   if (COUNT_ONLY) {
-    if (threadIdx.x < 2) {  // block threadIdx.x = tokens 16*blk .. 16*blk+15
+    if (c < 2) {  // block c = tokens 16c .. 16c+15
       int32_t tot = 0;
-      for (int r = 16 * 8 * threadIdx.x; r < 16 * 8 * (threadIdx.x + 1); ++r) tot += (&cnt[0][0])[r];
-      a.out_ptr[2 * (unit * a.nt_cap + tile) + threadIdx.x + 1] = tot;
+      for (int r = 16 * 8 * c; r < 16 * 8 * (c + 1); ++r) tot += (&cnt[0][0])[r];
+      a.out_ptr[2 * (unit * a.nt_cap + tile) + c + 1] = tot;
     }
     return;
   }
   // Exclusive prefix over (token, group) in order -> entry offsets.
-  if (threadIdx.x == 0) {
+  if (c == 0) {
     int32_t run = 0;
-    for (int r = 0; r < 32 * 8; ++r) {
+    for (int r = 0; r < kTileTokens * 8; ++r) {
       const int32_t v = (&cnt[0][0])[r];
       (&cnt[0][0])[r] = run;
       run += v;
@@ -359,22 +381,34 @@ __global__ void __launch_bounds__(128) emit_kernel(EmitArgs a) {
   }
   __syncthreads();
   const int64_t base = a.out_ptr[2 * (unit * a.nt_cap + tile)];  // first entry of the tile
+  // Outlier entries in (token, channel) order: rank within the 16-channel group.
+  const uint32_t below = (1u << (lane & 15)) - 1u;
+#pragma unroll
+  for (int i = 0; i < kTileTokens; ++i) {
+    const bool out = (omask >> i) & 1u;
+    const uint32_t bal = __ballot_sync(0xffffffffu, out);
+    if (out) {
+      const uint32_t grp = lane < 16 ? (bal & 0xffffu) : (bal >> 16);
+      const int64_t e = base + cnt[i][c >> 4] + __popc(grp & below);
+      if (e < a.nnz_cap) a.out_ent[e] = outlier_entry(i, c, nval[i]);
+    }
+  }
   // Slab store: threads 0..63 each pack the slab of (block, lane) = (tid >> 5,
   // tid & 31) in the fragment-native order of the decode kernels.
-  if (threadIdx.x < 64) {
-    const int blk = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g = lane >> 2, c = lane & 3;
+  if (c < 64) {
+    const int blk = c >> 5;
+    const int g = lane >> 2, cc = lane & 3;
     uint32_t slab[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // up to 32 bytes (4-bit)
 #pragma unroll
     for (int q = 0; q < 32; ++q) {
       int ta, ca, tb, cb2;
-      if (KIND == 0) {  // keys: token 16*blk + g + 8*(q&1), RoPE pair 4*(q>>1) + c
+      if (KIND == 0) {  // keys: token 16*blk + g + 8*(q&1), RoPE pair 4*(q>>1) + cc
         ta = tb = 16 * blk + g + 8 * (q & 1);
-        ca = 4 * (q >> 1) + c;
+        ca = 4 * (q >> 1) + cc;
         cb2 = ca + 64;
       } else {          // values: channel 16*(q>>2) + g + 8*(q&1), tokens (t, t+1)
         ca = cb2 = 16 * (q >> 2) + g + 8 * (q & 1);
-        ta = 16 * blk + 2 * c + 8 * ((q >> 1) & 1);
+        ta = 16 * blk + 2 * cc + 8 * ((q >> 1) & 1);
         tb = ta + 1;
       }
       const uint32_t pair = (uint32_t)s_code[ta][ca] | ((uint32_t)s_code[tb][cb2] << a.bits);
@@ -392,55 +426,6 @@ __global__ void __launch_bounds__(128) emit_kernel(EmitArgs a) {
       *reinterpret_cast<uint4*>(blk_base + 512 + lane * 16) = make_uint4(slab[4], slab[5], slab[6], slab[7]);
     else if (a.bits == 3)
       *reinterpret_cast<uint2*>(blk_base + 512 + lane * 8) = make_uint2(slab[4], slab[5]);
-  }
-  // Outlier entries in (token, channel) order.
-  if (omask) {
-    int32_t o0, o1;
-    if (KIND == 0) { o0 = cnt[i][j]; o1 = cnt[i][4 + j]; }
-    else { o0 = cnt[i][2 * j]; o1 = cnt[i][2 * j + 1]; }
-    // first group: KIND0 even slots (m ascending), KIND1 slots 0..15
-#pragma unroll
-    for (int q = 0; q < 32; ++q) {
-      const bool first = KIND == 0 ? ((q & 1) == 0) : (q < 16);
-      if (!first || !(omask & (1u << q))) continue;
-      const int64_t e = base + o0++;
-      if (e < a.nnz_cap) a.out_ent[e] = outlier_entry(i, slot_channel<KIND>(j, q), nval[q]);
-    }
-#pragma unroll
-    for (int q = 0; q < 32; ++q) {
-      const bool second = KIND == 0 ? ((q & 1) == 1) : (q >= 16);
-      if (!second || !(omask & (1u << q))) continue;
-      const int64_t e = base + o1++;
-      if (e < a.nnz_cap) a.out_ent[e] = outlier_entry(i, slot_channel<KIND>(j, q), nval[q]);
-    }
-  }
-  // Sink copy and fake-quant output.
-  const int64_t cl0 = h * kHeadDim;
-  if (is_sink && a.sink_out) {
-    for (int q = 0; q < 32; ++q) {
-      const int d = slot_channel<KIND>(j, q);
-      a.sink_out[b * CL + cl0 + d] = xrow[d];
-    }
-  }
-  if (a.dequant_out && t < a.S) {
-    __half* drow = a.dequant_out + (b * a.S + t) * CL + cl0;
-#pragma unroll
-    for (int q = 0; q < 32; ++q) {
-      const int d = slot_channel<KIND>(j, q);
-      if (is_sink) { drow[d] = xrow[d]; continue; }
-      const uint32_t code = s_code[i][d];
-      const bool out = (omask >> q) & 1u;
-      float s, z;
-      if (KIND == 0) {
-        const int64_t cfull = (a.h0 + h) * kHeadDim + d;
-        s = a.k_scale[cfull];
-        z = a.k_zero[cfull];
-      } else {
-        s = sc_t;
-        z = z_t;
-      }
-      drow[d] = __float2half_rn(dequant_ref(s_cb[code], out ? nval[q] : 0.f, s, z));
-    }
   }
 }
 
@@ -537,6 +522,15 @@ static int check_block(const char* what, int64_t B, int64_t S, int64_t C_full, i
   return KVQ_OK;
 }
 
+// The emit kernels stage a tile's inputs with 16-byte loads.
+static int check_x(const char* what, const void* x, int64_t C_full) {
+  if (reinterpret_cast<uintptr_t>(x) % 16 != 0 || C_full % 8 != 0) {
+    set_error("%s: the input must be 16-byte aligned with C_full a multiple of 8", what);
+    return KVQ_ERR_INVALID;
+  }
+  return KVQ_OK;
+}
+
 }  // namespace kvq
 
 extern "C" int kvq_quantize_keys_plan(const void* k, int64_t B, int64_t S, int64_t C_full,
@@ -547,6 +541,7 @@ extern "C" int kvq_quantize_keys_plan(const void* k, int64_t B, int64_t S, int64
   using namespace kvq;
   clear_error();
   int rc = check_block("quantize_keys_plan", B, S, C_full, h0, n_heads, nt_cap);
+  if (!rc) rc = check_x("quantize_keys_plan", k, C_full);
   if (rc) return rc;
   if (workspace_bytes < key_ws_bytes(B, n_heads) || !workspace) {
     set_error("quantize_keys_plan: workspace too small (%zu < %zu)", workspace_bytes,
@@ -599,6 +594,7 @@ extern "C" int kvq_quantize_keys_emit(const void* k, int64_t B, int64_t S, int64
   using namespace kvq;
   clear_error();
   int rc = check_block("quantize_keys_emit", B, S, C_full, h0, n_heads, nt_cap);
+  if (!rc) rc = check_x("quantize_keys_emit", k, C_full);
   if (rc) return rc;
   if (!bits_ok(bits)) {
     set_error("quantize_keys_emit: bits must be 2, 3 or 4 (got %d)", bits);
@@ -636,6 +632,7 @@ extern "C" int kvq_quantize_values_plan(const void* v, int64_t B, int64_t S, int
   using namespace kvq;
   clear_error();
   int rc = check_block("quantize_values_plan", B, S, C_full, h0, n_heads, nt_cap);
+  if (!rc) rc = check_x("quantize_values_plan", v, C_full);
   if (rc) return rc;
   if (C_full > kValRowMax) {
     set_error("quantize_values_plan: C=%lld channels exceed %d", (long long)C_full, kValRowMax);
@@ -694,6 +691,7 @@ extern "C" int kvq_quantize_values_emit(const void* v, int64_t B, int64_t S, int
   using namespace kvq;
   clear_error();
   int rc = check_block("quantize_values_emit", B, S, C_full, h0, n_heads, nt_cap);
+  if (!rc) rc = check_x("quantize_values_emit", v, C_full);
   if (rc) return rc;
   if (!bits_ok(bits)) {
     set_error("quantize_values_emit: bits must be 2, 3 or 4 (got %d)", bits);
