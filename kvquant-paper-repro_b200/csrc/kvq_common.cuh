@@ -59,6 +59,45 @@ __device__ __forceinline__ int nearest_centroid(float v, const float* cb, int n)
   return best;
 }
 
+// The same rule in O(log n) over the codebook sorted ascending (sv, with the
+// original indices si; equal values keep their original order). fl(v - c) is
+// non-increasing in c, so over the sorted codebook the rounded distances
+// |fl(v - c)| fall up to the last entry <= v and rise after it; the entries at
+// the minimal distance therefore form one contiguous run around that boundary,
+// and the first minimum of the original order is the lowest original index in
+// the run. n is a power of two <= 16.
+__device__ __forceinline__ int nearest_centroid_sorted(float v, const float* sv, const uint8_t* si,
+                                                       int n) {
+  int j = 0;  // number of entries <= v: binary search, then the last step
+#pragma unroll
+  for (int step = 8; step >= 1; step >>= 1)
+    if (step < n && sv[j + step - 1] <= v) j += step;
+  if (sv[j] <= v) ++j;  // here j <= n - 1
+  float m = INFINITY;
+  if (j > 0) m = fabsf(__fsub_rn(v, sv[j - 1]));
+  if (j < n) m = fminf(m, fabsf(__fsub_rn(v, sv[j])));
+  int best = 255;
+  for (int k = j - 1; k >= 0 && fabsf(__fsub_rn(v, sv[k])) == m; --k) best = min(best, (int)si[k]);
+  for (int k = j; k < n && fabsf(__fsub_rn(v, sv[k])) == m; ++k) best = min(best, (int)si[k]);
+  return best;
+}
+
+// Sorts a codebook of n <= 16 entries ascending (stable) with its original
+// indices; one thread.
+__device__ __forceinline__ void sort_codebook(const float* cb, int n, float* sv, uint8_t* si) {
+  for (int k = 0; k < n; ++k) {
+    const float x = cb[k];
+    int p = k;
+    while (p > 0 && sv[p - 1] > x) {
+      sv[p] = sv[p - 1];
+      si[p] = si[p - 1];
+      --p;
+    }
+    sv[p] = x;
+    si[p] = (uint8_t)k;
+  }
+}
+
 // Fake-quant dequantization (q + o) * s + z with the reference's fp32 op order
 // (kvquant/quant/kv_quantizer.py:89,117): add, multiply, add, each rounded.
 __device__ __forceinline__ float dequant_ref(float cbq, float o, float s, float z) {

@@ -113,19 +113,31 @@ __global__ void key_ties_kernel(KeyShape ks, Select* __restrict__ sel, int64_t n
   const int64_t n_rest = ks.S - ks.off;
   int32_t need = s.kleft;
   int32_t cut = -1;
-  for (int64_t r0 = 0; r0 < n_rest && need > 0; r0 += 32) {
-    const int64_t r = r0 + lane;
-    const bool tie = r < n_rest && abs_bits(key_norm(ks, b, r + ks.off, c)) == s.thr;
-    const uint32_t bal = __ballot_sync(0xffffffffu, tie);
-    const int cnt = __popc(bal);
-    if (cnt >= need) {
-      // the need-th set bit of bal
-      uint32_t m = bal;
-      for (int i = 1; i < need; ++i) m &= m - 1;
-      cut = (int32_t)(r0 + (__ffs(m) - 1));
+  // 256 tokens per step, 8 consecutive ones per lane (8 loads in flight)
+  for (int64_t r0 = 0; r0 < n_rest && need > 0; r0 += 256) {
+    uint32_t m8 = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int64_t r = r0 + lane * 8 + q;
+      if (r < n_rest && abs_bits(key_norm(ks, b, r + ks.off, c)) == s.thr) m8 |= 1u << q;
+    }
+    const int cnt = __popc(m8);
+    int incl = cnt;  // inclusive prefix of the tie counts in token order
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += o;
+    }
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
+    if (total >= need) {
+      const int L = __ffs(__ballot_sync(0xffffffffu, incl >= need)) - 1;
+      const int before = __shfl_sync(0xffffffffu, incl - cnt, L);
+      uint32_t m = __shfl_sync(0xffffffffu, m8, L);
+      for (int i = 1; i < need - before; ++i) m &= m - 1;  // the (need - before)-th tie of lane L
+      cut = (int32_t)(r0 + L * 8 + (__ffs(m) - 1));
       need = 0;
     } else {
-      need -= cnt;
+      need -= total;
     }
   }
   if (lane == 0) { s.tie_cut = cut; sel[col] = s; }
@@ -280,7 +292,8 @@ template <int KIND, bool COUNT_ONLY>
 __global__ void __launch_bounds__(128) emit_kernel(EmitArgs a) {
   __shared__ __align__(16) __half xs[kTileTokens][kHeadDim];  // the tile's inputs
   __shared__ int32_t cnt[kTileTokens][8];  // outliers per (token, 16-channel group)
-  __shared__ float s_cb[16];
+  __shared__ float s_cb[16], s_cbs[16];  // codebook, and sorted ascending
+  __shared__ uint8_t s_cbi[16];          // original index of each sorted entry
   __shared__ uint8_t s_code[kTileTokens][kHeadDim];  // codes of the tile (token, channel)
   __shared__ float s_vs[kTileTokens], s_vz[kTileTokens];  // values: per-token scale / zero
   __shared__ Select s_rs[kTileTokens];                   // values: per-token selection
@@ -294,7 +307,10 @@ __global__ void __launch_bounds__(128) emit_kernel(EmitArgs a) {
   const int64_t CL = a.H * kHeadDim;
   const int64_t cfull = (a.h0 + h) * kHeadDim + c;
   const int64_t t0 = tile * kTileTokens;
-  if (!COUNT_ONLY && c < ncb) s_cb[c] = a.cb[c];
+  if (!COUNT_ONLY && c == 0) {
+    for (int k = 0; k < ncb; ++k) s_cb[k] = a.cb[k];
+    sort_codebook(s_cb, ncb, s_cbs, s_cbi);
+  }
   // stage x[t0 .. t0+31][head channels] (rows beyond S read as 0)
   for (int k = c; k < kTileTokens * (kHeadDim / 8); k += 128) {
     const int i = k >> 4, ch8 = (k & 15) * 8;
@@ -339,7 +355,7 @@ __global__ void __launch_bounds__(128) emit_kernel(EmitArgs a) {
       }
       if (!COUNT_ONLY) {
         const float dense = out ? 0.f : fminf(fmaxf(n, -1.f), 1.f);
-        code = nearest_centroid(dense, s_cb, ncb);
+        code = nearest_centroid_sorted(dense, s_cbs, s_cbi, ncb);
       }
     }
     nval[i] = n;
