@@ -445,33 +445,90 @@ __global__ void __launch_bounds__(128) emit_kernel(EmitArgs a) {
   }
 }
 
-// Single-CTA exclusive scan of counts stored at ptr[1..n] (ptr[0] = 0) and the
-// total nnz. n is the number of CSR rows (2 * U * nt_cap).
-__global__ void __launch_bounds__(1024) scan_counts_kernel(int32_t* __restrict__ ptr, int64_t n,
-                                                           int64_t* __restrict__ nnz_out) {
-  __shared__ int64_t part[1024];
-  const int64_t per = (n + blockDim.x - 1) / blockDim.x;
-  const int64_t s = threadIdx.x * per, e = min(n, s + per);
-  int64_t sum = 0;
-  for (int64_t i = s; i < e; ++i) sum += ptr[i + 1];
-  part[threadIdx.x] = sum;
+// Exclusive scan of the per-row counts stored at ptr[1..n] (ptr[0] = 0) into
+// the CSR row pointer, and the total nnz; n is the number of rows. Three
+// launches and no scratch: (1) every chunk of kScanChunk counts is scanned in
+// place (inclusive, local); (2) one CTA turns the chunk totals (each chunk's
+// last element) into their final values; (3) every chunk but the first adds
+// the final value of the previous chunk's last element to its other elements.
+constexpr int kScanThreads = 1024, kScanPer = 4, kScanChunk = kScanThreads * kScanPer;
+
+__device__ __forceinline__ int64_t block_incl_scan(int64_t v, int64_t* sh) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int64_t o = __shfl_up_sync(0xffffffffu, v, d);
+    if (lane >= d) v += o;
+  }
+  if (lane == 31) sh[w] = v;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int64_t run = 0;
-    for (int i = 0; i < (int)blockDim.x; ++i) {
-      const int64_t v = part[i];
-      part[i] = run;
-      run += v;
+  if (w == 0) {
+    int64_t x = lane < (int)(blockDim.x >> 5) ? sh[lane] : 0;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int64_t o = __shfl_up_sync(0xffffffffu, x, d);
+      if (lane >= d) x += o;
     }
-    ptr[0] = 0;
-    if (nnz_out) *nnz_out = run;
+    sh[lane] = x;
   }
   __syncthreads();
-  int64_t run = part[threadIdx.x];
-  for (int64_t i = s; i < e; ++i) {
-    run += ptr[i + 1];
-    ptr[i + 1] = (int32_t)run;
+  const int64_t r = v + (w > 0 ? sh[w - 1] : 0);
+  __syncthreads();
+  return r;
+}
+
+__global__ void __launch_bounds__(kScanThreads) scan_chunks_kernel(int32_t* __restrict__ ptr, int64_t n) {
+  __shared__ int64_t sh[32];
+  const int64_t i0 = (int64_t)blockIdx.x * kScanChunk + (int64_t)threadIdx.x * kScanPer;
+  int32_t v[kScanPer];
+  int64_t sum = 0;
+#pragma unroll
+  for (int k = 0; k < kScanPer; ++k) {
+    v[k] = i0 + k < n ? ptr[1 + i0 + k] : 0;
+    sum += v[k];
   }
+  int64_t run = block_incl_scan(sum, sh) - sum;
+#pragma unroll
+  for (int k = 0; k < kScanPer; ++k) {
+    run += v[k];
+    if (i0 + k < n) ptr[1 + i0 + k] = (int32_t)run;
+  }
+}
+
+__global__ void __launch_bounds__(kScanThreads) scan_totals_kernel(int32_t* __restrict__ ptr, int64_t n,
+                                                                  int64_t* __restrict__ nnz_out) {
+  __shared__ int64_t sh[32];
+  const int64_t nb = (n + kScanChunk - 1) / kScanChunk;
+  int64_t carry = 0;
+  for (int64_t c0 = 0; c0 < nb; c0 += kScanThreads) {
+    const int64_t c = c0 + threadIdx.x;
+    const int64_t last = c < nb ? min(n, (c + 1) * kScanChunk) : 0;  // index (1-based) of the chunk's last count
+    const int64_t tot = c < nb ? ptr[last] : 0;
+    const int64_t incl = block_incl_scan(tot, sh);
+    if (c < nb) ptr[last] = (int32_t)(carry + incl);
+    if (threadIdx.x == kScanThreads - 1) sh[0] = incl;  // this batch's total
+    __syncthreads();
+    carry += sh[0];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    ptr[0] = 0;
+    if (nnz_out) *nnz_out = carry;
+  }
+}
+
+__global__ void __launch_bounds__(kScanThreads) scan_offsets_kernel(int32_t* __restrict__ ptr, int64_t n) {
+  const int64_t c = (int64_t)blockIdx.x + 1;  // chunk 0 needs no offset
+  const int32_t off = ptr[c * kScanChunk];    // final value of the previous chunk's last count
+  const int64_t last = min(n, (c + 1) * kScanChunk);
+  for (int64_t i = c * kScanChunk + 1 + threadIdx.x; i < last; i += kScanThreads) ptr[i] += off;
+}
+
+static void scan_counts(int32_t* ptr, int64_t n, int64_t* nnz_out, cudaStream_t st) {
+  const int64_t nb = (n + kScanChunk - 1) / kScanChunk;
+  scan_chunks_kernel<<<(unsigned)nb, kScanThreads, 0, st>>>(ptr, n);
+  scan_totals_kernel<<<1, kScanThreads, 0, st>>>(ptr, n, nnz_out);
+  if (nb > 1) scan_offsets_kernel<<<(unsigned)(nb - 1), kScanThreads, 0, st>>>(ptr, n);
 }
 
 __global__ void init_select_kernel(Select* __restrict__ sel, int64_t n, int32_t k) {
@@ -595,7 +652,7 @@ extern "C" int kvq_quantize_keys_plan(const void* k, int64_t B, int64_t S, int64
   const int64_t nt = (S + kTileTokens - 1) / kTileTokens;
   ea.cb = nullptr;  // COUNT_ONLY never reads the codebook
   emit_kernel<0, true><<<dim3((unsigned)nt, (unsigned)B, (unsigned)n_heads), 128, 0, st>>>(ea);
-  scan_counts_kernel<<<1, 1024, 0, st>>>(out_ptr, nrows, nnz_out);
+  scan_counts(out_ptr, nrows, nnz_out, st);
   return check_launch("quantize_keys_plan");
 }
 
@@ -691,7 +748,7 @@ extern "C" int kvq_quantize_values_plan(const void* v, int64_t B, int64_t S, int
   ea.out_ptr = out_ptr; ea.nnz_cap = outliers ? 0 : -1;
   const int64_t nt = (S + kTileTokens - 1) / kTileTokens;
   emit_kernel<1, true><<<dim3((unsigned)nt, (unsigned)B, (unsigned)n_heads), 128, 0, st>>>(ea);
-  scan_counts_kernel<<<1, 1024, 0, st>>>(out_ptr, nrows, nnz_out);
+  scan_counts(out_ptr, nrows, nnz_out, st);
   return check_launch("quantize_values_plan");
 }
 
