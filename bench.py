@@ -5,7 +5,8 @@ Workload (default "longctx-1m-4bit"): LLaMA-2-7B shape -- batch 1, 32 KV heads
 of 128 channels, 1,048,576 cached tokens in each of 32 layers, 4-bit NUQ keys
 (per channel, pre-RoPE) and values (per token) with 1% fp16 outliers, RoPE
 theta 10000. One step = one decode step of attention over the whole cache:
-for every layer, the fused key kernel, softmax and the value kernel. Synthetic
+for every layer, the fused key kernel (which also leaves the softmax partials)
+and the value kernel (which forms the probabilities from the raw scores). Synthetic
 seeded data (the reference's wikitext-2 activations are not available); the
 cache is built on the GPU by this library's quantize-on-append kernels.
 
@@ -206,19 +207,22 @@ def algorithmic_bytes(wl, pk, pv, hl, T):
     U = B * hl
     nt = -(-T // 32)
     codes = U * T * 16 * bits
+    stats = B * hl * G * -(-T // 256) * 8  # softmax partials (max, sum) per 256 tokens
+    # key: codes, outliers, row pointers, calibration, sink, q; writes scores + partials
     key = (codes + pk["nnz"] * 4 + U * nt * 8 + 2 * hl * 128 * 4 + B * hl * 128 * 2
-           + B * hl * G * 128 * 2 + B * hl * G * T * 4)
+           + B * hl * G * 128 * 2 + B * hl * G * T * 4 + stats)
+    # value: codes, outliers, row pointers, per-token scale/zero, sink, raw scores +
+    # partials; writes the output
     value = (codes + pv["nnz"] * 4 + U * nt * 8 + B * T * 8 + B * hl * 128 * 2
-             + B * hl * G * T * 4 + B * hl * G * 128 * 2)
-    softmax = 3 * B * hl * G * T * 4
-    return {"key_scores": key, "value_output": value, "softmax": softmax}
+             + B * hl * G * T * 4 + stats + B * hl * G * 128 * 2)
+    return {"key_scores": key, "value_output": value}
 
 
 def run_gpu(args):
     import torch
     import torch.distributed as dist
     from kvquant import synthetic as syn
-    from kvquant.kernels import qk_scores, softmax, pv_out, rope_inv_freq, decode_attention
+    from kvquant.kernels import qk_scores_stats, pv_out_scores, rope_inv_freq, decode_attention
     from kvquant.kernels.decode import DecodeWorkspace
 
     world, rank, local = setup_dist(args)
@@ -243,26 +247,26 @@ def run_gpu(args):
           for l in range(layers)]
     Hq_l = hl * G
     scores = torch.empty((wl.batch, Hq_l, T), dtype=torch.float32, device=dev)
+    stats = torch.empty((wl.batch * Hq_l, -(-T // 256), 2), dtype=torch.float32, device=dev)
     outs = [torch.empty((wl.batch, Hq_l, 128), dtype=torch.float16, device=dev)
             for _ in range(layers)]
     full = [gather_buffer(outs[l], world) for l in range(layers)] if world > 1 else None
     stream = torch.cuda.current_stream(dev)
-    n_launch_per_layer = 6  # key, softmax x2, value row max, value, combine
+    # key (scores + softmax partials), value row max, value (softmax of the raw
+    # scores fused in), combine
+    n_launch_per_layer = 4
 
     def step(events=None):
         handles = []
         for l, (pk, pv) in enumerate(cache):
             if events is not None:
                 events[l][0].record(stream)
-            qk_scores(qs[l], pk, inv, out=scores)
+            qk_scores_stats(qs[l], pk, inv, out=scores, stats_out=stats)
             if events is not None:
                 events[l][1].record(stream)
-            p = softmax(scores)
+            outs[l] = pv_out_scores(scores, stats, pv)
             if events is not None:
                 events[l][2].record(stream)
-            outs[l] = pv_out(p, pv)
-            if events is not None:
-                events[l][3].record(stream)
             if world > 1:
                 handles.append(gather_head_outputs(outs[l], full[l], async_op=True))
         for h in handles:
@@ -276,7 +280,7 @@ def run_gpu(args):
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
-    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(layers)]
+    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(layers)]
           for _ in range(args.steps)]
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
@@ -293,8 +297,7 @@ def run_gpu(args):
     clk = clocks.stop()
     elapsed = t_start.elapsed_time(t_end)  # ms
     key_ms = [ev[s][l][0].elapsed_time(ev[s][l][1]) for s in range(args.steps) for l in range(layers)]
-    sm_ms = [ev[s][l][1].elapsed_time(ev[s][l][2]) for s in range(args.steps) for l in range(layers)]
-    val_ms = [ev[s][l][2].elapsed_time(ev[s][l][3]) for s in range(args.steps) for l in range(layers)]
+    val_ms = [ev[s][l][1].elapsed_time(ev[s][l][2]) for s in range(args.steps) for l in range(layers)]
     if world > 1:
         t = torch.tensor([elapsed], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -349,8 +352,7 @@ def run_gpu(args):
     # roofline of the dominant kernel
     pk0, pv0 = cache[0]
     ab = algorithmic_bytes(wl, pk0, pv0, hl, T)
-    k_avg, v_avg, s_avg = (statistics.mean(key_ms), statistics.mean(val_ms),
-                           statistics.mean(sm_ms))
+    k_avg, v_avg = statistics.mean(key_ms), statistics.mean(val_ms)
     dom, dom_ms = ("key_scores", k_avg) if k_avg >= v_avg else ("value_output", v_avg)
     peak, peak_src = peak_hbm()
     achieved = ab[dom] / (dom_ms / 1e3) / 1e9
@@ -372,7 +374,7 @@ def run_gpu(args):
                          "traffic": ab[dom] * DRAM_PER_ALGORITHMIC_BYTE[dom],
                          "bytes_per_launch": ab[dom], "launch_ms": dom_ms},
             "step_bandwidth_gbs": step_bytes / (ms_step / 1e3) / 1e9,
-            "kernels_ms": {"key_scores": k_avg, "softmax": s_avg, "value_output": v_avg},
+            "kernels_ms": {"key_scores": k_avg, "value_output": v_avg},
             "cpu_baseline": cpu,
             "quantize_append": qstat,
             "e2e": e2e,

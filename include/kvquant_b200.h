@@ -12,15 +12,18 @@
  *     sized by the matching *_workspace() query.
  *   - Layout of the quantized cache (per layer; unit u = b*n_heads + h):
  *       codes    uint8 [U, nt_cap, 512*bits]: tiles of 32 tokens; tile =
- *                [2 blocks of 16 tokens][32 lanes][8*bits bytes], lane =
- *                4g + c; slot q (0..31) of a lane's slab is a code pair at
+ *                2 blocks of 16 tokens, block = one 8*bits-byte slab per
+ *                lane (lane = 4g + c) stored structure-of-arrays: bytes 0..15
+ *                of the 32 slabs (512 B), then their remaining 8*bits-16
+ *                bytes. Slot q (0..31) of a lane's slab is a code pair at
  *                bits [2*bits*q, +2*bits), first code in the low bits.
  *                Keys: kb = q>>1, r = q&1: token 16*blk + g + 8r, channels
  *                (p, p+64) with p = 4kb + c.
  *                Values: mb = q>>2, i = q&3: channel 16mb + g + 8(i&1),
  *                tokens (16blk + 2c + 8(i>>1), that + 1).
  *                (The order of the decode kernels' tensor-core fragments.)
- *       outliers CSR over rows (u, tile): ptr int32 [U*nt_cap+1] and one
+ *       outliers CSR over rows (u, tile, 16-token block), row index
+ *                2*(u*nt_cap + tile) + block: ptr int32 [2*U*nt_cap+1] and one
  *                uint32 entry per outlier: low 16 bits = (token_in_tile << 7)
  *                | channel_in_head, high 16 bits = the fp16 normalized raw
  *                value; entries of a row are ordered by (token, channel).
@@ -154,8 +157,37 @@ int kvq_value_output(const uint8_t* codes, const uint32_t* out_ent,
                      int64_t nt_cap, void* out, void* workspace, size_t workspace_bytes,
                      void* stream);
 
+/* Softmax fused into the key and value kernels (no counterpart in the
+ * reference, which materializes the probabilities; the result is the same
+ * softmax). kvq_key_scores_stats is kvq_key_scores that also writes, for
+ * every row and 256-token chunk k of the token axis, stats[row, k] = (m, l):
+ * m = max of scores*scale over the chunk, l = sum of exp(scores*scale - m);
+ * stats is fp32 pairs [B*n_heads*group, ceil(T/256)] (kvq_key_stats_size
+ * bytes). kvq_value_output_scores takes the raw scores and those stats in
+ * place of probabilities and forms softmax(scores * scale) itself (its
+ * workspace: kvq_value_output_scores_workspace bytes); it reads `scores` and
+ * `stats` and writes neither. */
+size_t kvq_key_stats_size(int64_t rows, int64_t T);
+size_t kvq_value_output_scores_workspace(int64_t B, int64_t n_heads, int64_t group, int64_t T);
+int kvq_key_scores_stats(const uint8_t* codes, const uint32_t* out_ent,
+                         const int32_t* out_ptr, const float* k_scale, const float* k_zero,
+                         const void* k_sink, const float* codebook, int bits, const void* q,
+                         const float* inv_freq, int64_t B, int64_t n_heads, int64_t group,
+                         int64_t T, int64_t nt_cap, float* scores, float scale, void* stats,
+                         void* stream);
+int kvq_value_output_scores(const uint8_t* codes, const uint32_t* out_ent,
+                            const int32_t* out_ptr, const float* v_scale, const float* v_zero,
+                            int64_t ld_stats, const void* v_sink, const float* codebook,
+                            int bits, const float* scores, const void* stats, float scale,
+                            int64_t B, int64_t n_heads, int64_t group, int64_t T,
+                            int64_t nt_cap, void* out, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
 /* scores -> softmax(scores / sqrt(128)) -> p.V in one call; scores_out and
- * probs_out may be NULL (then they live in the workspace). */
+ * probs_out may be NULL (then they live in the workspace). With probs_out
+ * NULL the softmax is fused (kvq_key_scores_stats + kvq_value_output_scores,
+ * two launches fewer); with probs_out set the probabilities are written by
+ * kvq_softmax. */
 size_t kvq_decode_attention_workspace(int64_t B, int64_t n_heads, int64_t group, int64_t T);
 int kvq_decode_attention(const uint8_t* k_codes, const uint32_t* k_out_ent,
                          const int32_t* k_out_ptr,

@@ -178,6 +178,10 @@ struct KeyArgs {
   const float* inv_freq;   // [64]
   int64_t B, H, G, T, nt_cap;
   float* scores;           // [B, H*G, T]
+  // optional softmax partials of softmax(scores * stat_scale): per (row,
+  // 256-token item) the max and the sum of exp(x - max), float2 [B*H*G, n_oct]
+  float2* stats;
+  float stat_scale;
   int units_per_group, n_groups;
   int64_t n_items;         // tile octets * groups
 };
@@ -508,13 +512,38 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
       __syncthreads();
     }
 
-    for (int idx = threadIdx.x; idx < nu * G * kKeyTokens; idx += blockDim.x) {
-      const int s = idx / kKeyTokens, tt = idx % kKeyTokens;
-      const int64_t t = (int64_t)tile0 * kTileTokens + tt;
-      if (t >= a.T) continue;
-      const int64_t u = u0 + s / G;
-      const int64_t b = u / a.H, h = u % a.H;
-      a.scores[(b * HG + h * G + s % G) * a.T + t] = sc[idx] * sigma[s];
+    // Scores of the item, one warp per slot (row u * G + gg = u0 * G + s), and
+    // the item's softmax partials of scores * stat_scale when asked for.
+    {
+      const int nvalid = (int)min((int64_t)kKeyTokens, a.T - (int64_t)tile0 * kTileTokens);
+      const float f = a.stat_scale;
+      for (int s = warp; s < nu * G; s += kKeyWarps) {
+        const int64_t row = (int64_t)u0 * G + s;
+        float* dst = a.scores + row * a.T + (int64_t)tile0 * kTileTokens;
+        const float sg = sigma[s];
+        float x[kKeyTokens / 32];
+#pragma unroll
+        for (int k = 0; k < kKeyTokens / 32; ++k) {
+          const int tt = lane + 32 * k;
+          x[k] = sc[s * kKeyTokens + tt] * sg;
+          if (tt < nvalid) dst[tt] = x[k];
+        }
+        if (a.stats) {
+          // the same rounding as the value kernel's (score * scale) on the stored score
+          float m = -INFINITY;
+#pragma unroll
+          for (int k = 0; k < kKeyTokens / 32; ++k) {
+            x[k] = lane + 32 * k < nvalid ? x[k] * f : -INFINITY;
+            m = fmaxf(m, x[k]);
+          }
+          m = warp_max(m);
+          float l = 0.f;
+#pragma unroll
+          for (int k = 0; k < kKeyTokens / 32; ++k) l += __expf(x[k] - m);  // exp(-inf) = 0
+          l = warp_sum(l);
+          if (lane == 0) a.stats[row * n_oct + tile0 / kKeyTiles] = make_float2(m, l);
+        }
+      }
     }
   }
 }
@@ -605,7 +634,12 @@ struct ValueArgs {
   int64_t ld;
   const __half* v_sink;    // [B, H*128] or null
   const float* cb;
-  const float* probs;      // [B, H*G, T]
+  const float* probs;      // [B, H*G, T] probabilities, or raw scores when stats is set
+  // optional: per row (M, 1/L) of softmax(scores * stat_scale), merged from
+  // the key kernel's partials; probs then holds raw scores and
+  // p = exp(score * stat_scale - M) / L is formed here
+  const float2* ml;        // [B*H*G]
+  float stat_scale;
   int64_t B, H, G, T, nt_cap;
   int n_splits;
   float* partial;          // [n_splits, B*H*G, 129]: 128 channels + zero term
@@ -614,7 +648,7 @@ struct ValueArgs {
 constexpr int kValWarps = 16;
 constexpr int kValThreads = kValWarps * 32;
 constexpr int kValMaxTiles = 2048;     // tiles per work item (row pointers sit in shared memory)
-constexpr int kValSmemLimit = 232448;  // opt-in shared memory per CTA (227 KB)
+constexpr int kValSmemLimit = 232448 - 1024;  // opt-in shared memory per CTA, less static data
 
 // max_t v_scale[b, t] for each batch row (bounds every weight p_t * s_t).
 // grid = (chunks of the token axis, B); out[b] starts at 0 and takes the
@@ -634,6 +668,61 @@ __global__ void __launch_bounds__(256) row_max_kernel(const float* __restrict__ 
     m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
     m = warp_max(m);
     if (threadIdx.x == 0) atomicMax(reinterpret_cast<int*>(out + b), __float_as_int(m));
+  }
+}
+
+// (max, sum of exp(x - max)) pairs merged: the pair of the union.
+__device__ __forceinline__ float2 ml_merge(float2 a, float2 b) {
+  const float m = fmaxf(a.x, b.x);
+  if (m == -INFINITY) return a;
+  return make_float2(m, a.y * __expf(a.x - m) + b.y * __expf(b.x - m));
+}
+
+// row_max_kernel for blockIdx.y < B; blocks with y >= B merge the key
+// kernel's softmax partials stats[row, 0..n_oct) into ml[row] = (M, 1/L).
+__global__ void __launch_bounds__(256) value_prep_kernel(const float* __restrict__ vs, int64_t T,
+                                                         int64_t ld, float* __restrict__ out,
+                                                         int64_t B,
+                                                         const float2* __restrict__ stats,
+                                                         int n_oct, int64_t rows,
+                                                         float2* __restrict__ ml) {
+  __shared__ float red[8];
+  __shared__ float2 red2[8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if ((int64_t)blockIdx.y < B) {
+    const int64_t b = blockIdx.y;
+    const int64_t s0 = (int64_t)blockIdx.x * kRowMaxChunk, s1 = min(T, s0 + kRowMaxChunk);
+    float m = 0.f;
+    for (int64_t t = s0 + threadIdx.x; t < s1; t += blockDim.x) m = fmaxf(m, vs[b * ld + t]);
+    m = warp_max(m);
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+      m = warp_max(m);
+      if (threadIdx.x == 0) atomicMax(reinterpret_cast<int*>(out + b), __float_as_int(m));
+    }
+    return;
+  }
+  const int64_t nb = (int64_t)gridDim.x * (gridDim.y - B);
+  for (int64_t r = blockIdx.x + (int64_t)gridDim.x * (blockIdx.y - B); r < rows; r += nb) {
+    float2 acc = make_float2(-INFINITY, 0.f);
+    for (int k = threadIdx.x; k < n_oct; k += blockDim.x) acc = ml_merge(acc, stats[r * n_oct + k]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float2 other;
+      other.x = __shfl_xor_sync(0xffffffffu, acc.x, o);
+      other.y = __shfl_xor_sync(0xffffffffu, acc.y, o);
+      acc = ml_merge(acc, other);
+    }
+    if (lane == 0) red2[warp] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float2 t = red2[0];
+      for (int w = 1; w < (int)(blockDim.x >> 5); ++w) t = ml_merge(t, red2[w]);
+      ml[r] = make_float2(t.x, 1.f / t.y);
+    }
+    __syncthreads();
   }
 }
 
@@ -706,6 +795,9 @@ __global__ void __launch_bounds__(kValThreads, 1)
   const float inv_e = 1.f / e_scale;
   for (int k = threadIdx.x; k <= tb - ta; k += blockDim.x)
     tptr[k] = __ldg(a.out_ptr + 2 * (u * a.nt_cap + ta + k));
+  // Softmax of raw scores: (M, 1/L) of each head of the unit.
+  __shared__ float2 s_ml[8];
+  if (a.ml && threadIdx.x < G) s_ml[threadIdx.x] = a.ml[b * HG + h * G + threadIdx.x];
   __syncthreads();
 
   float d[8][4];
@@ -768,9 +860,15 @@ __global__ void __launch_bounds__(kValThreads, 1)
     // fp32 registers.
     {
       const float2 szl = sz[lane];
+      const int tok = (ta + warp + i * kValWarps) * kTileTokens + lane;
+      const bool live = tok < T && !(sink && tok == 0);
 #pragma unroll
       for (int hd = 0; hd < G; ++hd) {
-        const float p = fp[hd * S::kPRow + lane];
+        float p = fp[hd * S::kPRow + lane];
+        if (a.ml) {  // raw score -> probability, in place for the outlier path
+          p = live ? __expf(p * a.stat_scale - s_ml[hd].x) * s_ml[hd].y : 0.f;
+          const_cast<float*>(fp)[hd * S::kPRow + lane] = p;
+        }
         zs[hd] = fmaf(p, szl.y, zs[hd]);
         wbuf[hd * 32 + lane] = __float2half_rn(p * szl.x * e_scale);
       }
@@ -821,8 +919,9 @@ __global__ void __launch_bounds__(kValThreads, 1)
   if (sink && ta == 0) {
     for (int idx = threadIdx.x; idx < G * kHeadDim; idx += blockDim.x) {
       const int hd = idx / kHeadDim, dd = idx % kHeadDim;
-      atomicAdd(acc + hd * kHeadDim + dd,
-                prow[hd * a.T] * __half2float(a.v_sink[(b * a.H + h) * kHeadDim + dd]));
+      float p0 = prow[hd * a.T];
+      if (a.ml) p0 = __expf(p0 * a.stat_scale - s_ml[hd].x) * s_ml[hd].y;
+      atomicAdd(acc + hd * kHeadDim + dd, p0 * __half2float(a.v_sink[(b * a.H + h) * kHeadDim + dd]));
     }
   }
   __syncthreads();  // all warps are done with their rings and accumulators
@@ -1008,12 +1107,17 @@ inline size_t value_ws(int64_t B, int64_t H, int64_t G, int64_t T) {
   return align256((size_t)value_splits(U, nt, G) * U * G * 129 * sizeof(float)) +
          align256((size_t)B * sizeof(float));
 }
+// ... of the raw-score variant: plus the merged (M, 1/L) per row.
+inline size_t value_scores_ws(int64_t B, int64_t H, int64_t G, int64_t T) {
+  return value_ws(B, H, G, T) + align256((size_t)(B * H * G > 0 ? B * H * G : 0) * sizeof(float2));
+}
 
 static int value_impl(const uint8_t* codes, const uint32_t* out_ent, const int32_t* out_ptr,
                       const float* v_scale, const float* v_zero, int64_t ld_stats,
                       const void* v_sink, const float* codebook, int bits, const float* probs,
                       int64_t B, int64_t H, int64_t G, int64_t T, int64_t nt_cap, void* out,
-                      void* workspace, size_t workspace_bytes, cudaStream_t st) {
+                      void* workspace, size_t workspace_bytes, cudaStream_t st,
+                      const float2* stats = nullptr, float stat_scale = 0.f) {
   int rc = check_decode_shape("value_output", B, H, G, T, nt_cap);
   if (rc) return rc;
   if (ld_stats < T) {
@@ -1024,7 +1128,8 @@ static int value_impl(const uint8_t* codes, const uint32_t* out_ent, const int32
   const int64_t nt = (T + kTileTokens - 1) / kTileTokens;
   const int n_splits = value_splits(U, nt, G);
   const size_t part_bytes = align256((size_t)n_splits * U * G * 129 * sizeof(float));
-  const size_t need = part_bytes + align256((size_t)B * sizeof(float));
+  const size_t need = stats ? value_scores_ws(B, H, G, T)
+                            : part_bytes + align256((size_t)B * sizeof(float));
   if (!workspace || workspace_bytes < need) {
     set_error("value_output: workspace too small (%zu < %zu)", workspace_bytes, need);
     return KVQ_ERR_INVALID;
@@ -1034,11 +1139,29 @@ static int value_impl(const uint8_t* codes, const uint32_t* out_ent, const int32
   a.v_zero = v_zero; a.ld = ld_stats; a.v_sink = (const __half*)v_sink; a.cb = codebook;
   a.probs = probs; a.B = B; a.H = H; a.G = G; a.T = T; a.nt_cap = nt_cap;
   a.n_splits = n_splits;
+  a.stat_scale = stat_scale;
   a.partial = reinterpret_cast<float*>(workspace);
   float* row_max = reinterpret_cast<float*>((char*)workspace + part_bytes);
   cudaMemsetAsync(row_max, 0, (size_t)B * sizeof(float), st);
-  row_max_kernel<<<dim3((unsigned)((T + kRowMaxChunk - 1) / kRowMaxChunk), (unsigned)B), 256, 0, st>>>(
-      v_scale, T, ld_stats, row_max);
+  const unsigned n_chunks = (unsigned)((T + kRowMaxChunk - 1) / kRowMaxChunk);
+  if (stats) {
+    // one launch: the row maxima and the merge of the key kernel's partials
+    float2* ml = reinterpret_cast<float2*>((char*)workspace + part_bytes +
+                                           align256((size_t)B * sizeof(float)));
+    a.ml = ml;
+    const int64_t rows = U * G;
+    const int n_oct = (int)((nt + kKeyTiles - 1) / kKeyTiles);
+    if (B >= 65535) {
+      set_error("value_output_scores: batch %lld leaves no grid rows for the softmax merge",
+                (long long)B);
+      return KVQ_ERR_INVALID;
+    }
+    const int64_t merge_y = min((rows + n_chunks - 1) / n_chunks, (int64_t)65535 - B);
+    value_prep_kernel<<<dim3(n_chunks, (unsigned)(B + merge_y)), 256, 0, st>>>(
+        v_scale, T, ld_stats, row_max, B, stats, n_oct, rows, ml);
+  } else {
+    row_max_kernel<<<dim3(n_chunks, (unsigned)B), 256, 0, st>>>(v_scale, T, ld_stats, row_max);
+  }
   switch (G) {
     case 1: rc = dispatch_value_bits<1>(bits, a, row_max, st); break;
     case 2: rc = dispatch_value_bits<2>(bits, a, row_max, st); break;
@@ -1052,9 +1175,17 @@ static int value_impl(const uint8_t* codes, const uint32_t* out_ent, const int32
   return check_launch("value_output");
 }
 
-// Workspace of decode_attention: [scores][probs][softmax partials][value partials].
+// Softmax partials of the key kernel: float2 [rows, n_oct] (n_oct = 256-token items).
+inline int64_t key_items(int64_t T) {
+  return ((T + kTileTokens - 1) / kTileTokens + kKeyTiles - 1) / kKeyTiles;
+}
+inline size_t stats_ws(int64_t rows, int64_t T) {
+  return align256((size_t)(rows > 0 ? rows : 0) * key_items(T > 0 ? T : 0) * sizeof(float2));
+}
+
+// Workspace of decode_attention: [scores][probs][softmax partials][value partials][key stats].
 struct DecodeWs {
-  size_t scores, probs, soft, value, total;
+  size_t scores, probs, soft, value, stats, total;
 };
 inline DecodeWs decode_ws(int64_t B, int64_t H, int64_t G, int64_t T) {
   DecodeWs w;
@@ -1062,20 +1193,20 @@ inline DecodeWs decode_ws(int64_t B, int64_t H, int64_t G, int64_t T) {
   w.scores = align256((size_t)rows * T * sizeof(float));
   w.probs = w.scores;
   w.soft = softmax_ws(rows, T);
-  w.value = value_ws(B, H, G, T);
-  w.total = w.scores + w.probs + w.soft + w.value;
+  w.value = value_scores_ws(B, H, G, T);  // room for either variant
+  w.stats = stats_ws(rows, T);
+  w.total = w.scores + w.probs + w.soft + w.value + w.stats;
   return w;
 }
 
 }  // namespace kvq
 
-extern "C" int kvq_key_scores(const uint8_t* codes, const uint32_t* out_ent,
-                              const int32_t* out_ptr, const float* k_scale, const float* k_zero,
-                              const void* k_sink, const float* codebook, int bits, const void* q,
-                              const float* inv_freq, int64_t B, int64_t n_heads, int64_t group,
-                              int64_t T, int64_t nt_cap, float* scores, void* stream) {
-  using namespace kvq;
-  clear_error();
+namespace kvq {
+static int key_impl(const uint8_t* codes, const uint32_t* out_ent, const int32_t* out_ptr,
+                    const float* k_scale, const float* k_zero, const void* k_sink,
+                    const float* codebook, int bits, const void* q, const float* inv_freq,
+                    int64_t B, int64_t n_heads, int64_t group, int64_t T, int64_t nt_cap,
+                    float* scores, float2* stats, float stat_scale, cudaStream_t st) {
   int rc = check_decode_shape("key_scores", B, n_heads, group, T, nt_cap);
   if (rc) return rc;
   KeyArgs a{};
@@ -1083,7 +1214,8 @@ extern "C" int kvq_key_scores(const uint8_t* codes, const uint32_t* out_ent,
   a.k_zero = k_zero; a.k_sink = (const __half*)k_sink; a.cb = codebook; a.q = (const __half*)q;
   a.inv_freq = inv_freq; a.B = B; a.H = n_heads; a.G = group; a.T = T; a.nt_cap = nt_cap;
   a.scores = scores;
-  cudaStream_t st = as_stream(stream);
+  a.stats = stats;
+  a.stat_scale = stat_scale;
   switch (group) {
     case 1: return dispatch_key_bits<1>(bits, a, st);
     case 2: return dispatch_key_bits<2>(bits, a, st);
@@ -1091,6 +1223,40 @@ extern "C" int kvq_key_scores(const uint8_t* codes, const uint32_t* out_ent,
     case 8: return dispatch_key_bits<8>(bits, a, st);
   }
   return KVQ_ERR_UNSUPPORTED;
+}
+}  // namespace kvq
+
+extern "C" int kvq_key_scores(const uint8_t* codes, const uint32_t* out_ent,
+                              const int32_t* out_ptr, const float* k_scale, const float* k_zero,
+                              const void* k_sink, const float* codebook, int bits, const void* q,
+                              const float* inv_freq, int64_t B, int64_t n_heads, int64_t group,
+                              int64_t T, int64_t nt_cap, float* scores, void* stream) {
+  kvq::clear_error();
+  return kvq::key_impl(codes, out_ent, out_ptr, k_scale, k_zero, k_sink, codebook, bits, q,
+                       inv_freq, B, n_heads, group, T, nt_cap, scores, nullptr, 0.f,
+                       kvq::as_stream(stream));
+}
+
+extern "C" size_t kvq_key_stats_size(int64_t rows, int64_t T) {
+  if (rows <= 0 || T <= 0) return 0;
+  return (size_t)rows * kvq::key_items(T) * sizeof(float2);
+}
+
+extern "C" int kvq_key_scores_stats(const uint8_t* codes, const uint32_t* out_ent,
+                                    const int32_t* out_ptr, const float* k_scale,
+                                    const float* k_zero, const void* k_sink,
+                                    const float* codebook, int bits, const void* q,
+                                    const float* inv_freq, int64_t B, int64_t n_heads,
+                                    int64_t group, int64_t T, int64_t nt_cap, float* scores,
+                                    float scale, void* stats, void* stream) {
+  kvq::clear_error();
+  if (!stats) {
+    kvq::set_error("key_scores_stats: stats is NULL");
+    return KVQ_ERR_INVALID;
+  }
+  return kvq::key_impl(codes, out_ent, out_ptr, k_scale, k_zero, k_sink, codebook, bits, q,
+                       inv_freq, B, n_heads, group, T, nt_cap, scores,
+                       reinterpret_cast<float2*>(stats), scale, kvq::as_stream(stream));
 }
 
 extern "C" size_t kvq_softmax_workspace(int64_t rows, int64_t T) {
@@ -1122,6 +1288,30 @@ extern "C" int kvq_value_output(const uint8_t* codes, const uint32_t* out_ent,
                          workspace_bytes, kvq::as_stream(stream));
 }
 
+extern "C" size_t kvq_value_output_scores_workspace(int64_t B, int64_t n_heads, int64_t group,
+                                                    int64_t T) {
+  return kvq::value_scores_ws(B, n_heads, group, T);
+}
+
+extern "C" int kvq_value_output_scores(const uint8_t* codes, const uint32_t* out_ent,
+                                       const int32_t* out_ptr, const float* v_scale,
+                                       const float* v_zero, int64_t ld_stats, const void* v_sink,
+                                       const float* codebook, int bits, const float* scores,
+                                       const void* stats, float scale, int64_t B,
+                                       int64_t n_heads, int64_t group, int64_t T, int64_t nt_cap,
+                                       void* out, void* workspace, size_t workspace_bytes,
+                                       void* stream) {
+  kvq::clear_error();
+  if (!stats) {
+    kvq::set_error("value_output_scores: stats is NULL");
+    return KVQ_ERR_INVALID;
+  }
+  return kvq::value_impl(codes, out_ent, out_ptr, v_scale, v_zero, ld_stats, v_sink, codebook,
+                         bits, scores, B, n_heads, group, T, nt_cap, out, workspace,
+                         workspace_bytes, kvq::as_stream(stream),
+                         reinterpret_cast<const float2*>(stats), scale);
+}
+
 extern "C" size_t kvq_decode_attention_workspace(int64_t B, int64_t n_heads, int64_t group,
                                                  int64_t T) {
   return kvq::decode_ws(B, n_heads, group, T).total;
@@ -1149,12 +1339,23 @@ extern "C" int kvq_decode_attention(
   float* probs = probs_out ? probs_out : reinterpret_cast<float*>(ws + w.scores);
   void* soft = ws + w.scores + w.probs;
   void* val = ws + w.scores + w.probs + w.soft;
-  rc = kvq_key_scores(k_codes, k_out_ent, k_out_ptr, k_scale, k_zero, k_sink, k_codebook, bits,
-                      q, inv_freq, B, n_heads, group, T, nt_cap, scores, stream);
-  if (rc) return rc;
+  float2* stats = reinterpret_cast<float2*>(ws + w.scores + w.probs + w.soft + w.value);
+  const float scale = 0.08838834764831845f;  // 1 / sqrt(128)
   cudaStream_t st = as_stream(stream);
-  rc = softmax_impl(scores, B * n_heads * group, T, 0.08838834764831845f /* 1/sqrt(128) */,
-                    probs, soft, w.soft, st);
+  if (!probs_out) {
+    // fused softmax: the key kernel leaves per-item partials, the value kernel
+    // turns the raw scores into probabilities itself
+    rc = key_impl(k_codes, k_out_ent, k_out_ptr, k_scale, k_zero, k_sink, k_codebook, bits, q,
+                  inv_freq, B, n_heads, group, T, nt_cap, scores, stats, scale, st);
+    if (rc) return rc;
+    return value_impl(v_codes, v_out_ent, v_out_ptr, v_scale, v_zero, ld_stats, v_sink,
+                      v_codebook, bits, scores, B, n_heads, group, T, nt_cap, out, val, w.value,
+                      st, stats, scale);
+  }
+  rc = key_impl(k_codes, k_out_ent, k_out_ptr, k_scale, k_zero, k_sink, k_codebook, bits, q,
+                inv_freq, B, n_heads, group, T, nt_cap, scores, nullptr, 0.f, st);
+  if (rc) return rc;
+  rc = softmax_impl(scores, B * n_heads * group, T, scale, probs, soft, w.soft, st);
   if (rc) return rc;
   return value_impl(v_codes, v_out_ent, v_out_ptr, v_scale, v_zero, ld_stats, v_sink, v_codebook,
                     bits, probs, B, n_heads, group, T, nt_cap, out, val, w.value, st);

@@ -2,8 +2,8 @@
 from .rope_fused import apply_rope_elementwise, apply_rope_inplace, rope_inv_freq
 from .matvec_ds import dense_matvec_lut, sparse_matvec, sparse_matvec_csr
 from .cuda_ops import get_cuda_ops, cuda_available
-from .decode import (quantize_keys, quantize_values, qk_scores, softmax, pv_out,
-                     decode_attention)
+from .decode import (quantize_keys, quantize_values, qk_scores, qk_scores_stats, softmax,
+                     pv_out, pv_out_scores, decode_attention)
 
 __all__ = [
     "apply_rope_elementwise",
@@ -17,7 +17,9 @@ __all__ = [
     "quantize_keys",
     "quantize_values",
     "qk_scores",
+    "qk_scores_stats",
     "softmax",
     "pv_out",
+    "pv_out_scores",
     "decode_attention",
 ]

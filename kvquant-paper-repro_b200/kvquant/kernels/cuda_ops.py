@@ -59,6 +59,14 @@ _SIGNATURES = {
                                           _c_size, _c_p]),
     "kvq_key_scores": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_int, _c_p,
                                 _c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p]),
+    "kvq_key_stats_size": (_c_size, [_c_i64, _c_i64]),
+    "kvq_value_output_scores_workspace": (_c_size, [_c_i64, _c_i64, _c_i64, _c_i64]),
+    "kvq_key_scores_stats": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_int, _c_p,
+                                      _c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_flt,
+                                      _c_p, _c_p]),
+    "kvq_value_output_scores": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p, _c_p,
+                                         _c_int, _c_p, _c_p, _c_flt, _c_i64, _c_i64, _c_i64,
+                                         _c_i64, _c_i64, _c_p, _c_p, _c_size, _c_p]),
     "kvq_softmax_workspace": (_c_size, [_c_i64, _c_i64]),
     "kvq_softmax": (_c_int, [_c_p, _c_i64, _c_i64, _c_flt, _c_p, _c_p, _c_size, _c_p]),
     "kvq_value_output_workspace": (_c_size, [_c_i64, _c_i64, _c_i64, _c_i64]),

@@ -18,7 +18,7 @@ import math
 
 import torch
 
-from .cuda_ops import _check, _ptr, _stream, get_cuda_ops
+from .cuda_ops import _check, _ptr, _stream, ceil_div, get_cuda_ops
 
 TILE_TOKENS = 32
 HEAD_DIM = 128
@@ -213,6 +213,75 @@ def pv_out(probs: torch.Tensor, packed_v: dict, length: int | None = None) -> to
                                     packed_v["bits"], _ptr(p), B, H, G, T,
                                     packed_v["q_idx"].shape[1], _ptr(out), _ptr(ws), ws.numel(),
                                     _stream(p)), lib)
+    return out
+
+
+def qk_scores_stats(q: torch.Tensor, packed_k: dict, inv_freq: torch.Tensor,
+                    length: int | None = None, scale: float | None = None,
+                    out: torch.Tensor | None = None, stats_out: torch.Tensor | None = None):
+    """qk_scores plus the key kernel's softmax partials of softmax(scores * scale).
+
+    Returns (scores fp32 [B, Hq, T], stats fp32 [B*Hq, ceil(T/256), 2]) where
+    stats[row, k] = (max over the k-th 256-token chunk of scores * scale,
+    sum over that chunk of exp(scores * scale - max)). pv_out_scores turns the
+    pair back into the softmax of the whole row.
+    """
+    lib = get_cuda_ops().lib
+    qc = q.to(torch.float16).contiguous()
+    G = _group(qc, packed_k)
+    T = int(length or packed_k["length"])
+    B, Hq, _ = qc.shape
+    scale = 1.0 / math.sqrt(HEAD_DIM) if scale is None else float(scale)
+    f = inv_freq.to(qc.device, torch.float32).contiguous()
+    scores = out if out is not None else torch.empty((B, Hq, T), dtype=torch.float32,
+                                                      device=qc.device)
+    n_chunks = ceil_div(T, 256)
+    if lib.kvq_key_stats_size(B * Hq, T) != B * Hq * n_chunks * 8:
+        raise RuntimeError("qk_scores_stats: library disagrees on the stats size")
+    stats = stats_out if stats_out is not None else torch.empty(
+        (B * Hq, n_chunks, 2), dtype=torch.float32, device=qc.device)
+    if (scores.shape != (B, Hq, T) or scores.dtype != torch.float32
+            or not scores.is_contiguous() or stats.numel() != B * Hq * n_chunks * 2
+            or stats.dtype != torch.float32 or not stats.is_contiguous()):
+        raise RuntimeError("qk_scores_stats: out / stats_out do not match the shapes")
+    with torch.cuda.device(qc.device):
+        _check(lib.kvq_key_scores_stats(
+            _ptr(packed_k["q_idx"]), _ptr(packed_k["outlier_entries"]),
+            _ptr(packed_k["outlier_rowptr"]), _ptr(packed_k["scale"]), _ptr(packed_k["zero"]),
+            _ptr(packed_k["sink"]), _ptr(packed_k["codebook"]), packed_k["bits"], _ptr(qc),
+            _ptr(f), B, packed_k["n_heads"], G, T, packed_k["q_idx"].shape[1], _ptr(scores),
+            scale, _ptr(stats), _stream(qc)), lib)
+    return scores, stats
+
+
+def pv_out_scores(scores: torch.Tensor, stats: torch.Tensor, packed_v: dict,
+                  scale: float | None = None) -> torch.Tensor:
+    """Value kernel on raw scores: sum_t softmax(scores * scale)[t] * Vhat_t, fp16 [B, Hq, 128].
+
+    `stats` comes from qk_scores_stats with the same scale.
+    """
+    lib = get_cuda_ops().lib
+    s = scores.contiguous()
+    if s.dtype != torch.float32:
+        raise RuntimeError("pv_out_scores: scores must be fp32")
+    B, Hq, T = s.shape
+    H = packed_v["n_heads"]
+    if B != packed_v["batch"] or Hq % H:
+        raise RuntimeError("pv_out_scores: scores do not match the value cache")
+    G = Hq // H
+    scale = 1.0 / math.sqrt(HEAD_DIM) if scale is None else float(scale)
+    st = stats.contiguous()
+    if st.dtype != torch.float32 or st.numel() * 4 != lib.kvq_key_stats_size(B * Hq, T):
+        raise RuntimeError("pv_out_scores: stats do not match the scores")
+    out = torch.empty((B, Hq, HEAD_DIM), dtype=torch.float16, device=s.device)
+    with torch.cuda.device(s.device):
+        ws = _workspace(lib.kvq_value_output_scores_workspace(B, H, G, T), s.device)
+        _check(lib.kvq_value_output_scores(
+            _ptr(packed_v["q_idx"]), _ptr(packed_v["outlier_entries"]),
+            _ptr(packed_v["outlier_rowptr"]), _ptr(packed_v["scale"]), _ptr(packed_v["zero"]),
+            packed_v["scale"].shape[1], _ptr(packed_v["sink"]), _ptr(packed_v["codebook"]),
+            packed_v["bits"], _ptr(s), _ptr(st), scale, B, H, G, T, packed_v["q_idx"].shape[1],
+            _ptr(out), _ptr(ws), ws.numel(), _stream(s)), lib)
     return out
 
 
