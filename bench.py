@@ -186,9 +186,10 @@ def build_cache(wl, layers, h0, hl, dev, log):
 
 # DRAM bytes (ncu dram__bytes_read.sum + dram__bytes_write.sum) per algorithmic
 # byte of each decode kernel, from one capture of the 4-bit 1%-outlier workload
-# at 262144 tokens x 32 KV heads (traffic grows in proportion to the tokens).
-DRAM_PER_ALGORITHMIC_BYTE = {"key_scores": 617608960 / 615514116,
-                             "value_output": 622571776 / 608190336}
+# at 262144 tokens x 32 KV heads, fused softmax (traffic grows in proportion to
+# the tokens).
+DRAM_PER_ALGORITHMIC_BYTE = {"key_scores": 618100480 / 615776256,
+                             "value_output": 622502400 / 608452480}
 
 
 def bench_config(wl, layers, world):
@@ -375,6 +376,7 @@ def run_gpu(args):
                          "bytes_per_launch": ab[dom], "launch_ms": dom_ms},
             "step_bandwidth_gbs": step_bytes / (ms_step / 1e3) / 1e9,
             "kernels_ms": {"key_scores": k_avg, "value_output": v_avg},
+            "algorithmic_bytes_per_launch": ab,
             "cpu_baseline": cpu,
             "quantize_append": qstat,
             "e2e": e2e,
