@@ -118,7 +118,12 @@ def fit_codebooks(k: torch.Tensor, v: torch.Tensor, k_scale: torch.Tensor, k_zer
         if x.numel() > n_samples:
             idx = torch.randperm(x.numel(), generator=g)[:n_samples]
             x, wt = x[idx], wt[idx]
-        out.append(train_nuq_codebook(x, wt, n_bits=bits))
+        # one solver thread: the multi-threaded k-means reductions round
+        # differently from run to run, and the synthetic model's codebooks
+        # (hence every cached code) should be the same in every process
+        from threadpoolctl import threadpool_limits
+        with threadpool_limits(limits=1):
+            out.append(train_nuq_codebook(x, wt, n_bits=bits))
     return out[0], out[1]
 
 
