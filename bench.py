@@ -50,6 +50,7 @@ def parse():
     ap.add_argument("--tokens", type=int, default=None, help="override the cached token count")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-append", action="store_true")
     return ap.parse_args()
 
 
@@ -182,6 +183,42 @@ def build_cache(wl, layers, h0, hl, dev, log):
                  "what": "quantize_keys + quantize_values of one layer's prefill block "
                          "(plan + emit, outliers, packing), CUDA events"}
     return cache, qstat
+
+
+def measure_decode_append(wl, h0, hl, dev, cbk, cbv, log, T0=4096, steps=32):
+    """Decode-time append of one token (keys + values) into an appendable cache of
+    this rank's heads: CUDA-event time per token and layer (O(1) in the length)."""
+    import torch
+    from kvquant import synthetic as syn
+    from kvquant.kernels import (quantize_keys, quantize_values, make_appendable, append_keys,
+                                 append_values, key_outlier_thresholds)
+
+    B, C = wl.batch, wl.channels
+    k = torch.empty((B, T0 + steps + 3, C), dtype=torch.float16, device=dev)
+    v = torch.empty_like(k)
+    syn.fill_layer(k, v, 0, seed=1)
+    ks, kz = syn.key_calibration(k[:, :T0])
+    pk = make_appendable(quantize_keys(k[:, :T0], ks, kz, cbk, wl.bits, wl.outlier_ratio, True,
+                                       h0=h0, n_heads=hl), steps + 3)
+    pv = make_appendable(quantize_values(v[:, :T0], cbv, wl.bits, wl.outlier_ratio, True,
+                                         h0=h0, n_heads=hl), steps + 3)
+    thr = key_outlier_thresholds(k[:, :T0], ks, kz, wl.outlier_ratio, h0=h0, n_heads=hl)
+    rows = [(k[:, t:t + 1].contiguous(), v[:, t:t + 1].contiguous()) for t in range(T0, T0 + steps + 3)]
+    for kt, vt in rows[:3]:
+        append_keys(pk, kt, thr)
+        append_values(pv, vt)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for kt, vt in rows[3:]:
+        append_keys(pk, kt, thr, check=False)
+        append_values(pv, vt, check=False)
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / steps
+    log(f"decode append: {us:.1f} us per token and layer")
+    return {"us_per_token_per_layer": us, "cached_tokens": T0, "kv_heads": hl,
+            "what": "append_keys (calibrated thresholds) + append_values of one new token "
+                    "into an appendable cache, CUDA events over 32 consecutive tokens"}
 
 
 # DRAM bytes (ncu dram__bytes_read.sum + dram__bytes_write.sum) per algorithmic
@@ -350,6 +387,11 @@ def run_gpu(args):
                "h2d_bytes_per_step": sum(q.numel() * 2 for q in qs),
                "d2h_bytes_per_step": layers * world * wl.batch * Hq_l * 128 * 2}
 
+    append_stat = None
+    if not args.no_append:
+        append_stat = measure_decode_append(wl, h0, hl, dev, cache[0][0]["codebook"],
+                                            cache[0][1]["codebook"], log)
+
     # roofline of the dominant kernel
     pk0, pv0 = cache[0]
     ab = algorithmic_bytes(wl, pk0, pv0, hl, T)
@@ -379,6 +421,7 @@ def run_gpu(args):
             "algorithmic_bytes_per_launch": ab,
             "cpu_baseline": cpu,
             "quantize_append": qstat,
+            "decode_append": append_stat,
             "e2e": e2e,
             "gpu_launches": n_launch_per_layer * layers * args.steps,
             "clocks": clk,

@@ -130,6 +130,45 @@ int kvq_quantize_values_emit(const void* v, int64_t B, int64_t S, int64_t C_full
                              void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Decode-time append: quantizes S_new new tokens [B, S_new, C_full] fp16 into
+ * an existing cache holding T_old >= 1 tokens, at positions T_old.. . The
+ * reference re-runs quantize_k / quantize_v on each new block through its
+ * k_proj / v_proj hooks (kvquant/attention_patch.py:22-35); these calls keep
+ * that per-step semantics for values and give keys the calibrated-threshold
+ * outliers of the KVQuant paper (section 3.4), O(S_new) work per call.
+ *
+ * Layout requirements (kvquant.kernels.make_appendable builds them): a spare
+ * tile after the last token (T_old + S_new <= (nt_cap - 1) * 32), and per-unit
+ * outlier segments: unit u owns entries [u*ent_stride, (u+1)*ent_stride) and
+ * its row pointers address that range. A unit whose segment cannot take the
+ * new outliers is left untouched and bit 0 of *status (a device int32) is set;
+ * the caller clears *status and reads it after the call.
+ * ------------------------------------------------------------------------- */
+
+/* Keys (kv_quantizer.py:72-94 with per-channel thresholds): n = (k - zero) /
+ * (scale + 1e-8); |n| >= thresholds[c] is an outlier (fp16 entry, dense part
+ * 0), the rest is clamped to [-1, 1] and coded by the first nearest centroid.
+ * scale, zero and thresholds are fp32 [n_heads*128], the cache's own channels
+ * (heads h0.. of k_new); thresholds NULL = no outliers. thresholds = 0 makes
+ * every channel an outlier: the reference's quantize_k on a one-token block. */
+int kvq_append_keys(const void* k_new, int64_t B, int64_t S_new, int64_t C_full, int64_t h0,
+                    int64_t n_heads, const float* scale, const float* zero,
+                    const float* thresholds, const float* codebook, int bits, int64_t T_old,
+                    uint8_t* codes, int64_t nt_cap, int32_t* out_ptr, uint32_t* out_ent,
+                    int64_t ent_stride, int32_t* status, void* stream);
+
+/* Values (kv_quantizer.py:96-122, each new token as a one-token call: no
+ * sink): writes v_scale / v_zero [B, ld_stats] at positions T_old.., codes and
+ * entries. Workspace: kvq_append_values_workspace(B, S_new) bytes. */
+size_t kvq_append_values_workspace(int64_t B, int64_t S_new);
+int kvq_append_values(const void* v_new, int64_t B, int64_t S_new, int64_t C_full, int64_t h0,
+                      int64_t n_heads, double outlier_ratio, const float* codebook, int bits,
+                      int64_t T_old, float* v_scale, float* v_zero, int64_t ld_stats,
+                      uint8_t* codes, int64_t nt_cap, int32_t* out_ptr, uint32_t* out_ent,
+                      int64_t ent_stride, void* workspace, size_t workspace_bytes,
+                      int32_t* status, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Decode attention over the packed cache (T cached tokens at positions
  * 0..T-1, token 0 = sink). q fp16 [B, n_heads*group, 128] (already rotated
  * to its own position); query head hq reads KV head hq / group.

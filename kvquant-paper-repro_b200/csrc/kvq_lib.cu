@@ -4,5 +4,6 @@
 #include "kvq_runtime.cuh"
 #include "kvq_ref_ops.cuh"
 #include "kvq_quantize.cuh"
+#include "kvq_append.cuh"
 #include "kvq_decode.cuh"
 #include "kvq_noalloc.cuh"

@@ -3,7 +3,8 @@ from .rope_fused import apply_rope_elementwise, apply_rope_inplace, rope_inv_fre
 from .matvec_ds import dense_matvec_lut, sparse_matvec, sparse_matvec_csr
 from .cuda_ops import get_cuda_ops, cuda_available
 from .decode import (quantize_keys, quantize_values, qk_scores, qk_scores_stats, softmax,
-                     pv_out, pv_out_scores, decode_attention)
+                     pv_out, pv_out_scores, decode_attention, make_appendable, append_keys,
+                     append_values, key_outlier_thresholds)
 
 __all__ = [
     "apply_rope_elementwise",
@@ -22,4 +23,8 @@ __all__ = [
     "pv_out",
     "pv_out_scores",
     "decode_attention",
+    "make_appendable",
+    "append_keys",
+    "append_values",
+    "key_outlier_thresholds",
 ]

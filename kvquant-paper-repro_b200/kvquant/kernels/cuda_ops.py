@@ -76,6 +76,13 @@ _SIGNATURES = {
     "kvq_value_output_noalloc": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p, _c_p,
                                           _c_int, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                                           _c_p, _c_p]),
+    "kvq_append_keys": (_c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p,
+                                 _c_p, _c_int, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p,
+                                 _c_p]),
+    "kvq_append_values_workspace": (_c_size, [_c_i64, _c_i64]),
+    "kvq_append_values": (_c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_dbl, _c_p,
+                                   _c_int, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p,
+                                   _c_i64, _c_p, _c_size, _c_p, _c_p]),
     "kvq_decode_attention_workspace": (_c_size, [_c_i64, _c_i64, _c_i64, _c_i64]),
     "kvq_decode_attention": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
                                       _c_p, _c_p, _c_p, _c_i64, _c_p, _c_p, _c_int, _c_p,

@@ -9,6 +9,10 @@ qk_scores
     Fused key kernel: packed codes -> LUT -> outliers -> RoPE -> q.K.
 softmax, pv_out, decode_attention
     Softmax over tokens, value kernel (p.V), and the whole decode step.
+make_appendable, append_keys, append_values, key_outlier_thresholds
+    Decode-time append of new tokens into a packed cache (O(new tokens) per
+    call): values exactly as one-token calls of quantize_v, keys with
+    calibrated per-channel outlier thresholds.
 
 All tensors are CUDA tensors; work is launched on the current stream.
 """
@@ -119,11 +123,13 @@ def _quantize(kind: str, x: torch.Tensor, codebook: torch.Tensor, bits: int,
         "bits": int(bits),
         "kind": kind,
         "batch": B,
+        "C_full": C_full,
         "n_heads": H,
         "h0": int(h0),
         "length": S,
         "capacity": nt_cap * TILE_TOKENS,
         "nnz": nnz,
+        "outlier_ratio": float(outlier_ratio),
     }
     if dequant:
         packed["dequant"] = deq
@@ -328,3 +334,178 @@ def decode_attention(q: torch.Tensor, packed_k: dict, packed_v: dict, inv_freq: 
             B, H, G, T, packed_k["q_idx"].shape[1], _ptr(o), _ptr(scores_out), _ptr(probs_out),
             _ptr(ws), ws.numel(), _stream(qc)), lib)
     return o
+
+
+# ---------------------------------------------------------------------------
+# Decode-time append
+# ---------------------------------------------------------------------------
+def make_appendable(packed: dict, extra_tokens: int,
+                    entries_per_token: int | None = None) -> dict:
+    """Copy of a packed cache laid out for appending up to `extra_tokens` tokens.
+
+    The prefill layout packs every unit's outlier entries back to back, so a
+    unit's CSR rows cannot grow. This copy gives each unit (b, head) its own
+    entry segment of `ent_stride` entries (its current entries plus
+    extra_tokens * entries_per_token free slots) and one spare code tile after
+    the last appendable token; the decode kernels read it unchanged. Default
+    entries_per_token: 128 for keys (every channel of a token may be an outlier,
+    as with thresholds = 0), min(128, k) for values (k = the per-token top-k).
+    The `nnz` field keeps the count at the time of the copy.
+    """
+    if extra_tokens < 0:
+        raise RuntimeError("make_appendable: extra_tokens must be >= 0")
+    dev = packed["q_idx"].device
+    U, nt_cap, tb = packed["q_idx"].shape
+    T = int(packed["length"])
+    nt = _tiles(T)
+    new_cap = _tiles(T + extra_tokens) + 1
+    if entries_per_token is None:
+        if packed["kind"] == "k":
+            entries_per_token = HEAD_DIM
+        else:
+            C_full = packed.get("C_full", packed["n_heads"] * HEAD_DIM)
+            r = packed.get("outlier_ratio", 0.01)
+            entries_per_token = min(HEAD_DIM, max(1, int(C_full * r))) if r > 0 else 0
+    codes = torch.zeros((U, new_cap, tb), dtype=torch.uint8, device=dev)
+    codes[:, :nt] = packed["q_idx"][:, :nt]
+    ptr = packed["outlier_rowptr"].to(torch.int64)
+    R, R2 = 2 * nt_cap, 2 * new_cap
+    rows = torch.arange(U, device=dev) * R
+    starts = ptr[rows].cpu().tolist()
+    ends = ptr[rows + 2 * nt].cpu().tolist()
+    used = [e - s for s, e in zip(starts, ends)]
+    stride = max(used + [0]) + extra_tokens * int(entries_per_token)
+    stride = max(64, -(-stride // 64) * 64)
+    if U * stride >= 2 ** 31:
+        raise RuntimeError("make_appendable: the entry segments exceed int32 indexing")
+    ent = torch.zeros(U * stride, dtype=torch.int32, device=dev)
+    new_ptr = torch.empty(U * R2 + 1, dtype=torch.int32, device=dev)
+    old_ent = packed["outlier_entries"]
+    for u in range(U):
+        s, n = starts[u], used[u]
+        if n:
+            ent[u * stride:u * stride + n] = old_ent[s:s + n]
+        seg = ptr[u * R:u * R + 2 * nt + 1] - s + u * stride
+        new_ptr[u * R2:u * R2 + 2 * nt + 1] = seg.to(torch.int32)
+        new_ptr[u * R2 + 2 * nt + 1:(u + 1) * R2] = u * stride + n
+    new_ptr[U * R2] = U * stride
+    out = dict(packed)
+    pairs = ent.view(torch.int16).view(-1, 2)
+    out.update({
+        "q_idx": codes,
+        "outlier_entries": ent,
+        "outlier_values": pairs[:, 1].view(torch.float16),
+        "outlier_cols": pairs[:, 0],
+        "outlier_rowptr": new_ptr,
+        "capacity": (new_cap - 1) * TILE_TOKENS,
+        "ent_stride": stride,
+        "appendable": True,
+    })
+    if packed["kind"] == "v":
+        B = packed["batch"]
+        for key in ("scale", "zero"):
+            st = torch.zeros((B, new_cap * TILE_TOKENS), dtype=torch.float32, device=dev)
+            st[:, :T] = packed[key][:, :T]
+            out[key] = st
+    return out
+
+
+def _append_status(status: torch.Tensor, what: str, check: bool) -> None:
+    if check and int(status.item()) != 0:
+        raise RuntimeError(f"{what}: a unit's outlier segment is full (nothing was appended "
+                           "for that unit); rebuild with make_appendable and more "
+                           "entries_per_token")
+
+
+def _append_prologue(kind: str, packed: dict, x: torch.Tensor):
+    if not packed.get("appendable"):
+        raise RuntimeError(f"append_{kind}: the cache is not appendable (see make_appendable)")
+    if not x.is_cuda or x.dim() != 3:
+        raise RuntimeError(f"append_{kind}: expected a CUDA tensor [B, S_new, C]")
+    xc = x.to(torch.float16).contiguous()
+    if xc.shape[0] != packed["batch"]:
+        raise RuntimeError(f"append_{kind}: batch {xc.shape[0]} != cache batch {packed['batch']}")
+    if packed["length"] + xc.shape[1] > packed["capacity"]:
+        raise RuntimeError(f"append_{kind}: {packed['length']} + {xc.shape[1]} tokens exceed the "
+                           f"appendable capacity {packed['capacity']}")
+    return xc
+
+
+def append_keys(packed_k: dict, k_new: torch.Tensor, thresholds: torch.Tensor | None,
+                check: bool = True) -> dict:
+    """Appends k_new [B, S_new, C] (pre-RoPE keys) to an appendable key cache, in place.
+
+    thresholds: fp32 [n_heads*128] per-channel outlier thresholds on the
+    normalized |n| (key_outlier_thresholds), or None for no outliers; zeros
+    reproduce the reference's quantize_k on one-token blocks. check=True reads
+    the status back (one host sync) and raises if a unit ran out of room.
+    """
+    lib = get_cuda_ops().lib
+    kc = _append_prologue("keys", packed_k, k_new)
+    B, S, C_full = kc.shape
+    H, dev = packed_k["n_heads"], kc.device
+    thr = None
+    if thresholds is not None:
+        thr = thresholds.to(dev, torch.float32).reshape(-1).contiguous()
+        if thr.numel() != H * HEAD_DIM:
+            raise RuntimeError("append_keys: thresholds must have n_heads*128 entries")
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _check(lib.kvq_append_keys(
+            _ptr(kc), B, S, C_full, packed_k["h0"], H, _ptr(packed_k["scale"]),
+            _ptr(packed_k["zero"]), _ptr(thr), _ptr(packed_k["codebook"]), packed_k["bits"],
+            packed_k["length"], _ptr(packed_k["q_idx"]), packed_k["q_idx"].shape[1],
+            _ptr(packed_k["outlier_rowptr"]), _ptr(packed_k["outlier_entries"]),
+            packed_k["ent_stride"], _ptr(status), _stream(kc)), lib)
+    _append_status(status, "append_keys", check)
+    packed_k["length"] += S
+    return packed_k
+
+
+def append_values(packed_v: dict, v_new: torch.Tensor, check: bool = True) -> dict:
+    """Appends v_new [B, S_new, C] to an appendable value cache, in place.
+
+    Every new token is quantized as a one-token call of quantize_v would
+    (kv_quantizer.py:96-122): per-token scale/zero and top-k outliers over all
+    C channels of v_new, with the cache's outlier ratio.
+    """
+    lib = get_cuda_ops().lib
+    vc = _append_prologue("values", packed_v, v_new)
+    B, S, C_full = vc.shape
+    dev = vc.device
+    ws = _workspace(lib.kvq_append_values_workspace(B, S), dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _check(lib.kvq_append_values(
+            _ptr(vc), B, S, C_full, packed_v["h0"], packed_v["n_heads"],
+            float(packed_v.get("outlier_ratio", 0.01)), _ptr(packed_v["codebook"]),
+            packed_v["bits"], packed_v["length"], _ptr(packed_v["scale"]),
+            _ptr(packed_v["zero"]), packed_v["scale"].shape[1], _ptr(packed_v["q_idx"]),
+            packed_v["q_idx"].shape[1], _ptr(packed_v["outlier_rowptr"]),
+            _ptr(packed_v["outlier_entries"]), packed_v["ent_stride"], _ptr(ws), ws.numel(),
+            _ptr(status), _stream(vc)), lib)
+    _append_status(status, "append_values", check)
+    packed_v["length"] += S
+    return packed_v
+
+
+def key_outlier_thresholds(k: torch.Tensor, scale: torch.Tensor, zero: torch.Tensor,
+                           outlier_ratio: float = 0.01, sink: bool = True, h0: int = 0,
+                           n_heads: int | None = None) -> torch.Tensor:
+    """Per-channel thresholds on |n| from a calibration block k [B, S, C] (offline).
+
+    n = (k - zero) / (scale + 1e-8) over the block's tokens (the sink token
+    excluded, as quantize_k does); the threshold of a channel is the m-th
+    largest |n| over all B * S' values, m = max(1, int(B * S' * ratio)), so the
+    calibration block itself has about the reference's outlier share.
+    Returns fp32 [n_heads*128] for heads [h0, h0 + n_heads).
+    """
+    B, S, C_full = k.shape
+    H = C_full // HEAD_DIM - h0 if n_heads is None else int(n_heads)
+    c0, c1 = h0 * HEAD_DIM, (h0 + H) * HEAD_DIM
+    x = k[:, 1:] if (sink and S > 1) else k
+    sc = scale.to(k.device, torch.float32).reshape(-1)[c0:c1]
+    ze = zero.to(k.device, torch.float32).reshape(-1)[c0:c1]
+    n = ((x[:, :, c0:c1].float() - ze) / (sc + 1e-8)).abs().reshape(-1, c1 - c0)
+    m = max(1, int(n.shape[0] * outlier_ratio))
+    return torch.topk(n.t(), m, dim=1).values[:, -1].contiguous()

@@ -149,6 +149,33 @@ def quantize_k(k: np.ndarray, codebook, scale, zero, outlier_ratio=0.01,
     return dict(dequant=out, idx=idx, mask=mask, norm=n, has_sink=k_sink is not None)
 
 
+def quantize_k_thresholds(k: np.ndarray, codebook, scale, zero, thresholds):
+    """Keys of appended tokens with per-channel outlier thresholds on |n|.
+
+    The reference has no threshold path (the KVQuant paper's calibrated
+    thresholds, section 3.4, are not in its code): its quantize_k on a
+    one-token block (kvquant/quant/kv_quantizer.py:72-94 with k =
+    max(1, int(1 * r)) = 1 per channel, dense_sparse.py:22-23) makes every
+    channel an outlier, which is thresholds = 0 here. Normalization, dense
+    clamp, first-minimum centroid and dequantization follow
+    kv_quantizer.py:82-89 and dense_sparse.py:25-31 (outlier = x - dense).
+    k: [B, S, C] fp16 (no sink); thresholds: [C] fp32. Same dict keys as
+    quantize_k.
+    """
+    k = np.asarray(k, dtype=F16)
+    cb = np.asarray(codebook, dtype=F32).reshape(-1)
+    scale = np.asarray(scale, dtype=F32)
+    zero = np.asarray(zero, dtype=F32)
+    n = ((k.astype(F32) - zero) / (scale + EPS)).astype(F32)
+    mask = np.abs(n) >= np.asarray(thresholds, dtype=F32)
+    dense_raw = np.where(mask, F32(0), n).astype(F32)
+    outl = (n - dense_raw).astype(F32)
+    dense = np.clip(dense_raw, F32(-1.0), F32(1.0)).astype(F32)
+    idx, q = lut_lookup(dense, cb)
+    deq = (((q + outl).astype(F32) * scale).astype(F32) + zero).astype(F32)
+    return dict(dequant=deq.astype(F16), idx=idx, mask=mask, norm=n, has_sink=False)
+
+
 def value_token_stats(v_rest: np.ndarray):
     """kvquant/quant/kv_quantizer.py:103-107: per-token scale/zero over all C channels."""
     vf = v_rest.astype(F32)
