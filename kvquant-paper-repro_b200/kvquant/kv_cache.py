@@ -30,6 +30,19 @@ class QuantizedKVCache:
             self.v_cache.append(None)
         self.v_cache[layer_idx] = packed_v
 
+    def append_tokens(self, layer_idx: int, k_new, v_new, key_thresholds=None):
+        """Decode-time append of new tokens [B, S_new, C] into the layer's stored
+        packed caches (which make_appendable must have produced), in place.
+        No counterpart in the reference, whose hooks re-quantize each new block
+        (kvquant/attention_patch.py:22-35)."""
+        from .kernels import append_keys, append_values
+        pk, pv = self.k_cache[layer_idx], self.v_cache[layer_idx]
+        if pk is None or pv is None:
+            raise RuntimeError(f"append_tokens: layer {layer_idx} holds no cache")
+        append_keys(pk, k_new, key_thresholds)
+        append_values(pv, v_new)
+        self.seq_len = max(self.seq_len, int(pk["length"]))
+
     def clear(self):
         self.k_cache = []
         self.v_cache = []

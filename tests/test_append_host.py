@@ -88,3 +88,12 @@ def test_append_rejects_bad_arguments_before_any_launch():
     rc = lib.kvq_append_keys(None, 1, 1, 128, 0, 1, None, None, None, None, 5, 1, None, 4, None,
                              None, 64, None, None)
     assert rc == 3
+
+
+def test_cache_container_append_needs_a_stored_layer():
+    import pytest
+    from kvquant.kv_cache import QuantizedKVCache
+    c = QuantizedKVCache()
+    c.k_cache, c.v_cache = [None], [None]
+    with pytest.raises(RuntimeError, match="holds no cache"):
+        c.append_tokens(0, None, None)
