@@ -42,15 +42,6 @@ struct AppendArgs {
   int32_t* status;          // bit 0: a unit's segment had no room (nothing written for it)
 };
 
-// Code pair q of a lane slab held in registers (runtime bit width).
-__device__ __forceinline__ uint32_t slab_pair_rt(const uint32_t* w, int q, int bits) {
-  const int W = 2 * bits, bit = W * q;
-  const int wi = bit >> 5, sh = bit & 31;
-  uint32_t lo = w[wi] >> sh;
-  if (sh + W > 32) lo |= w[wi + 1] << (32 - sh);
-  return lo & ((1u << W) - 1u);
-}
-
 // Token / channel of the two codes of slot q in lane (g, cc)'s slab of block blk
 // (the fragment-native order of the decode kernels; the same map the emit
 // kernel packs with).
@@ -74,7 +65,7 @@ __device__ __forceinline__ void slot_map(int q, int blk, int g, int cc, int& ta,
 // unpacks the old tokens' codes of the tile, quantizes the new tokens,
 // appends their outlier entries in (token, channel) order behind the unit's
 // last entry, moves the tile's two row pointers and rewrites the tile's slabs.
-template <int KIND>
+template <int KIND, int BITS>
 __global__ void __launch_bounds__(128) append_kernel(AppendArgs a) {
   __shared__ __align__(16) __half xs[kTileTokens][kHeadDim];
   __shared__ int32_t cnt[kTileTokens][8];
@@ -88,7 +79,7 @@ __global__ void __launch_bounds__(128) append_kernel(AppendArgs a) {
   const int64_t h = blockIdx.x, b = blockIdx.y;
   const int c = threadIdx.x, lane = c & 31, w = c >> 5;
   const int64_t unit = b * a.H + h;
-  const int ncb = 1 << a.bits;
+  constexpr int ncb = 1 << BITS;
   const int64_t cfull = (a.h0 + h) * kHeadDim + c;
   const int64_t T_new = a.T_old + a.S_new;
   const int64_t urow = unit * 2 * a.nt_cap;  // first CSR row of the unit
@@ -132,30 +123,31 @@ __global__ void __launch_bounds__(128) append_kernel(AppendArgs a) {
 
   for (int64_t tile = a.T_old / kTileTokens; tile <= (T_new - 1) / kTileTokens; ++tile) {
     const int64_t t0 = tile * kTileTokens;
-    uint8_t* tile_base = a.codes + (unit * a.nt_cap + tile) * (int64_t)tile_bytes(a.bits);
+    uint8_t* tile_base = a.codes + (unit * a.nt_cap + tile) * (int64_t)(kTileTokens * kHeadDim * BITS / 8);
     for (int k = c; k < kTileTokens * kHeadDim; k += 128) (&s_code[0][0])[k] = 0;
     __syncthreads();
     // Old tokens' codes of the tile: threads 0..63 unpack slab (block, lane).
     if (t0 < a.T_old && c < 64) {
       const int blk = c >> 5, g = lane >> 2, cc = lane & 3;
-      const uint8_t* bb = tile_base + blk * (256 * a.bits);
+      const uint8_t* bb = tile_base + blk * (256 * BITS);
       uint32_t slab[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       const uint4 v0 = *reinterpret_cast<const uint4*>(bb + lane * 16);
       slab[0] = v0.x; slab[1] = v0.y; slab[2] = v0.z; slab[3] = v0.w;
-      if (a.bits == 4) {
+      if (BITS == 4) {
         const uint4 v1 = *reinterpret_cast<const uint4*>(bb + 512 + lane * 16);
         slab[4] = v1.x; slab[5] = v1.y; slab[6] = v1.z; slab[7] = v1.w;
-      } else if (a.bits == 3) {
+      } else if (BITS == 3) {
         const uint2 v1 = *reinterpret_cast<const uint2*>(bb + 512 + lane * 8);
         slab[4] = v1.x; slab[5] = v1.y;
       }
-      const uint32_t cmask = (1u << a.bits) - 1u;
+      constexpr uint32_t cmask = (1u << BITS) - 1u;
+#pragma unroll
       for (int q = 0; q < 32; ++q) {
         int ta, ca, tb, cb2;
         slot_map<KIND>(q, blk, g, cc, ta, ca, tb, cb2);
-        const uint32_t pair = slab_pair_rt(slab, q, a.bits);
+        const uint32_t pair = slab_pair<BITS>(slab, q);
         if (t0 + ta < a.T_old) s_code[ta][ca] = (uint8_t)(pair & cmask);
-        if (t0 + tb < a.T_old) s_code[tb][cb2] = (uint8_t)(pair >> a.bits);
+        if (t0 + tb < a.T_old) s_code[tb][cb2] = (uint8_t)(pair >> BITS);
       }
     }
     // New tokens of the tile, staged with coalesced 16-byte loads.
@@ -206,15 +198,24 @@ __global__ void __launch_bounds__(128) append_kernel(AppendArgs a) {
       }
     }
     __syncthreads();
-    if (c == 0) {  // exclusive prefix over (token, 16-channel group)
-      int32_t run = 0;
-      for (int r = 0; r < kTileTokens * 8; ++r) {
-        if (r == 16 * 8) s_n0 = run;  // entries of tokens 0..15
-        const int32_t v = (&cnt[0][0])[r];
-        (&cnt[0][0])[r] = run;
-        run += v;
+    {  // exclusive prefix over (token, 16-channel group): thread c owns entries 2c, 2c+1
+      int32_t* flat = &cnt[0][0];
+      const int32_t v0 = flat[2 * c], v1 = flat[2 * c + 1];
+      int32_t incl = v0 + v1;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int32_t o = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += o;
       }
-      s_tot = run;
+      if (lane == 31) s_red[w] = incl;
+      __syncthreads();
+      int32_t base = 0;
+      for (int k = 0; k < w; ++k) base += s_red[k];
+      const int32_t excl = base + incl - v0 - v1;
+      flat[2 * c] = excl;
+      flat[2 * c + 1] = excl + v0;
+      if (c == 64) s_n0 = excl;  // entries of tokens 0..15 (flat index 128)
+      if (c == 127) s_tot = excl + v0 + v1;
     }
     __syncthreads();
     const uint32_t below = (1u << (lane & 15)) - 1u;
@@ -240,20 +241,29 @@ __global__ void __launch_bounds__(128) append_kernel(AppendArgs a) {
       for (int q = 0; q < 32; ++q) {
         int ta, ca, tb, cb2;
         slot_map<KIND>(q, blk, g, cc, ta, ca, tb, cb2);
-        const uint32_t pair = (uint32_t)s_code[ta][ca] | ((uint32_t)s_code[tb][cb2] << a.bits);
-        const int bit = 2 * a.bits * q;
+        const uint32_t pair = (uint32_t)s_code[ta][ca] | ((uint32_t)s_code[tb][cb2] << BITS);
+        const int bit = 2 * BITS * q;
         slab[bit >> 5] |= pair << (bit & 31);
-        if ((bit & 31) + 2 * a.bits > 32) slab[(bit >> 5) + 1] |= pair >> (32 - (bit & 31));
+        if ((bit & 31) + 2 * BITS > 32) slab[(bit >> 5) + 1] |= pair >> (32 - (bit & 31));
       }
-      uint8_t* bb = tile_base + blk * (256 * a.bits);
+      uint8_t* bb = tile_base + blk * (256 * BITS);
       *reinterpret_cast<uint4*>(bb + lane * 16) = make_uint4(slab[0], slab[1], slab[2], slab[3]);
-      if (a.bits == 4)
+      if (BITS == 4)
         *reinterpret_cast<uint4*>(bb + 512 + lane * 16) = make_uint4(slab[4], slab[5], slab[6], slab[7]);
-      else if (a.bits == 3)
+      else if (BITS == 3)
         *reinterpret_cast<uint2*>(bb + 512 + lane * 8) = make_uint2(slab[4], slab[5]);
     }
     end += s_tot;
     __syncthreads();  // the next tile reuses the shared buffers
+  }
+}
+
+template <int KIND>
+static void launch_append(const AppendArgs& aa, dim3 grid, cudaStream_t st) {
+  switch (aa.bits) {
+    case 2: append_kernel<KIND, 2><<<grid, 128, 0, st>>>(aa); break;
+    case 3: append_kernel<KIND, 3><<<grid, 128, 0, st>>>(aa); break;
+    default: append_kernel<KIND, 4><<<grid, 128, 0, st>>>(aa); break;
   }
 }
 
@@ -305,7 +315,7 @@ extern "C" int kvq_append_keys(const void* k_new, int64_t B, int64_t S_new, int6
   aa.outliers = thresholds != nullptr; aa.cb = codebook; aa.bits = bits; aa.codes = codes;
   aa.nt_cap = nt_cap; aa.out_ptr = out_ptr; aa.out_ent = out_ent; aa.ent_stride = ent_stride;
   aa.status = status;
-  append_kernel<0><<<dim3((unsigned)n_heads, (unsigned)B), 128, 0, as_stream(stream)>>>(aa);
+  launch_append<0>(aa, dim3((unsigned)n_heads, (unsigned)B), as_stream(stream));
   return check_launch("append_keys");
 }
 
@@ -355,6 +365,6 @@ extern "C" int kvq_append_values(const void* v_new, int64_t B, int64_t S_new, in
   aa.ld_stats = ld_stats; aa.sel = sel; aa.outliers = outliers; aa.cb = codebook; aa.bits = bits;
   aa.codes = codes; aa.nt_cap = nt_cap; aa.out_ptr = out_ptr; aa.out_ent = out_ent;
   aa.ent_stride = ent_stride; aa.status = status;
-  append_kernel<1><<<dim3((unsigned)n_heads, (unsigned)B), 128, 0, st>>>(aa);
+  launch_append<1>(aa, dim3((unsigned)n_heads, (unsigned)B), st);
   return check_launch("append_values");
 }

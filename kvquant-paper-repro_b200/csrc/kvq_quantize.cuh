@@ -201,17 +201,40 @@ __global__ void __launch_bounds__(256) value_plan_kernel(
       if ((ab & mask_hi) == prefix) atomicAdd(&hist[(ab >> shift) & 0xffu], 1u);
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      int32_t k = sh_kleft;
-      int d = 255;
-      for (; d > 0; --d) {
-        const int32_t n = (int32_t)hist[d];
-        if (k <= n) break;
-        k -= n;
+    // The digit holding the k-th largest entry: walking the bins from 255 down,
+    // the first d >= 1 whose suffix count reaches k (d = 0 if none). Warp 0:
+    // lane L holds bins 8L..8L+7; a suffix scan over the lanes finds the one
+    // lane where the count crosses k, which then walks its own 8 bins.
+    if (threadIdx.x < 32) {
+      const int L = threadIdx.x;
+      const int32_t k0 = sh_kleft;
+      int32_t h8[8], s8 = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        h8[j] = (int32_t)hist[8 * L + j];
+        s8 += h8[j];
       }
-      sh_kleft = k;
-      sh_digit = d;
-      sh_ties = (int32_t)hist[d];
+      int32_t suf = s8;  // bins 8L .. 255
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int32_t v = __shfl_down_sync(0xffffffffu, suf, o);
+        if (L + o < 32) suf += v;
+      }
+      const int32_t above = suf - s8;  // bins 8L+8 .. 255
+      const bool mine = (k0 <= suf && (L == 31 || above < k0)) || (L == 0 && k0 > suf);
+      if (mine) {
+        int32_t k = k0 - above;
+        int d = 0;  // bin 0 is the fall-through: it is never tested
+#pragma unroll
+        for (int j = 7; j >= 0; --j) {
+          if (8 * L + j == 0) break;
+          if (k <= h8[j]) { d = 8 * L + j; break; }
+          k -= h8[j];
+        }
+        sh_kleft = k;
+        sh_digit = d;
+        sh_ties = (int32_t)hist[d];
+      }
     }
     __syncthreads();
     prefix |= (uint32_t)sh_digit << shift;
@@ -386,14 +409,25 @@ __global__ void __launch_bounds__(128) emit_kernel(EmitArgs a) {
     }
     return;
   }
-  // Exclusive prefix over (token, group) in order -> entry offsets.
-  if (c == 0) {
-    int32_t run = 0;
-    for (int r = 0; r < kTileTokens * 8; ++r) {
-      const int32_t v = (&cnt[0][0])[r];
-      (&cnt[0][0])[r] = run;
-      run += v;
+  // Exclusive prefix over (token, group) in order -> entry offsets; thread c
+  // owns entries 2c, 2c+1 of the 256 (token, group) counts.
+  {
+    __shared__ int32_t s_wsum[4];
+    int32_t* flat = &cnt[0][0];
+    const int32_t v0 = flat[2 * c], v1 = flat[2 * c + 1];
+    int32_t incl = v0 + v1;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int32_t o = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += o;
     }
+    if (lane == 31) s_wsum[w] = incl;
+    __syncthreads();
+    int32_t base_w = 0;
+    for (int k = 0; k < w; ++k) base_w += s_wsum[k];
+    const int32_t excl = base_w + incl - v0 - v1;
+    flat[2 * c] = excl;
+    flat[2 * c + 1] = excl + v0;
   }
   __syncthreads();
   const int64_t base = a.out_ptr[2 * (unit * a.nt_cap + tile)];  // first entry of the tile

@@ -400,6 +400,9 @@ def make_appendable(packed: dict, extra_tokens: int,
         "capacity": (new_cap - 1) * TILE_TOKENS,
         "ent_stride": stride,
         "appendable": True,
+        # reused by every append call: the status word and the values' scratch
+        "append_status": torch.zeros(1, dtype=torch.int32, device=dev),
+        "append_workspace": None,
     })
     if packed["kind"] == "v":
         B = packed["batch"]
@@ -411,7 +414,11 @@ def make_appendable(packed: dict, extra_tokens: int,
 
 
 def _append_status(status: torch.Tensor, what: str, check: bool) -> None:
+    # The status word only ever gets bits set (by a unit that had no room), so
+    # it is cleared only after a failure is read; an unchecked call's failure
+    # is reported by the next checked one.
     if check and int(status.item()) != 0:
+        status.zero_()
         raise RuntimeError(f"{what}: a unit's outlier segment is full (nothing was appended "
                            "for that unit); rebuild with make_appendable and more "
                            "entries_per_token")
@@ -438,7 +445,8 @@ def append_keys(packed_k: dict, k_new: torch.Tensor, thresholds: torch.Tensor | 
     thresholds: fp32 [n_heads*128] per-channel outlier thresholds on the
     normalized |n| (key_outlier_thresholds), or None for no outliers; zeros
     reproduce the reference's quantize_k on one-token blocks. check=True reads
-    the status back (one host sync) and raises if a unit ran out of room.
+    the status back (one host sync) and raises if a unit ran out of room (in
+    this call or in an earlier call made with check=False).
     """
     lib = get_cuda_ops().lib
     kc = _append_prologue("keys", packed_k, k_new)
@@ -449,7 +457,7 @@ def append_keys(packed_k: dict, k_new: torch.Tensor, thresholds: torch.Tensor | 
         thr = thresholds.to(dev, torch.float32).reshape(-1).contiguous()
         if thr.numel() != H * HEAD_DIM:
             raise RuntimeError("append_keys: thresholds must have n_heads*128 entries")
-    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    status = packed_k["append_status"]
     with torch.cuda.device(dev):
         _check(lib.kvq_append_keys(
             _ptr(kc), B, S, C_full, packed_k["h0"], H, _ptr(packed_k["scale"]),
@@ -473,8 +481,11 @@ def append_values(packed_v: dict, v_new: torch.Tensor, check: bool = True) -> di
     vc = _append_prologue("values", packed_v, v_new)
     B, S, C_full = vc.shape
     dev = vc.device
-    ws = _workspace(lib.kvq_append_values_workspace(B, S), dev)
-    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    need = lib.kvq_append_values_workspace(B, S)
+    ws = packed_v.get("append_workspace")
+    if ws is None or ws.numel() < need:
+        ws = packed_v["append_workspace"] = _workspace(need, dev)
+    status = packed_v["append_status"]
     with torch.cuda.device(dev):
         _check(lib.kvq_append_values(
             _ptr(vc), B, S, C_full, packed_v["h0"], packed_v["n_heads"],
