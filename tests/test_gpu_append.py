@@ -156,3 +156,22 @@ def test_full_segment_is_reported_and_left_alone(cuda):
     # without outliers the same append fits
     append_keys(pk, t(k[:, 32:40], cuda), None)
     assert pk["length"] == 40
+
+
+def test_regrow_and_append_again(cuda):
+    """make_appendable on a grown cache gives more room; values stay identical
+    to quantizing the whole sequence at once."""
+    from kvquant.kernels import quantize_values, make_appendable, append_values
+    B, H, bits, ratio = 1, 3, 4, 0.02
+    _, v = synth.make_kv(B, 120, H * 128, seed=51)
+    cb = t(np.linspace(-1, 1, 16).astype(np.float32), cuda)
+    pv = make_appendable(quantize_values(t(v[:, :40], cuda), cb, bits, ratio, True), 10)
+    append_values(pv, t(v[:, 40:50], cuda))
+    with pytest.raises(RuntimeError, match="capacity"):
+        append_values(pv, t(v[:, 50:120], cuda))
+    pv = make_appendable(pv, 70)
+    append_values(pv, t(v[:, 50:51], cuda))
+    append_values(pv, t(v[:, 51:120], cuda))
+    full = quantize_values(t(v, cuda), cb, bits, ratio, True)
+    for g_, w_ in zip(read_packed(pv), read_packed(full)):
+        np.testing.assert_array_equal(g_, w_)
