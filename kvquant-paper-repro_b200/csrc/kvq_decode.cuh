@@ -385,21 +385,23 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
     // cos (c < 2) or sin (c >= 2) of tokens g, g + 8 of this warp's block for
     // pairs 4kb + 2(c & 1) + {0, 1}.
     const int tok0 = tile0 * kTileTokens + 16 * warp;  // first token of the block
-    const float phase = c < 2 ? 0.f : 1.5707963267948966f;  // cos (c < 2) or sin
+    // Lanes c and c ^ 2 need the same angles (one the cosines, the other the
+    // sines): each evaluates one of the pair's two angles (e = c >> 1) with
+    // sin and cos, keeps its own function and passes the other one across.
+    const bool want_cos = c < 2;
     // tw[kb][0] = the pair (e = 0, 1) for token g, tw[kb][1] for token g + 8
     uint64_t tw[16][2];
 #pragma unroll
     for (int kb = 0; kb < 16; ++kb) {
-      float v[4];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const float f = invf[4 * kb + 2 * (c & 1) + e];
-        // sin r = cos(r - pi/2): one hardware cosine per value
-        v[e] = __cosf(rope_reduce(tok0 + g, f) - phase);
-        v[2 + e] = __cosf(rope_reduce(tok0 + g + 8, f) - phase);
-      }
-      tw[kb][0] = f2pack(v[0], v[1]);
-      tw[kb][1] = f2pack(v[2], v[3]);
+      const float f = invf[4 * kb + 2 * (c & 1) + (c >> 1)];
+      float s0, c0, s8, c8;
+      __sincosf(rope_reduce(tok0 + g, f), &s0, &c0);
+      __sincosf(rope_reduce(tok0 + g + 8, f), &s8, &c8);
+      const float k0 = want_cos ? c0 : s0, k8 = want_cos ? c8 : s8;
+      const float r0 = __shfl_xor_sync(0xffffffffu, want_cos ? s0 : c0, 2);
+      const float r8 = __shfl_xor_sync(0xffffffffu, want_cos ? s8 : c8, 2);
+      tw[kb][0] = want_cos ? f2pack(k0, r0) : f2pack(r0, k0);
+      tw[kb][1] = want_cos ? f2pack(k8, r8) : f2pack(r8, k8);
     }
 
     int rd_stage = 0;
@@ -1001,11 +1003,20 @@ template <int BITS, int G>
 static int launch_key(const KeyArgs& a0, cudaStream_t st) {
   KeyArgs a = a0;
   const int64_t U = a.B * a.H;
-  const int UG = (int)(U < (int64_t)(kMaxSlots / G) ? U : (int64_t)(kMaxSlots / G));
-  a.units_per_group = UG;
-  a.n_groups = (int)((U + UG - 1) / UG);
   const int64_t nt = (a.T + kTileTokens - 1) / kTileTokens;
   const int64_t n_oct = (nt + kKeyTiles - 1) / kKeyTiles;
+  // Units per work item: as many as fit (the RoPE twiddles of an item are shared by
+  // its units), unless that leaves fewer than two items per SM: short contexts then
+  // split the units into more, smaller groups so that every SM gets work.
+  int64_t UG = U < (int64_t)(kMaxSlots / G) ? U : (int64_t)(kMaxSlots / G);
+  const int64_t want_items = 2 * (int64_t)kValSlots;
+  if (n_oct * ((U + UG - 1) / UG) < want_items) {
+    const int64_t groups = (want_items + n_oct - 1) / n_oct;
+    const int64_t ug = (U + groups - 1) / groups;
+    UG = ug < 1 ? 1 : (ug < UG ? ug : UG);
+  }
+  a.units_per_group = (int)UG;
+  a.n_groups = (int)((U + UG - 1) / UG);
   a.n_items = n_oct * a.n_groups;
   const int smem = key_smem_bytes<BITS>();
   cudaFuncSetAttribute(key_scores_kernel<BITS, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
