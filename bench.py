@@ -51,6 +51,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-append", action="store_true")
+    ap.add_argument("--shard", choices=["auto", "heads", "tokens"], default="auto",
+                    help="multi-GPU split: KV heads, or token ranges of all heads (auto: heads "
+                         "while every rank keeps at least 16 KV heads)")
     return ap.parse_args()
 
 
@@ -138,13 +141,16 @@ def peak_hbm():
         return 6650.0, "fallback"
 
 
-def build_cache(wl, layers, h0, hl, dev, log):
-    """Quantized cache of this rank's heads, every layer (built with our kernels)."""
+def build_cache(wl, layers, h0, hl, dev, log, T=None, sink=True, seed=0):
+    """Quantized cache of this rank's heads (and token range), every layer (built
+    with our kernels). T: tokens of the range (default: the workload's); sink:
+    whether its first token is the context's sink; seed: synthetic data seed."""
     import torch
     from kvquant import synthetic as syn
     from kvquant.kernels import quantize_keys, quantize_values
 
-    B, T, C = wl.batch, wl.tokens, wl.channels
+    B, C = wl.batch, wl.channels
+    T = wl.tokens if T is None else T
     k = torch.empty((B, T, C), dtype=torch.float16, device=dev)
     v = torch.empty((B, T, C), dtype=torch.float16, device=dev)
     cache = []
@@ -152,15 +158,15 @@ def build_cache(wl, layers, h0, hl, dev, log):
     t0 = time.time()
     q_ms = []  # quantize-on-append time of the whole prefill block, per layer (after the first)
     for layer in range(layers):
-        syn.fill_layer(k, v, layer, seed=0)
-        ks, kz = syn.key_calibration(k)
+        syn.fill_layer(k, v, layer, seed=seed)
+        ks, kz = syn.key_calibration(k, sink=sink)
         if cbk is None:  # one codebook pair for the synthetic model (same distribution per layer)
             cbk, cbv = syn.fit_codebooks(k, v, ks, kz, wl.bits)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        pk = quantize_keys(k, ks, kz, cbk, wl.bits, wl.outlier_ratio, True, h0=h0, n_heads=hl,
+        pk = quantize_keys(k, ks, kz, cbk, wl.bits, wl.outlier_ratio, sink, h0=h0, n_heads=hl,
                            capacity=T)
-        pv = quantize_values(v, cbv, wl.bits, wl.outlier_ratio, True, h0=h0, n_heads=hl,
+        pv = quantize_values(v, cbv, wl.bits, wl.outlier_ratio, sink, h0=h0, n_heads=hl,
                              capacity=T)
         e1.record()
         if 1 <= layer <= 3:
@@ -240,7 +246,17 @@ def flush_l2_needed(wl, layers, world) -> bool:
     return per_rank < 2 * L2_BYTES
 
 
-def bench_config(wl, layers, world):
+def shard_mode(args, wl, world) -> str:
+    """'heads' or 'tokens'. The key kernel shares each 16-token block's RoPE
+    twiddles across a work item's units, so a rank with few KV heads runs it
+    below its 32-head rate; auto keeps KV-head sharding while every rank has at
+    least 16 heads and splits token ranges of all heads beyond that."""
+    if args.shard != "auto":
+        return args.shard
+    return "heads" if world == 1 or wl.kv_heads // world >= 16 else "tokens"
+
+
+def bench_config(wl, layers, world, mode="heads"):
     """The workload description both arms print (identical for the same run)."""
     l2 = ("L2 flushed between timed steps (256 MiB write outside the timed region)"
           if flush_l2_needed(wl, layers, world)
@@ -248,7 +264,9 @@ def bench_config(wl, layers, world):
     return {"workload": wl.name, "batch": wl.batch, "kv_heads": wl.kv_heads,
             "q_per_kv": wl.q_per_kv, "tokens": wl.tokens, "layers": layers, "bits": wl.bits,
             "outlier_ratio": wl.outlier_ratio, "rope_base": wl.rope_base,
-            "sharding": f"kv heads / {world} GPUs",
+            "sharding": (f"kv heads / {world} GPUs" if mode == "heads" else
+                         f"token ranges / {world} GPUs (all {wl.kv_heads} KV heads per GPU, "
+                         "softmax partials all-gathered and merged)"),
             "compute": "fp16 tensor-core MMA on LUT-dequantized codes, fp32 accumulate",
             "l2": l2}
 
@@ -284,16 +302,25 @@ def run_gpu(args):
         import dataclasses
         wl = dataclasses.replace(wl, tokens=args.tokens, name=f"{wl.name}@{args.tokens}tok")
     layers = args.layers or wl.layers
-    from kvquant.sharding import shard_heads, gather_buffer, gather_head_outputs
+    from kvquant.sharding import (shard_heads, shard_tokens, gather_buffer, gather_head_outputs,
+                                  gather_shard_partials)
+    from kvquant.kernels import merge_shards, decode_attention_shard
+    mode = shard_mode(args, wl, world)
     try:
-        h0, hl = shard_heads(wl.kv_heads, world, rank)
+        if mode == "heads":
+            h0, hl = shard_heads(wl.kv_heads, world, rank)
+            t0, t1 = 0, wl.tokens
+        else:  # every rank: all KV heads over its range of cached positions
+            h0, hl = 0, wl.kv_heads
+            t0, t1 = shard_tokens(wl.tokens, world, rank)
     except ValueError as e:
         raise SystemExit(str(e))
     G = wl.q_per_kv
-    T = wl.tokens
+    T = t1 - t0  # cached tokens on this rank
     log = (lambda m: print(f"[rank {rank}] {m}", file=sys.stderr, flush=True))
 
-    cache, qstat = build_cache(wl, layers, h0, hl, dev, log)
+    cache, qstat = build_cache(wl, layers, h0, hl, dev, log, T=T, sink=(t0 == 0),
+                               seed=0 if mode == "heads" else rank)
     inv = rope_inv_freq(128, wl.rope_base).to(dev)
     qs = [syn.make_query(wl.batch, wl.kv_heads * G, l, 0, dev)[:, h0 * G:(h0 + hl) * G].contiguous()
           for l in range(layers)]
@@ -302,27 +329,48 @@ def run_gpu(args):
     stats = torch.empty((wl.batch * Hq_l, -(-T // 256), 2), dtype=torch.float32, device=dev)
     outs = [torch.empty((wl.batch, Hq_l, 128), dtype=torch.float16, device=dev)
             for _ in range(layers)]
-    full = [gather_buffer(outs[l], world) for l in range(layers)] if world > 1 else None
+    tok_split = mode == "tokens" and world > 1
+    if tok_split:  # shard outputs + softmax row stats of every rank, merged per layer
+        mls = [torch.empty((wl.batch * Hq_l, 2), dtype=torch.float32, device=dev)
+               for _ in range(layers)]
+        o_buf = [torch.empty((world, wl.batch, Hq_l, 128), dtype=torch.float16, device=dev)
+                 for _ in range(layers)]
+        ml_buf = [torch.empty((world, wl.batch * Hq_l, 2), dtype=torch.float32, device=dev)
+                  for _ in range(layers)]
+        merged = [torch.empty((wl.batch, Hq_l, 128), dtype=torch.float16, device=dev)
+                  for _ in range(layers)]
+        full = None
+    else:
+        full = [gather_buffer(outs[l], world) for l in range(layers)] if world > 1 else None
     stream = torch.cuda.current_stream(dev)
     # key (scores + softmax partials), value row max, value (softmax of the raw
-    # scores fused in), combine
-    n_launch_per_layer = 4
+    # scores fused in), combine; token ranges add the merge of the ranks' shards
+    n_launch_per_layer = 5 if tok_split else 4
 
     def step(events=None):
         handles = []
         for l, (pk, pv) in enumerate(cache):
             if events is not None:
                 events[l][0].record(stream)
-            qk_scores_stats(qs[l], pk, inv, out=scores, stats_out=stats)
+            qk_scores_stats(qs[l], pk, inv, out=scores, stats_out=stats, pos0=t0)
             if events is not None:
                 events[l][1].record(stream)
-            outs[l] = pv_out_scores(scores, stats, pv)
+            if tok_split:
+                pv_out_scores(scores, stats, pv, ml_out=mls[l], out=outs[l])
+            else:
+                outs[l] = pv_out_scores(scores, stats, pv)
             if events is not None:
                 events[l][2].record(stream)
-            if world > 1:
-                handles.append(gather_head_outputs(outs[l], full[l], async_op=True))
-        for h in handles:
-            h.wait()
+            if tok_split:
+                handles.append((l, gather_shard_partials(outs[l], mls[l], o_buf[l], ml_buf[l],
+                                                         async_op=True)))
+            elif world > 1:
+                handles.append((l, (gather_head_outputs(outs[l], full[l], async_op=True),)))
+        for l, hs in handles:
+            for h in hs:
+                h.wait()
+            if tok_split:
+                merge_shards(o_buf[l], ml_buf[l], out=merged[l])
 
     for _ in range(args.warmup):
         step()
@@ -368,14 +416,15 @@ def run_gpu(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         elapsed = float(t.item())
     ms_step = elapsed / args.steps
-    total_tokens = wl.batch * T * layers
+    total_tokens = wl.batch * wl.tokens * layers  # the whole context, all ranks together
     value = total_tokens / (ms_step / 1e3)
 
     # e2e through the public API: pinned host q in, host output out, every step
     e2e = None
     if not args.no_e2e:
         q_host = [q.cpu().pin_memory() for q in qs]
-        o_host = [torch.empty((world * wl.batch, Hq_l, 128), dtype=torch.float16).pin_memory()
+        o_rows = wl.batch if tok_split else world * wl.batch  # token ranges: merged output
+        o_host = [torch.empty((o_rows, Hq_l, 128), dtype=torch.float16).pin_memory()
                   for _ in range(layers)]
         q_dev = [torch.empty_like(q) for q in qs]
         wsp = DecodeWorkspace()
@@ -384,14 +433,25 @@ def run_gpu(args):
             handles = []
             for l, (pk, pv) in enumerate(cache):
                 q_dev[l].copy_(q_host[l], non_blocking=True)
+                if tok_split:
+                    o, ml = decode_attention_shard(q_dev[l], pk, pv, inv, pos0=t0, scores=scores,
+                                                   stats=stats, out=outs[l], ml_out=mls[l])
+                    handles.append((l, gather_shard_partials(o, ml, o_buf[l], ml_buf[l],
+                                                             async_op=True)))
+                    continue
                 o = decode_attention(q_dev[l], pk, pv, inv, workspace=wsp)
                 if world > 1:
-                    handles.append((l, gather_head_outputs(o, full[l], async_op=True)))
+                    handles.append((l, (gather_head_outputs(o, full[l], async_op=True),)))
                 else:
                     o_host[l].copy_(o, non_blocking=True)
-            for l, h in handles:
-                h.wait()
-                o_host[l].copy_(full[l], non_blocking=True)
+            for l, hs in handles:
+                for h in hs:
+                    h.wait()
+                if tok_split:
+                    o_host[l].copy_(merge_shards(o_buf[l], ml_buf[l], out=merged[l]),
+                                    non_blocking=True)
+                else:
+                    o_host[l].copy_(full[l], non_blocking=True)
             torch.cuda.current_stream(dev).synchronize()
 
         for _ in range(max(1, args.warmup)):
@@ -415,7 +475,7 @@ def run_gpu(args):
             e_el = float(t.item())
         e2e = {"value": total_tokens / (e_el / args.steps / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": sum(q.numel() * 2 for q in qs),
-               "d2h_bytes_per_step": layers * world * wl.batch * Hq_l * 128 * 2}
+               "d2h_bytes_per_step": layers * o_rows * Hq_l * 128 * 2}
 
     append_stat = None
     if not args.no_append:
@@ -440,7 +500,7 @@ def run_gpu(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f16", "data": "synthetic",
-            "config": bench_config(wl, layers, world),
+            "config": bench_config(wl, layers, world, mode),
             "bytes_read_per_gpu_per_step": step_bytes,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
                          "peak_source": peak_src, "unit": "GB/s", "frac": achieved / peak,
@@ -582,7 +642,8 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": statistics.mean(walls) * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": bench_config(wl, args.layers or wl.layers, args.gpus),
+        "config": bench_config(wl, args.layers or wl.layers, args.gpus,
+                               shard_mode(args, wl, args.gpus)),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": min(cores, units), "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

@@ -222,6 +222,33 @@ int kvq_value_output_scores(const uint8_t* codes, const uint32_t* out_ent,
                             int64_t nt_cap, void* out, void* workspace, size_t workspace_bytes,
                             void* stream);
 
+/* Token-range shards of one decode step (restated; the reference has no decode
+ * attention). A cache holding the tokens at positions [pos0, pos0 + T) -- its own
+ * token 0 is the sink only when pos0 == 0 -- gives, with the two calls below, its
+ * shard's output and the softmax row stats (M, 1/L) of softmax(scores * scale)
+ * over its tokens, fp32 pairs [B*n_heads*group]; kvq_merge_shards combines the
+ * shards of all ranks into the output over the whole context.
+ * kvq_key_scores_stats_at = kvq_key_scores_stats with RoPE positions pos0 + t. */
+int kvq_key_scores_stats_at(const uint8_t* codes, const uint32_t* out_ent,
+                            const int32_t* out_ptr, const float* k_scale, const float* k_zero,
+                            const void* k_sink, const float* codebook, int bits, const void* q,
+                            const float* inv_freq, int64_t B, int64_t n_heads, int64_t group,
+                            int64_t T, int64_t nt_cap, int64_t pos0, float* scores, float scale,
+                            void* stats, void* stream);
+/* kvq_value_output_scores that also writes the row stats (M, 1/L) to ml_out. */
+int kvq_value_output_scores_ml(const uint8_t* codes, const uint32_t* out_ent,
+                               const int32_t* out_ptr, const float* v_scale, const float* v_zero,
+                               int64_t ld_stats, const void* v_sink, const float* codebook,
+                               int bits, const float* scores, const void* stats, float scale,
+                               int64_t B, int64_t n_heads, int64_t group, int64_t T,
+                               int64_t nt_cap, void* out, float* ml_out, void* workspace,
+                               size_t workspace_bytes, void* stream);
+/* out[row] = sum_i w_i o_i[row] / sum_i w_i, w_i = L_i exp(M_i - max_j M_j):
+ * o_shards fp16 [n_shards, rows, 128], ml_shards fp32 pairs [n_shards, rows],
+ * out fp16 [rows, 128]. */
+int kvq_merge_shards(const void* o_shards, const float* ml_shards, int64_t n_shards,
+                     int64_t rows, void* out, void* stream);
+
 /* scores -> softmax(scores / sqrt(128)) -> p.V in one call; scores_out and
  * probs_out may be NULL (then they live in the workspace). With probs_out
  * NULL the softmax is fused (kvq_key_scores_stats + kvq_value_output_scores,

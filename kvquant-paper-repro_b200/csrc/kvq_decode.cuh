@@ -184,6 +184,7 @@ struct KeyArgs {
   float stat_scale;
   int units_per_group, n_groups;
   int64_t n_items;         // tile octets * groups
+  int64_t pos0;            // position of cached token 0 (a token-range shard starts later)
 };
 
 constexpr int kKeyWarps = 16;
@@ -384,7 +385,7 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
 
     // cos (c < 2) or sin (c >= 2) of tokens g, g + 8 of this warp's block for
     // pairs 4kb + 2(c & 1) + {0, 1}.
-    const int tok0 = tile0 * kTileTokens + 16 * warp;  // first token of the block
+    const int tok0 = (int)a.pos0 + tile0 * kTileTokens + 16 * warp;  // position of the block's first token
     // Lanes c and c ^ 2 need the same angles (one the cosines, the other the
     // sines): each evaluates one of the pair's two angles (e = c >> 1) with
     // sin and cos, keeps its own function and passes the other one across.
@@ -972,6 +973,26 @@ __global__ void value_combine_kernel(const float* __restrict__ partial, int n_sp
   out[slot * kHeadDim + d] = __float2half_rn(v + z);
 }
 
+// Merge of token-range shards of one decode step: shard i produced o_i (its
+// tokens' softmax-weighted values, normalized by its own L_i) and the row's
+// (M_i, 1/L_i) of softmax(scores * scale). The whole row's output is
+// sum_i w_i o_i / sum_i w_i with w_i = L_i exp(M_i - M), M = max_i M_i.
+__global__ void merge_shards_kernel(const __half* __restrict__ o, const float2* __restrict__ ml,
+                                    int64_t n, int64_t rows, __half* __restrict__ out) {
+  const int64_t row = blockIdx.x;
+  const int d = threadIdx.x;  // 128 threads
+  float m = -INFINITY;
+  for (int64_t i = 0; i < n; ++i) m = fmaxf(m, ml[i * rows + row].x);
+  float num = 0.f, den = 0.f;
+  for (int64_t i = 0; i < n; ++i) {
+    const float2 p = ml[i * rows + row];
+    const float w = __expf(p.x - m) / p.y;
+    num = fmaf(w, __half2float(o[(i * rows + row) * kHeadDim + d]), num);
+    den += w;
+  }
+  out[row * kHeadDim + d] = __float2half_rn(num / den);
+}
+
 // Splits of each unit's tiles into value work items. The value kernel runs
 // one 16-warp CTA per SM (16 tiles in flight), so the items run in waves of
 // kValSlots; the split count minimises waves x (tile rounds per warp + a
@@ -1128,7 +1149,8 @@ static int value_impl(const uint8_t* codes, const uint32_t* out_ent, const int32
                       const void* v_sink, const float* codebook, int bits, const float* probs,
                       int64_t B, int64_t H, int64_t G, int64_t T, int64_t nt_cap, void* out,
                       void* workspace, size_t workspace_bytes, cudaStream_t st,
-                      const float2* stats = nullptr, float stat_scale = 0.f) {
+                      const float2* stats = nullptr, float stat_scale = 0.f,
+                      float2* ml_out = nullptr) {
   int rc = check_decode_shape("value_output", B, H, G, T, nt_cap);
   if (rc) return rc;
   if (ld_stats < T) {
@@ -1157,8 +1179,9 @@ static int value_impl(const uint8_t* codes, const uint32_t* out_ent, const int32
   const unsigned n_chunks = (unsigned)((T + kRowMaxChunk - 1) / kRowMaxChunk);
   if (stats) {
     // one launch: the row maxima and the merge of the key kernel's partials
-    float2* ml = reinterpret_cast<float2*>((char*)workspace + part_bytes +
-                                           align256((size_t)B * sizeof(float)));
+    float2* ml = ml_out ? ml_out
+                        : reinterpret_cast<float2*>((char*)workspace + part_bytes +
+                                                    align256((size_t)B * sizeof(float)));
     a.ml = ml;
     const int64_t rows = U * G;
     const int n_oct = (int)((nt + kKeyTiles - 1) / kKeyTiles);
@@ -1217,9 +1240,15 @@ static int key_impl(const uint8_t* codes, const uint32_t* out_ent, const int32_t
                     const float* k_scale, const float* k_zero, const void* k_sink,
                     const float* codebook, int bits, const void* q, const float* inv_freq,
                     int64_t B, int64_t n_heads, int64_t group, int64_t T, int64_t nt_cap,
-                    float* scores, float2* stats, float stat_scale, cudaStream_t st) {
+                    float* scores, float2* stats, float stat_scale, cudaStream_t st,
+                    int64_t pos0 = 0) {
   int rc = check_decode_shape("key_scores", B, n_heads, group, T, nt_cap);
   if (rc) return rc;
+  if (pos0 < 0 || pos0 + T > (1LL << 24)) {  // positions are exact fp32 integers up to 2^24
+    set_error("key_scores: positions [%lld, %lld) outside [0, 2^24]", (long long)pos0,
+              (long long)(pos0 + T));
+    return KVQ_ERR_INVALID;
+  }
   KeyArgs a{};
   a.codes = codes; a.out_ent = out_ent; a.out_ptr = out_ptr; a.k_scale = k_scale;
   a.k_zero = k_zero; a.k_sink = (const __half*)k_sink; a.cb = codebook; a.q = (const __half*)q;
@@ -1227,6 +1256,7 @@ static int key_impl(const uint8_t* codes, const uint32_t* out_ent, const int32_t
   a.scores = scores;
   a.stats = stats;
   a.stat_scale = stat_scale;
+  a.pos0 = pos0;
   switch (group) {
     case 1: return dispatch_key_bits<1>(bits, a, st);
     case 2: return dispatch_key_bits<2>(bits, a, st);
@@ -1268,6 +1298,23 @@ extern "C" int kvq_key_scores_stats(const uint8_t* codes, const uint32_t* out_en
   return kvq::key_impl(codes, out_ent, out_ptr, k_scale, k_zero, k_sink, codebook, bits, q,
                        inv_freq, B, n_heads, group, T, nt_cap, scores,
                        reinterpret_cast<float2*>(stats), scale, kvq::as_stream(stream));
+}
+
+extern "C" int kvq_key_scores_stats_at(const uint8_t* codes, const uint32_t* out_ent,
+                                       const int32_t* out_ptr, const float* k_scale,
+                                       const float* k_zero, const void* k_sink,
+                                       const float* codebook, int bits, const void* q,
+                                       const float* inv_freq, int64_t B, int64_t n_heads,
+                                       int64_t group, int64_t T, int64_t nt_cap, int64_t pos0,
+                                       float* scores, float scale, void* stats, void* stream) {
+  kvq::clear_error();
+  if (!stats) {
+    kvq::set_error("key_scores_stats_at: stats is NULL");
+    return KVQ_ERR_INVALID;
+  }
+  return kvq::key_impl(codes, out_ent, out_ptr, k_scale, k_zero, k_sink, codebook, bits, q,
+                       inv_freq, B, n_heads, group, T, nt_cap, scores,
+                       reinterpret_cast<float2*>(stats), scale, kvq::as_stream(stream), pos0);
 }
 
 extern "C" size_t kvq_softmax_workspace(int64_t rows, int64_t T) {
@@ -1321,6 +1368,41 @@ extern "C" int kvq_value_output_scores(const uint8_t* codes, const uint32_t* out
                          bits, scores, B, n_heads, group, T, nt_cap, out, workspace,
                          workspace_bytes, kvq::as_stream(stream),
                          reinterpret_cast<const float2*>(stats), scale);
+}
+
+extern "C" int kvq_value_output_scores_ml(const uint8_t* codes, const uint32_t* out_ent,
+                                          const int32_t* out_ptr, const float* v_scale,
+                                          const float* v_zero, int64_t ld_stats,
+                                          const void* v_sink, const float* codebook, int bits,
+                                          const float* scores, const void* stats, float scale,
+                                          int64_t B, int64_t n_heads, int64_t group, int64_t T,
+                                          int64_t nt_cap, void* out, float* ml_out,
+                                          void* workspace, size_t workspace_bytes, void* stream) {
+  kvq::clear_error();
+  if (!stats || !ml_out) {
+    kvq::set_error("value_output_scores_ml: stats and ml_out are required");
+    return KVQ_ERR_INVALID;
+  }
+  return kvq::value_impl(codes, out_ent, out_ptr, v_scale, v_zero, ld_stats, v_sink, codebook,
+                         bits, scores, B, n_heads, group, T, nt_cap, out, workspace,
+                         workspace_bytes, kvq::as_stream(stream),
+                         reinterpret_cast<const float2*>(stats), scale,
+                         reinterpret_cast<float2*>(ml_out));
+}
+
+extern "C" int kvq_merge_shards(const void* o_shards, const float* ml_shards, int64_t n_shards,
+                                int64_t rows, void* out, void* stream) {
+  kvq::clear_error();
+  if (n_shards < 1 || rows < 0 || rows > (1LL << 31) - 1 || !o_shards || !ml_shards || !out) {
+    kvq::set_error("merge_shards: invalid arguments (n_shards=%lld, rows=%lld)",
+                   (long long)n_shards, (long long)rows);
+    return KVQ_ERR_INVALID;
+  }
+  if (rows == 0) return KVQ_OK;
+  kvq::merge_shards_kernel<<<(unsigned)rows, kvq::kHeadDim, 0, kvq::as_stream(stream)>>>(
+      (const __half*)o_shards, reinterpret_cast<const float2*>(ml_shards), n_shards, rows,
+      (__half*)out);
+  return kvq::check_launch("merge_shards");
 }
 
 extern "C" size_t kvq_decode_attention_workspace(int64_t B, int64_t n_heads, int64_t group,

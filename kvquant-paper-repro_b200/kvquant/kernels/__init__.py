@@ -4,7 +4,8 @@ from .matvec_ds import dense_matvec_lut, sparse_matvec, sparse_matvec_csr
 from .cuda_ops import get_cuda_ops, cuda_available
 from .decode import (quantize_keys, quantize_values, qk_scores, qk_scores_stats, softmax,
                      pv_out, pv_out_scores, decode_attention, make_appendable, append_keys,
-                     append_values, key_outlier_thresholds)
+                     append_values, key_outlier_thresholds, decode_attention_shard,
+                     merge_shards)
 
 __all__ = [
     "apply_rope_elementwise",
@@ -27,4 +28,6 @@ __all__ = [
     "append_keys",
     "append_values",
     "key_outlier_thresholds",
+    "decode_attention_shard",
+    "merge_shards",
 ]

@@ -67,6 +67,13 @@ _SIGNATURES = {
     "kvq_value_output_scores": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p, _c_p,
                                          _c_int, _c_p, _c_p, _c_flt, _c_i64, _c_i64, _c_i64,
                                          _c_i64, _c_i64, _c_p, _c_p, _c_size, _c_p]),
+    "kvq_key_scores_stats_at": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_int,
+                                         _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+                                         _c_i64, _c_p, _c_flt, _c_p, _c_p]),
+    "kvq_value_output_scores_ml": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p, _c_p,
+                                            _c_int, _c_p, _c_p, _c_flt, _c_i64, _c_i64, _c_i64,
+                                            _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_size, _c_p]),
+    "kvq_merge_shards": (_c_int, [_c_p, _c_p, _c_i64, _c_i64, _c_p, _c_p]),
     "kvq_softmax_workspace": (_c_size, [_c_i64, _c_i64]),
     "kvq_softmax": (_c_int, [_c_p, _c_i64, _c_i64, _c_flt, _c_p, _c_p, _c_size, _c_p]),
     "kvq_value_output_workspace": (_c_size, [_c_i64, _c_i64, _c_i64, _c_i64]),

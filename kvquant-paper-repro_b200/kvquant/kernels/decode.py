@@ -224,13 +224,15 @@ def pv_out(probs: torch.Tensor, packed_v: dict, length: int | None = None) -> to
 
 def qk_scores_stats(q: torch.Tensor, packed_k: dict, inv_freq: torch.Tensor,
                     length: int | None = None, scale: float | None = None,
-                    out: torch.Tensor | None = None, stats_out: torch.Tensor | None = None):
+                    out: torch.Tensor | None = None, stats_out: torch.Tensor | None = None,
+                    pos0: int = 0):
     """qk_scores plus the key kernel's softmax partials of softmax(scores * scale).
 
     Returns (scores fp32 [B, Hq, T], stats fp32 [B*Hq, ceil(T/256), 2]) where
     stats[row, k] = (max over the k-th 256-token chunk of scores * scale,
     sum over that chunk of exp(scores * scale - max)). pv_out_scores turns the
-    pair back into the softmax of the whole row.
+    pair back into the softmax of the whole row. pos0: RoPE position of the
+    cache's token 0 (a token-range shard of a longer context).
     """
     lib = get_cuda_ops().lib
     qc = q.to(torch.float16).contiguous()
@@ -251,20 +253,32 @@ def qk_scores_stats(q: torch.Tensor, packed_k: dict, inv_freq: torch.Tensor,
             or stats.dtype != torch.float32 or not stats.is_contiguous()):
         raise RuntimeError("qk_scores_stats: out / stats_out do not match the shapes")
     with torch.cuda.device(qc.device):
-        _check(lib.kvq_key_scores_stats(
-            _ptr(packed_k["q_idx"]), _ptr(packed_k["outlier_entries"]),
-            _ptr(packed_k["outlier_rowptr"]), _ptr(packed_k["scale"]), _ptr(packed_k["zero"]),
-            _ptr(packed_k["sink"]), _ptr(packed_k["codebook"]), packed_k["bits"], _ptr(qc),
-            _ptr(f), B, packed_k["n_heads"], G, T, packed_k["q_idx"].shape[1], _ptr(scores),
-            scale, _ptr(stats), _stream(qc)), lib)
+        if pos0:
+            _check(lib.kvq_key_scores_stats_at(
+                _ptr(packed_k["q_idx"]), _ptr(packed_k["outlier_entries"]),
+                _ptr(packed_k["outlier_rowptr"]), _ptr(packed_k["scale"]),
+                _ptr(packed_k["zero"]), _ptr(packed_k["sink"]), _ptr(packed_k["codebook"]),
+                packed_k["bits"], _ptr(qc), _ptr(f), B, packed_k["n_heads"], G, T,
+                packed_k["q_idx"].shape[1], int(pos0), _ptr(scores), scale, _ptr(stats),
+                _stream(qc)), lib)
+        else:
+            _check(lib.kvq_key_scores_stats(
+                _ptr(packed_k["q_idx"]), _ptr(packed_k["outlier_entries"]),
+                _ptr(packed_k["outlier_rowptr"]), _ptr(packed_k["scale"]),
+                _ptr(packed_k["zero"]), _ptr(packed_k["sink"]), _ptr(packed_k["codebook"]),
+                packed_k["bits"], _ptr(qc), _ptr(f), B, packed_k["n_heads"], G, T,
+                packed_k["q_idx"].shape[1], _ptr(scores), scale, _ptr(stats), _stream(qc)), lib)
     return scores, stats
 
 
 def pv_out_scores(scores: torch.Tensor, stats: torch.Tensor, packed_v: dict,
-                  scale: float | None = None) -> torch.Tensor:
+                  scale: float | None = None, ml_out: torch.Tensor | None = None,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
     """Value kernel on raw scores: sum_t softmax(scores * scale)[t] * Vhat_t, fp16 [B, Hq, 128].
 
-    `stats` comes from qk_scores_stats with the same scale.
+    `stats` comes from qk_scores_stats with the same scale. ml_out (fp32
+    [B*Hq, 2], optional) receives each row's softmax stats (M, 1/L), which
+    merge_shards needs to combine token-range shards.
     """
     lib = get_cuda_ops().lib
     s = scores.contiguous()
@@ -279,15 +293,63 @@ def pv_out_scores(scores: torch.Tensor, stats: torch.Tensor, packed_v: dict,
     st = stats.contiguous()
     if st.dtype != torch.float32 or st.numel() * 4 != lib.kvq_key_stats_size(B * Hq, T):
         raise RuntimeError("pv_out_scores: stats do not match the scores")
-    out = torch.empty((B, Hq, HEAD_DIM), dtype=torch.float16, device=s.device)
+    if out is None:
+        out = torch.empty((B, Hq, HEAD_DIM), dtype=torch.float16, device=s.device)
+    if ml_out is not None and (ml_out.dtype != torch.float32 or not ml_out.is_contiguous()
+                               or ml_out.numel() != B * Hq * 2):
+        raise RuntimeError("pv_out_scores: ml_out must be contiguous fp32 [B*Hq, 2]")
     with torch.cuda.device(s.device):
         ws = _workspace(lib.kvq_value_output_scores_workspace(B, H, G, T), s.device)
-        _check(lib.kvq_value_output_scores(
-            _ptr(packed_v["q_idx"]), _ptr(packed_v["outlier_entries"]),
-            _ptr(packed_v["outlier_rowptr"]), _ptr(packed_v["scale"]), _ptr(packed_v["zero"]),
-            packed_v["scale"].shape[1], _ptr(packed_v["sink"]), _ptr(packed_v["codebook"]),
-            packed_v["bits"], _ptr(s), _ptr(st), scale, B, H, G, T, packed_v["q_idx"].shape[1],
-            _ptr(out), _ptr(ws), ws.numel(), _stream(s)), lib)
+        args = (_ptr(packed_v["q_idx"]), _ptr(packed_v["outlier_entries"]),
+                _ptr(packed_v["outlier_rowptr"]), _ptr(packed_v["scale"]), _ptr(packed_v["zero"]),
+                packed_v["scale"].shape[1], _ptr(packed_v["sink"]), _ptr(packed_v["codebook"]),
+                packed_v["bits"], _ptr(s), _ptr(st), scale, B, H, G, T,
+                packed_v["q_idx"].shape[1], _ptr(out))
+        if ml_out is None:
+            _check(lib.kvq_value_output_scores(*args, _ptr(ws), ws.numel(), _stream(s)), lib)
+        else:
+            _check(lib.kvq_value_output_scores_ml(*args, _ptr(ml_out), _ptr(ws), ws.numel(),
+                                                  _stream(s)), lib)
+    return out
+
+
+def decode_attention_shard(q: torch.Tensor, packed_k: dict, packed_v: dict,
+                           inv_freq: torch.Tensor, pos0: int, scores: torch.Tensor | None = None,
+                           stats: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                           ml_out: torch.Tensor | None = None):
+    """One decode step over a token-range shard: the cache holds the tokens at
+    positions [pos0, pos0 + length) (its token 0 is the sink only when pos0 == 0).
+    Returns (o fp16 [B, Hq, 128] normalized over the shard's tokens, ml fp32
+    [B*Hq, 2] = the shard's softmax row stats); merge_shards combines shards."""
+    qc = q.to(torch.float16).contiguous()
+    B, Hq, _ = qc.shape
+    if ml_out is None:
+        ml_out = torch.empty((B * Hq, 2), dtype=torch.float32, device=qc.device)
+    sc, st = qk_scores_stats(qc, packed_k, inv_freq, out=scores, stats_out=stats, pos0=pos0)
+    o = pv_out_scores(sc, st, packed_v, ml_out=ml_out, out=out)
+    return o, ml_out
+
+
+def merge_shards(o_shards: torch.Tensor, ml_shards: torch.Tensor,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """Output over the whole context from n token-range shards.
+
+    o_shards fp16 [n, B, Hq, 128] and ml_shards fp32 [n, B*Hq, 2] as returned
+    by decode_attention_shard on each shard (e.g. all-gathered across ranks).
+    """
+    lib = get_cuda_ops().lib
+    o = o_shards.contiguous()
+    ml = ml_shards.contiguous()
+    if o.dtype != torch.float16 or ml.dtype != torch.float32 or o.shape[-1] != HEAD_DIM:
+        raise RuntimeError("merge_shards: expected fp16 outputs [n, ..., 128] and fp32 stats")
+    n = o.shape[0]
+    rows = o[0].numel() // HEAD_DIM
+    if ml.numel() != n * rows * 2:
+        raise RuntimeError("merge_shards: stats do not match the outputs")
+    if out is None:
+        out = torch.empty(o.shape[1:], dtype=torch.float16, device=o.device)
+    with torch.cuda.device(o.device):
+        _check(lib.kvq_merge_shards(_ptr(o), _ptr(ml), n, rows, _ptr(out), _stream(o)), lib)
     return out
 
 

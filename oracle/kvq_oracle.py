@@ -288,8 +288,8 @@ def sparse_matvec_csr(row_ptr, col_idx, values, vec):
 # --------------------------------------------------------------------------
 # Decode attention restated on the reference's dequantized cache
 # --------------------------------------------------------------------------
-def key_scores(q, k_hat, n_kv_heads: int, inv_freq):
-    """Raw scores s[b,h,t] = q[b,h] . RoPE_t(K_hat[b,t,kvh]) in float64.
+def key_scores(q, k_hat, n_kv_heads: int, inv_freq, pos0: int = 0):
+    """Raw scores s[b,h,t] = q[b,h] . RoPE_{pos0+t}(K_hat[b,t,kvh]) in float64.
 
     K_hat is the reference's fake-quant output (kv_quantizer.py:72-94, fp16),
     RoPE uses the fp32 angle tables of rope_fused.py:6-12 (the CUDA-path
@@ -300,9 +300,9 @@ def key_scores(q, k_hat, n_kv_heads: int, inv_freq):
     B, Hq, D = q.shape
     T = k_hat.shape[1]
     half = D // 2
-    cos, sin = rope_cos_sin(T, D, inv_freq=inv_freq)
-    c = cos.astype(np.float64)[None, :, None, :]
-    s = sin.astype(np.float64)[None, :, None, :]
+    cos, sin = rope_cos_sin(pos0 + T, D, inv_freq=inv_freq)
+    c = cos[pos0:].astype(np.float64)[None, :, None, :]
+    s = sin[pos0:].astype(np.float64)[None, :, None, :]
     K = np.asarray(k_hat, dtype=F16).astype(np.float64).reshape(B, T, n_kv_heads, D)
     k1, k2 = K[..., :half], K[..., half:]
     Kr = np.concatenate([k1 * c - k2 * s, k1 * s + k2 * c], axis=-1)  # [B,T,Hkv,D]
@@ -333,6 +333,26 @@ def decode_attention(q, k_hat, v_hat, n_kv_heads: int, inv_freq):
     s = key_scores(q, k_hat, n_kv_heads, inv_freq)
     p = softmax_probs(s, q.shape[-1])
     return s, p, value_output(p, v_hat, n_kv_heads)
+
+
+def decode_shard(q, k_hat, v_hat, n_kv_heads: int, inv_freq, pos0: int):
+    """Decode over the tokens at positions [pos0, pos0 + T) only (restated; the
+    reference has no decode attention): (o normalized over the range, M, L)
+    with M = max of s/sqrt(D) and L = sum of exp(s/sqrt(D) - M) per row."""
+    s = key_scores(q, k_hat, n_kv_heads, inv_freq, pos0)
+    z = s / math.sqrt(q.shape[-1])
+    m = z.max(axis=-1, keepdims=True)
+    e = np.exp(z - m)
+    l = e.sum(axis=-1, keepdims=True)
+    return value_output(e / l, v_hat, n_kv_heads), m[..., 0], l[..., 0]
+
+
+def merge_shards(os_, ms, ls):
+    """Softmax merge of range shards: sum_i w_i o_i / sum_i w_i, w_i = L_i e^(M_i - M)."""
+    m = np.max(np.stack(ms), axis=0)
+    w = [l * np.exp(mi - m) for mi, l in zip(ms, ls)]
+    num = sum(wi[..., None] * oi for wi, oi in zip(w, os_))
+    return num / sum(w)[..., None]
 
 
 # --------------------------------------------------------------------------

@@ -1,0 +1,72 @@
+"""GPU parity of token-range shards of a decode step (position offset, row
+stats, merge) against the oracle's decode over the whole context."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import kvq_oracle as O
+import synth
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3
+
+
+def t(x, dev):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+
+
+def rel_l2(got, ref):
+    got, ref = np.asarray(got, np.float64), np.asarray(ref, np.float64)
+    return np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30)
+
+
+@pytest.mark.parametrize("G,bits,cuts", [(1, 4, (0, 256, 700)), (2, 3, (0, 300, 512, 833)),
+                                         (4, 2, (0, 131072, 131072 + 999))])
+def test_shards_merge_to_the_whole_decode(cuda, G, bits, cuts):
+    """Every shard is quantized as its own block (the first with the sink),
+    decoded with its positions and merged; the oracle dequantizes the same
+    blocks and decodes the whole context."""
+    from kvquant.kernels import (quantize_keys, quantize_values, decode_attention_shard,
+                                 merge_shards, rope_inv_freq)
+    B, Hkv, ratio = 1, 2, 0.01
+    T = cuts[-1]
+    k, v = synth.make_kv(B, T, Hkv * 128, seed=61 + bits)
+    scale, zero = synth.key_calibration(k)
+    rng = np.random.default_rng(bits)
+    cbk = np.sort(rng.uniform(-1, 1, 1 << bits)).astype(np.float32)
+    cbv = np.sort(rng.uniform(-1, 1, 1 << bits)).astype(np.float32)
+    q = (synth.make_query(B, Hkv * G, 128, seed=5).astype(np.float32) * 0.25).astype(np.float16)
+    inv = rope_inv_freq(128, 10000.0)
+    os_, mls, k_hat, v_hat = [], [], [], []
+    for a, b in zip(cuts, cuts[1:]):
+        sink = a == 0
+        pk = quantize_keys(t(k[:, a:b], cuda), t(scale, cuda), t(zero, cuda), t(cbk, cuda), bits,
+                           ratio, sink)
+        pv = quantize_values(t(v[:, a:b], cuda), t(cbv, cuda), bits, ratio, sink)
+        o, ml = decode_attention_shard(t(q, cuda), pk, pv, inv, pos0=a)
+        os_.append(o)
+        mls.append(ml)
+        k_hat.append(O.quantize_k(k[:, a:b], cbk, scale, zero, ratio, sink)["dequant"])
+        v_hat.append(O.quantize_v(v[:, a:b], cbv, ratio, sink)["dequant"])
+    out = merge_shards(torch.stack(os_), torch.stack(mls)).cpu().numpy()
+    _, _, ref = O.decode_attention(q, np.concatenate(k_hat, 1), np.concatenate(v_hat, 1), Hkv,
+                                   O.rope_inv_freq(128, 10000.0))
+    assert rel_l2(out, ref) <= TOL, rel_l2(out, ref)
+
+
+def test_single_shard_at_zero_is_decode_attention(cuda):
+    from kvquant.kernels import (quantize_keys, quantize_values, decode_attention,
+                                 decode_attention_shard, merge_shards, rope_inv_freq)
+    k, v = synth.make_kv(2, 300, 256, seed=71)
+    scale, zero = synth.key_calibration(k)
+    cb = t(np.linspace(-1, 1, 16).astype(np.float32), cuda)
+    pk = quantize_keys(t(k, cuda), t(scale, cuda), t(zero, cuda), cb, 4, 0.01, True)
+    pv = quantize_values(t(v, cuda), cb, 4, 0.01, True)
+    q = t(synth.make_query(2, 2, 128, seed=2), cuda)
+    inv = rope_inv_freq(128, 10000.0)
+    full = decode_attention(q, pk, pv, inv)
+    o, ml = decode_attention_shard(q, pk, pv, inv, pos0=0)
+    torch.testing.assert_close(o, full, rtol=0, atol=0)
+    merged = merge_shards(o[None], ml[None])
+    assert (merged.float() - full.float()).abs().max().item() <= 1e-3 * full.float().abs().max().item()

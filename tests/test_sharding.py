@@ -85,3 +85,64 @@ def test_two_rank_gather_matches_single_process(tmp_path):
     _, _, ref = O.decode_attention(q, kh, vh, Hkv, O.rope_inv_freq(128, 10000.0))
     assert got.shape == ref.shape
     np.testing.assert_allclose(got, ref, rtol=1e-6, atol=1e-7)
+
+
+# ---------------------------------------------------------------------------
+# Token-range sharding
+# ---------------------------------------------------------------------------
+def test_shard_tokens_partition():
+    from kvquant.sharding import shard_tokens
+    for T, world in ((4096, 1), (4096, 2), (1 << 20, 8), (1000, 3), (2049, 8)):
+        got = [shard_tokens(T, world, r) for r in range(world)]
+        assert got[0][0] == 0 and got[-1][1] == T
+        assert all(a[1] == b[0] for a, b in zip(got, got[1:]))
+        assert all(t1 > t0 and t0 % 256 == 0 for t0, t1 in got)
+    with pytest.raises(ValueError):
+        shard_tokens(300, 4, 0)
+
+
+def test_oracle_shard_merge_is_the_whole_decode():
+    q, kh, vh, Hkv, G = _case(T=200)
+    inv = O.rope_inv_freq(128, 10000.0)
+    _, _, ref = O.decode_attention(q, kh, vh, Hkv, inv)
+    parts = [O.decode_shard(q, kh[:, a:b], vh[:, a:b], Hkv, inv, a) for a, b in ((0, 77), (77, 200))]
+    got = O.merge_shards(*zip(*parts))
+    np.testing.assert_allclose(got, ref, rtol=1e-10, atol=1e-12)
+
+
+def _token_rank_main(rank, world, port, out_path):
+    import torch.distributed as dist
+    from kvquant.sharding import shard_tokens, gather_shard_partials
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        q, kh, vh, Hkv, G = _case(T=600)
+        t0, t1 = shard_tokens(kh.shape[1], world, rank)
+        o, m, l = O.decode_shard(q, kh[:, t0:t1], vh[:, t0:t1], Hkv,
+                                 O.rope_inv_freq(128, 10000.0), t0)
+        B, Hq = o.shape[:2]
+        o_t = torch.from_numpy(np.ascontiguousarray(o, dtype=np.float32))
+        ml_t = torch.from_numpy(np.stack([m.reshape(-1), 1.0 / l.reshape(-1)], -1).astype(np.float32))
+        o_buf = torch.empty((world, B, Hq, 128), dtype=torch.float32)
+        ml_buf = torch.empty((world, B * Hq, 2), dtype=torch.float32)
+        gather_shard_partials(o_t, ml_t, o_buf, ml_buf)
+        if rank == 0:
+            ms = [ml_buf[i, :, 0].numpy().astype(np.float64).reshape(B, Hq) for i in range(world)]
+            ls = [1.0 / ml_buf[i, :, 1].numpy().astype(np.float64).reshape(B, Hq) for i in range(world)]
+            merged = O.merge_shards([o_buf[i].numpy().astype(np.float64) for i in range(world)], ms, ls)
+            np.save(out_path, merged)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_token_shards_match_single_process(tmp_path):
+    """Each rank decodes its token range (positions offset), the shard outputs
+    and row stats are all-gathered with the helper bench.py uses and merged."""
+    import torch.multiprocessing as mp
+    out_path = str(tmp_path / "merged.npy")
+    mp.spawn(_token_rank_main, args=(2, _free_port(), out_path), nprocs=2, join=True)
+    got = np.load(out_path)
+    q, kh, vh, Hkv, G = _case(T=600)
+    _, _, ref = O.decode_attention(q, kh, vh, Hkv, O.rope_inv_freq(128, 10000.0))
+    np.testing.assert_allclose(got, ref, rtol=2e-6, atol=1e-6)
