@@ -435,7 +435,8 @@ def run_gpu(args):
                 q_dev[l].copy_(q_host[l], non_blocking=True)
                 if tok_split:
                     o, ml = decode_attention_shard(q_dev[l], pk, pv, inv, pos0=t0, scores=scores,
-                                                   stats=stats, out=outs[l], ml_out=mls[l])
+                                                   stats=stats, out=outs[l], ml_out=mls[l],
+                                                   workspace=wsp)
                     handles.append((l, gather_shard_partials(o, ml, o_buf[l], ml_buf[l],
                                                              async_op=True)))
                     continue

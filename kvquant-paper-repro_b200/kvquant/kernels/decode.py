@@ -273,7 +273,8 @@ def qk_scores_stats(q: torch.Tensor, packed_k: dict, inv_freq: torch.Tensor,
 
 def pv_out_scores(scores: torch.Tensor, stats: torch.Tensor, packed_v: dict,
                   scale: float | None = None, ml_out: torch.Tensor | None = None,
-                  out: torch.Tensor | None = None) -> torch.Tensor:
+                  out: torch.Tensor | None = None,
+                  workspace: "DecodeWorkspace | None" = None) -> torch.Tensor:
     """Value kernel on raw scores: sum_t softmax(scores * scale)[t] * Vhat_t, fp16 [B, Hq, 128].
 
     `stats` comes from qk_scores_stats with the same scale. ml_out (fp32
@@ -299,7 +300,8 @@ def pv_out_scores(scores: torch.Tensor, stats: torch.Tensor, packed_v: dict,
                                or ml_out.numel() != B * Hq * 2):
         raise RuntimeError("pv_out_scores: ml_out must be contiguous fp32 [B*Hq, 2]")
     with torch.cuda.device(s.device):
-        ws = _workspace(lib.kvq_value_output_scores_workspace(B, H, G, T), s.device)
+        need = lib.kvq_value_output_scores_workspace(B, H, G, T)
+        ws = workspace.get(need, s.device) if workspace is not None else _workspace(need, s.device)
         args = (_ptr(packed_v["q_idx"]), _ptr(packed_v["outlier_entries"]),
                 _ptr(packed_v["outlier_rowptr"]), _ptr(packed_v["scale"]), _ptr(packed_v["zero"]),
                 packed_v["scale"].shape[1], _ptr(packed_v["sink"]), _ptr(packed_v["codebook"]),
@@ -316,7 +318,8 @@ def pv_out_scores(scores: torch.Tensor, stats: torch.Tensor, packed_v: dict,
 def decode_attention_shard(q: torch.Tensor, packed_k: dict, packed_v: dict,
                            inv_freq: torch.Tensor, pos0: int, scores: torch.Tensor | None = None,
                            stats: torch.Tensor | None = None, out: torch.Tensor | None = None,
-                           ml_out: torch.Tensor | None = None):
+                           ml_out: torch.Tensor | None = None,
+                           workspace: "DecodeWorkspace | None" = None):
     """One decode step over a token-range shard: the cache holds the tokens at
     positions [pos0, pos0 + length) (its token 0 is the sink only when pos0 == 0).
     Returns (o fp16 [B, Hq, 128] normalized over the shard's tokens, ml fp32
@@ -326,7 +329,7 @@ def decode_attention_shard(q: torch.Tensor, packed_k: dict, packed_v: dict,
     if ml_out is None:
         ml_out = torch.empty((B * Hq, 2), dtype=torch.float32, device=qc.device)
     sc, st = qk_scores_stats(qc, packed_k, inv_freq, out=scores, stats_out=stats, pos0=pos0)
-    o = pv_out_scores(sc, st, packed_v, ml_out=ml_out, out=out)
+    o = pv_out_scores(sc, st, packed_v, ml_out=ml_out, out=out, workspace=workspace)
     return o, ml_out
 
 
