@@ -146,3 +146,22 @@ def test_two_rank_token_shards_match_single_process(tmp_path):
     q, kh, vh, Hkv, G = _case(T=600)
     _, _, ref = O.decode_attention(q, kh, vh, Hkv, O.rope_inv_freq(128, 10000.0))
     np.testing.assert_allclose(got, ref, rtol=2e-6, atol=1e-6)
+
+
+def test_bench_shard_mode():
+    """bench.py keeps KV-head sharding while every rank has >= 16 heads."""
+    import argparse
+    import importlib.util
+    from pathlib import Path
+    spec = importlib.util.spec_from_file_location("bench", Path(__file__).resolve().parent.parent / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    from kvquant import synthetic as syn
+    wl = syn.WORKLOADS["longctx-1m-4bit"]
+    auto = argparse.Namespace(shard="auto")
+    assert [bench.shard_mode(auto, wl, n) for n in (1, 2, 4, 8)] == ["heads", "heads", "tokens", "tokens"]
+    assert bench.shard_mode(argparse.Namespace(shard="heads"), wl, 8) == "heads"
+    cfg = bench.bench_config(wl, 32, 8, "tokens")
+    assert cfg["sharding"].startswith("token ranges / 8 GPUs")
+    assert not bench.flush_l2_needed(wl, 32, 8)
+    assert bench.flush_l2_needed(syn.WORKLOADS["layer-4k-4bit"], 1, 1)
