@@ -1312,6 +1312,11 @@ extern "C" int kvq_key_scores_stats_at(const uint8_t* codes, const uint32_t* out
     kvq::set_error("key_scores_stats_at: stats is NULL");
     return KVQ_ERR_INVALID;
   }
+  if (k_sink && pos0 != 0) {  // the sink is position 0, scored without rotation
+    kvq::set_error("key_scores_stats_at: a sink token needs pos0 == 0 (got %lld)",
+                   (long long)pos0);
+    return KVQ_ERR_INVALID;
+  }
   return kvq::key_impl(codes, out_ent, out_ptr, k_scale, k_zero, k_sink, codebook, bits, q,
                        inv_freq, B, n_heads, group, T, nt_cap, scores,
                        reinterpret_cast<float2*>(stats), scale, kvq::as_stream(stream), pos0);

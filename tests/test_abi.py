@@ -81,3 +81,17 @@ def test_workspace_queries(lib):
     assert lib.kvq_quantize_keys_workspace(1, 4096, 32) >= 32 * 128 * 256 * 4
     assert lib.kvq_decode_attention_workspace(1, 32, 1, 4096) >= 2 * 32 * 4096 * 4
     assert lib.kvq_softmax_workspace(32, 4096) >= 32 * 8
+
+
+def test_shard_entry_points_reject_bad_arguments(lib):
+    import ctypes as ct
+    # a sink belongs to position 0 only
+    rc = lib.kvq_key_scores_stats_at(None, None, None, None, None, ct.c_void_p(16), None, 4, None,
+                                     None, 1, 1, 1, 64, 2, 32, None, 0.1, ct.c_void_p(16), None)
+    assert rc == 1 and b"pos0" in lib.kvq_last_error()
+    rc = lib.kvq_merge_shards(None, None, 0, 4, None, None)
+    assert rc == 1
+    rc = lib.kvq_value_output_scores_ml(None, None, None, None, None, 64, None, None, 4, None,
+                                        None, 0.1, 1, 1, 1, 64, 2, None, None, None, 0, None)
+    assert rc == 1 and b"ml_out" in lib.kvq_last_error()
+
