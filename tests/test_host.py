@@ -69,3 +69,21 @@ def test_dense_sparse_helpers_follow_reference():
     v, c, rp = pack_csr(x)
     assert rp.tolist() == [0, 1, 1, 3] and c.tolist() == [1, 0, 2]
     assert torch.equal(unpack_csr(v, c, rp, 3, 3, dtype=torch.float32), x)
+
+
+def test_hf_cache_install_and_uninstall():
+    """kvquant.hf_cache hooks a LLaMA model and restores it (no forward pass: the
+    quantize and decode kernels need the GPU)."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+    from kvquant.hf_cache import ATTN_NAME, install, uninstall
+    cfg = LlamaConfig(vocab_size=64, hidden_size=256, intermediate_size=256, num_hidden_layers=2,
+                      num_attention_heads=2, num_key_value_heads=1, head_dim=128)
+    m = LlamaForCausalLM(cfg).eval()
+    m.set_attn_implementation("sdpa")
+    kv = install(m, quantizer=None, max_new_tokens=4)
+    assert m.config._attn_implementation == ATTN_NAME
+    assert kv.get_seq_length() == 0 and len(m._kvq_hooks) == 4
+    assert all(hasattr(layer.self_attn, "_kvq_state") for layer in m.model.layers)
+    uninstall(m)
+    assert m.config._attn_implementation == "sdpa" and not m._kvq_hooks
+    assert not any(hasattr(layer.self_attn, "_kvq_state") for layer in m.model.layers)
