@@ -17,6 +17,7 @@ V) scanned per second over the whole job: batch * tokens * layers / step time,
 step time = max over ranks of CUDA-event time.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+  python bench.py --codebook [--steps K]   (NUQ codebook fitting, offline calibration)
 """
 from __future__ import annotations
 
@@ -51,6 +52,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-append", action="store_true")
+    ap.add_argument("--codebook", action="store_true",
+                    help="benchmark NUQ codebook fitting (offline calibration) instead of decode")
+    ap.add_argument("--codebook-samples", type=int, default=1 << 24)
     ap.add_argument("--shard", choices=["auto", "heads", "tokens"], default="auto",
                     help="multi-GPU split: KV heads, or token ranges of all heads (auto: heads "
                          "while every rank keeps at least 16 KV heads)")
@@ -651,8 +655,136 @@ def run_reference(args):
     }), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# NUQ codebook fitting (offline calibration; --codebook)
+# ---------------------------------------------------------------------------
+CB_METRIC = "NUQ codebook fit (Fisher-weighted 1-D k-means, 16 centres): samples/s"
+CB_BITS = 4
+CB_REFINE = 2
+
+
+def codebook_samples(n: int, seed: int = 0):
+    """Normalised calibration activations in [-1, 1] (two clipped normal modes, like
+    per-channel keys after min/max scaling) with Fisher-like gamma weights."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    half = n // 2
+    x = np.concatenate([rng.normal(-0.2, 0.3, half), rng.normal(0.3, 0.25, n - half)])
+    x = np.clip(x, -1.0, 1.0).astype(np.float32)
+    rng.shuffle(x)
+    w = rng.gamma(2.0, 1.0, n).astype(np.float32)
+    return x, w
+
+
+def codebook_cpu_baseline(x, w, n_cpu: int, log):
+    """The reference's solver (weighted KMeans, n_init=10, max_iter=100) on the host
+    cores, over the first n_cpu samples."""
+    import torch
+    from kvquant.quant.nuq import train_nuq_codebook
+    xs, ws = torch.from_numpy(x[:n_cpu].copy()), torch.from_numpy(w[:n_cpu].copy())
+    train_nuq_codebook(xs[:4096], ws[:4096], n_bits=CB_BITS)  # import / thread-pool warm-up
+    t0 = time.perf_counter()
+    train_nuq_codebook(xs, ws, n_bits=CB_BITS)
+    wall = time.perf_counter() - t0
+    cores = os.cpu_count() or 1
+    log(f"codebook cpu baseline: {n_cpu / wall:.3g} samples/s ({wall:.1f}s)")
+    return {"value": n_cpu / wall, "unit": "samples/s", "cores": cores, "kind": "port",
+            "sample": f"{n_cpu} of the {x.size} samples; train_nuq_codebook on CPU tensors "
+                      f"(scikit-learn KMeans, n_init=10, max_iter=100, the reference's solver), "
+                      f"its default thread pool"}
+
+
+def run_codebook(args):
+    import torch
+    from kvquant.kernels.cuda_ops import _ptr, get_cuda_ops
+    from kvquant.quant.nuq import train_nuq_codebook
+
+    def log(msg):
+        print(msg, file=sys.stderr, flush=True)
+
+    n = int(args.codebook_samples)
+    x, w = codebook_samples(n)
+    if args.impl == "reference":
+        base = codebook_cpu_baseline(x, w, min(n, 1 << 18), log)
+        print(json.dumps({
+            "impl": "reference", "metric": CB_METRIC, "value": base["value"],
+            "unit": "samples/s", "n_gpus": args.gpus, "steps": 1, "warmup": 1,
+            "ms_per_step": n / base["value"] * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"codebook-fit-{n}-samples-4bit"}, "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": "samples/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    dev = torch.device("cuda", 0)
+    lib = get_cuda_ops().lib
+    xd, wd = torch.from_numpy(x).to(dev), torch.from_numpy(w).to(dev)
+    ws = torch.empty(int(lib.kvq_fit_codebook_workspace(n)), dtype=torch.uint8, device=dev)
+    status = torch.zeros(2, dtype=torch.int32, device=dev)
+    out = torch.empty(2 ** CB_BITS, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=dev)  # inputs ~ L2 size: flush
+
+    def fit():
+        rc = lib.kvq_fit_codebook(_ptr(xd), _ptr(wd), n, CB_BITS, CB_REFINE, _ptr(out), _ptr(ws),
+                                  ws.numel(), _ptr(status), stream.cuda_stream)
+        if rc:
+            raise RuntimeError(lib.kvq_last_error().decode())
+
+    for _ in range(max(3, args.warmup)):
+        fit()
+    torch.cuda.synchronize()
+    if int(status[0]):
+        raise RuntimeError("codebook fit reported too few occupied bins")
+    clocks = ClockSampler(0)
+    clocks.start()
+    time.sleep(0.3)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    for a, b in evs:
+        flush.zero_()
+        a.record(stream)
+        fit()
+        b.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    value = n / (ms / 1e3)
+    # end to end through the public API: pinned host samples in, centres back to the host
+    xh, wh = torch.from_numpy(x).pin_memory(), torch.from_numpy(w).pin_memory()
+    e2e_steps = max(2, min(args.steps, 5))
+    train_nuq_codebook(xh.to(dev), wh.to(dev), n_bits=CB_BITS).cpu()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        c = train_nuq_codebook(xh.to(dev, non_blocking=True), wh.to(dev, non_blocking=True),
+                               n_bits=CB_BITS).cpu()
+    e2e = n * e2e_steps / (time.perf_counter() - t0)
+    peak, src = peak_hbm()
+    achieved = 8.0 * n / (ms / 1e3) / 1e9  # x and w read once: the algorithmic bytes
+    base = None if args.no_cpu_baseline else codebook_cpu_baseline(x, w, min(n, 1 << 18), log)
+    print(json.dumps({
+        "metric": CB_METRIC, "value": value, "unit": "samples/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": f"codebook-fit-{n}-samples-4bit", "refine_iters": CB_REFINE,
+                   "l2": "flushed before every fit (256 MiB write)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": None, "peak_source": src,
+                     "note": "whole fit (range, histogram, reduce, solve, 2 x refine + "
+                             "finalize); algorithmic bytes = 8 B per sample, read once"},
+        "cpu_baseline": base, "clocks": clk,
+        "e2e": {"value": e2e, "unit": "samples/s", "h2d_bytes_per_step": 8 * n,
+                "d2h_bytes_per_step": 4 * c.numel()},
+        "gpu_launches": args.steps * (4 + 2 * CB_REFINE)}), flush=True)
+
+
 def main():
     args = parse()
+    if args.codebook:
+        if int(os.environ.get("RANK", "0")) == 0:
+            run_codebook(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

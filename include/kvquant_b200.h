@@ -291,6 +291,27 @@ int kvq_value_output_noalloc(const uint8_t* codes, const uint32_t* out_ent,
                              int bits, const float* probs, int64_t B, int64_t n_heads,
                              int64_t group, int64_t T, int64_t nt_cap, void* out, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * NUQ codebook fitting (offline calibration).
+ * ------------------------------------------------------------------------- */
+
+/* Replaces the KMeans fit of train_nuq_codebook (kvquant/quant/nuq.py:39-44):
+ * the 2^bits centres minimising sum_i w_i (x_i - c(x_i))^2 over x [n] fp32
+ * with weights w [n] fp32 (>= 0, not all 0). Exact 1-D method: weighted
+ * histogram of 8192 bins over [min x, max x], the optimal split of the bins
+ * into 2^bits intervals (dynamic programming), then refine_iters (0..64)
+ * Lloyd steps on the samples. centres: fp32 [2^bits], ascending.
+ * status: int32 [2] (device), written by the call: status[1] = occupied bins;
+ * status[0] = 1 when fewer than 2^bits bins are occupied, in which case
+ * `centres` is not written (the caller applies the reference's few-distinct-
+ * values rule, nuq.py:26-37). bits 1..4; n >= 1; workspace 256-byte aligned,
+ * kvq_fit_codebook_workspace(n) bytes. The reference's degenerate cases
+ * (n = 0, n < 2^bits) are the caller's. */
+size_t kvq_fit_codebook_workspace(int64_t n);
+int kvq_fit_codebook(const float* x, const float* weights, int64_t n, int bits,
+                     int refine_iters, float* centres, void* workspace,
+                     size_t workspace_bytes, int32_t* status, void* stream);
+
 /* Reads and clears the device-side error flag set by kernels that skip
  * out-of-range accesses (synchronizes `stream`). */
 int kvq_check_status(void* stream);

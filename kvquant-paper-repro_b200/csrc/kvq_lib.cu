@@ -7,3 +7,4 @@
 #include "kvq_append.cuh"
 #include "kvq_decode.cuh"
 #include "kvq_noalloc.cuh"
+#include "kvq_codebook.cuh"

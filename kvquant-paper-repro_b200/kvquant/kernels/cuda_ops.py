@@ -90,6 +90,9 @@ _SIGNATURES = {
     "kvq_append_values": (_c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_dbl, _c_p,
                                    _c_int, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p,
                                    _c_i64, _c_p, _c_size, _c_p, _c_p]),
+    "kvq_fit_codebook_workspace": (_c_size, [_c_i64]),
+    "kvq_fit_codebook": (_c_int, [_c_p, _c_p, _c_i64, _c_int, _c_int, _c_p, _c_p, _c_size, _c_p,
+                                  _c_p]),
     "kvq_decode_attention_workspace": (_c_size, [_c_i64, _c_i64, _c_i64, _c_i64]),
     "kvq_decode_attention": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
                                       _c_p, _c_p, _c_p, _c_i64, _c_p, _c_p, _c_int, _c_p,

@@ -1,9 +1,15 @@
 """NUQ codebook fitting (drop-in for kvquant/quant/nuq.py).
 
-Offline calibration, not part of the decode path: a Fisher-weighted 1-D
-k-means with the reference's settings (n_init=10, max_iter=100,
-random_state=0; nuq.py:39-44) and its degenerate-input rules (nuq.py:20-37),
-using the same third-party solver (scikit-learn KMeans).
+Offline calibration, not part of the decode path. ``train_nuq_codebook`` keeps
+the reference's signature and rules:
+
+* CPU tensors: the reference's solver, a Fisher-weighted scikit-learn KMeans
+  with its settings (n_init=10, max_iter=100, random_state=0; nuq.py:39-44)
+  and its degenerate-input rules (nuq.py:20-37);
+* CUDA tensors: ``fit_nuq_codebook_cuda``, the same objective solved on the GPU
+  by the library's exact 1-D method (weighted histogram, optimal interval split,
+  Lloyd refinement; ``kvq_fit_codebook``), with the same degenerate-input rules.
+  The centres come back on the input's device.
 """
 from __future__ import annotations
 
@@ -11,8 +17,62 @@ import numpy as np
 import torch
 
 
+def _pad_sorted(vals: torch.Tensor, n_clusters: int) -> torch.Tensor:
+    """Sorted values padded with their maximum to n_clusters (nuq.py:26-37)."""
+    c = torch.sort(vals.reshape(-1)).values
+    pad = c[-1:].expand(n_clusters - c.numel())
+    return torch.sort(torch.cat([c, pad])).values
+
+
+def fit_nuq_codebook_cuda(activations: torch.Tensor, fisher: torch.Tensor, n_bits: int = 3,
+                          refine_iters: int = 2) -> torch.Tensor:
+    """Weighted 1-D k-means of activations [N] (CUDA) with weights fisher [N] (>= 0)
+    -> sorted fp32 centres [2^n_bits] on the same device.
+
+    Minimises the objective of nuq.py:39-42 (the weights' normalisation to sum 1,
+    nuq.py:23, does not move the centres). n_bits 1..4. Raises RuntimeError when
+    the library is missing, and when at least 2^n_bits distinct values fall into
+    fewer than 2^n_bits of the 8192 histogram bins (values bunched far below the
+    bin width of their range), which the GPU method does not resolve.
+    """
+    from ..kernels.cuda_ops import _check, _ptr, _stream, get_cuda_ops
+
+    if not activations.is_cuda:
+        raise RuntimeError("fit_nuq_codebook_cuda: activations must be a CUDA tensor")
+    lib = get_cuda_ops().lib
+    n_clusters = 2 ** int(n_bits)
+    x = activations.reshape(-1).to(torch.float32).contiguous()
+    w = fisher.reshape(-1).to(device=x.device, dtype=torch.float32).contiguous()
+    if w.numel() != x.numel():
+        raise ValueError(f"fisher has {w.numel()} values for {x.numel()} activations")
+    n = x.numel()
+    if n == 0:
+        return torch.zeros(n_clusters, dtype=torch.float32, device=x.device)
+    if n < n_clusters:
+        return _pad_sorted(x, n_clusters)
+    ws = torch.empty(max(int(lib.kvq_fit_codebook_workspace(n)), 1), dtype=torch.uint8,
+                     device=x.device)
+    status = torch.zeros(2, dtype=torch.int32, device=x.device)
+    out = torch.empty(n_clusters, dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        _check(lib.kvq_fit_codebook(_ptr(x), _ptr(w), n, int(n_bits), int(refine_iters),
+                                    _ptr(out), _ptr(ws), ws.numel(), _ptr(status),
+                                    _stream(x)), lib)
+    flag, occupied = (int(v) for v in status.cpu())
+    if flag:
+        uniq = torch.unique(x)
+        if uniq.numel() < n_clusters:
+            return _pad_sorted(uniq, n_clusters)
+        raise RuntimeError(
+            f"fit_nuq_codebook_cuda: {uniq.numel()} distinct values fall into {occupied} "
+            f"of the 8192 histogram bins, fewer than the {n_clusters} clusters")
+    return out
+
+
 def train_nuq_codebook(activations: torch.Tensor, fisher: torch.Tensor, n_bits: int = 3):
     """activations [N] in [-1, 1], fisher [N] weights -> sorted fp32 centers [2^n_bits]."""
+    if activations.is_cuda:
+        return fit_nuq_codebook_cuda(activations, fisher, n_bits)
     from sklearn.cluster import KMeans
 
     n_clusters = 2 ** n_bits

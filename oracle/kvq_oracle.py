@@ -592,3 +592,71 @@ def decode_packed(q, k_hat_units, v_hat_units, inv_freq, group: int = 1):
         p /= p.sum(axis=1, keepdims=True)
         out[u * group:(u + 1) * group] = p @ v_hat_units[u].astype(F32)
     return out
+
+
+# --------------------------------------------------------------------------
+# NUQ codebook fitting (offline calibration)
+# --------------------------------------------------------------------------
+def codebook_degenerate(x, n_bits: int):
+    """train_nuq_codebook's rules for empty input, fewer samples than clusters and
+    fewer distinct values than clusters (kvquant/quant/nuq.py:20-37); None when the
+    reference would run KMeans."""
+    K = 2 ** n_bits
+    x = np.asarray(x, dtype=F32).reshape(-1)
+    if x.size == 0:
+        return np.zeros(K, dtype=F32)
+    if x.size < K:
+        c = np.sort(x)
+        return np.sort(np.concatenate([c, np.full(K - c.size, c[-1])])).astype(F32)
+    u = np.unique(x)
+    if u.size < K:
+        return np.sort(np.concatenate([u, np.full(K - u.size, u[-1])])).astype(F32)
+    return None
+
+
+def kmeans_1d_inertia(x, w, centres) -> float:
+    """sum_i w_i min_k (x_i - c_k)^2 in float64: the objective of the reference's
+    weighted KMeans (kvquant/quant/nuq.py:39-42)."""
+    x = np.asarray(x, dtype=np.float64).reshape(-1, 1)
+    w = np.asarray(w, dtype=np.float64).reshape(-1)
+    c = np.asarray(centres, dtype=np.float64).reshape(1, -1)
+    return float(np.sum(w * np.min((x - c) ** 2, axis=1)))
+
+
+def kmeans_1d_optimal(x, w, K: int) -> np.ndarray:
+    """Global optimum of the weighted 1-D k-means objective (kvquant/quant/nuq.py:39-42).
+
+    The optimal clusters are intervals of the sorted distinct values; dynamic
+    programming over them, O(K n^2) time and O(n^2) memory: small n only.
+    Returns the K centres ascending (fewer if there are fewer distinct values).
+    """
+    x = np.asarray(x, dtype=np.float64).reshape(-1)
+    w = np.asarray(w, dtype=np.float64).reshape(-1)
+    u, inv = np.unique(x, return_inverse=True)
+    wu = np.bincount(inv, weights=w, minlength=u.size)
+    n = u.size
+    PW = np.concatenate([[0.0], np.cumsum(wu)])
+    PS = np.concatenate([[0.0], np.cumsum(wu * u)])
+    i = np.arange(n + 1)[:, None]
+    j = np.arange(n + 1)[None, :]
+    Wij = PW[j] - PW[i]
+    Sij = PS[j] - PS[i]
+    with np.errstate(divide="ignore", invalid="ignore"):
+        gain = np.where(Wij > 0, Sij * Sij / np.where(Wij > 0, Wij, 1.0), 0.0)
+    gain = np.where(i <= j, gain, -np.inf)
+    D = gain[0].copy()
+    args = []
+    for _ in range(2, min(K, n) + 1):
+        tot = D[:, None] + gain
+        a = np.argmax(tot, axis=0)
+        D = tot[a, np.arange(n + 1)]
+        args.append(a)
+    centres = []
+    jj = n
+    for a in reversed(args):
+        ii = int(a[jj])
+        centres.append((PS[jj] - PS[ii]) / (PW[jj] - PW[ii]) if PW[jj] > PW[ii] else np.nan)
+        jj = ii
+    centres.append(PS[jj] / PW[jj] if PW[jj] > 0 else np.nan)
+    c = np.array(centres[::-1])
+    return c[~np.isnan(c)]
