@@ -65,7 +65,7 @@ inline CbLayout cb_layout(int64_t n) {
   L.hist = take(sizeof(float) * 2 * kCbBins * (size_t)G);
   L.wsum = take(sizeof(double) * kCbBins);
   L.ssum = take(sizeof(double) * kCbBins);
-  L.drow = take(sizeof(double) * 2 * (kCbBins + 1));
+  L.drow = take(sizeof(double) * (kCbBins + 1));
   L.arg = take(sizeof(int) * (kCbMaxK + 1) * (size_t)(kCbBins + 1));
   L.cen = take(sizeof(double) * kCbMaxK);
   L.ref = take(sizeof(double) * 2 * kCbMaxK * (size_t)(kCbStreamMul * G));
@@ -252,8 +252,10 @@ __device__ __forceinline__ double cb_gain(const double* PW, const double* PS, in
   return wt > 0.0 ? s * s / wt : 0.0;
 }
 
-// 4. Optimal K-interval split of the bins (one CTA). drow: two DP rows of
+// 4. Optimal K-interval split of the bins (one CTA). drow: one DP row of
 // kCbBins+1 doubles; arg[l][j]: best start of the l-th cluster for bins [0, j).
+constexpr size_t kCbSolveSmem =
+    sizeof(double) * 3 * (kCbBins + 1) + ((sizeof(unsigned short) * (kCbBins + 1) + 7) & ~7ul);
 __global__ void __launch_bounds__(kCbSolveThreads, 1)
     cb_solve_kernel(const double* __restrict__ wsum, const double* __restrict__ ssum, int K,
                     const CbBins* __restrict__ bins_in, double* __restrict__ drow,
@@ -262,9 +264,12 @@ __global__ void __launch_bounds__(kCbSolveThreads, 1)
   constexpr int NB = kCbBins;
   constexpr int per = NB / kCbSolveThreads;
   extern __shared__ double cb_solve_sh[];
-  double* PW = cb_solve_sh;           // [NB + 1] prefix weight
-  double* PS = cb_solve_sh + NB + 1;  // [NB + 1] prefix weighted sum
-  __shared__ double wtot[32], stot[32];
+  double* PW = cb_solve_sh;                 // [NB + 1] prefix weight
+  double* PS = cb_solve_sh + (NB + 1);      // [NB + 1] prefix weighted sum
+  double* PV = cb_solve_sh + 2 * (NB + 1);  // [NB + 1] previous DP layer
+  unsigned short* A16 = reinterpret_cast<unsigned short*>(cb_solve_sh + 3 * (NB + 1));
+  __shared__ double wtot[32], stot[32], slot_v[32];
+  __shared__ int slot_i[32];
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   if (status[1] < K) {  // fewer occupied bins than clusters: the host decides
     if (t == 0) status[0] = 1;
@@ -321,41 +326,46 @@ __global__ void __launch_bounds__(kCbSolveThreads, 1)
   __syncthreads();
 
   // Layer 1: one cluster over bins [0, j).
-  for (int j = t; j <= NB; j += kCbSolveThreads) drow[j] = cb_gain(PW, PS, 0, j);
+  for (int j = t; j <= NB; j += kCbSolveThreads) PV[j] = cb_gain(PW, PS, 0, j);
   __syncthreads();
 
   // Layer l: D_l[j] = max_{i <= j} D_{l-1}[i] + gain(i, j), best i monotone in j.
   // j = NB first, then the midpoints j = s(2m+1) for s = NB/2 .. 1, whose split
-  // points lie between those of j - s and j + s (already filled).
+  // points lie between those of j - s and j + s (already filled). Every level uses
+  // the whole block: a group of L threads per midpoint (L = 1024 / midpoints, at
+  // least 1), the group's threads striding its candidate range. D_{l-1} (PV) and the
+  // layer's split points (A16) are in shared memory; D_l goes to `drow`.
   for (int l = 2; l <= K; ++l) {
-    const double* prev = drow + ((l - 2) & 1) * (NB + 1);
-    double* cur = drow + ((l - 1) & 1) * (NB + 1);
     int* A = arg + (size_t)l * (NB + 1);
     if (t == 0) {
-      cur[0] = 0.0;
+      drow[0] = 0.0;
       A[0] = 0;
+      A16[0] = 0;
     }
     for (int s = NB; s >= 1; s >>= 1) {
       const int count = (s == NB) ? 1 : NB / (2 * s);
-      for (int m = warp; m < count; m += kCbSolveThreads / 32) {
+      const int L = count >= kCbSolveThreads ? 1 : kCbSolveThreads / count;
+      for (int base = 0; base < count * L; base += kCbSolveThreads) {
+        const int g = base + t;
+        const int m = g / L, r = g - m * L;
         const int j = (s == NB) ? NB : s * (2 * m + 1);
         int lo = 0, hi = j;
         if (s != NB) {
-          lo = (m == 0) ? 0 : A[j - s];
-          hi = min(A[j + s], j);
+          lo = (m == 0) ? 0 : (int)A16[j - s];
+          hi = min((int)A16[j + s], j);
           if (hi < lo) hi = lo;  // rounding broke monotonicity: scan the lower bound only
         }
         double best = -1.0;
         int bi = lo;
-        for (int i = lo + lane; i <= hi; i += 32) {
-          const double v = prev[i] + cb_gain(PW, PS, i, j);
+#pragma unroll 4
+        for (int i = lo + r; i <= hi; i += L) {
+          const double v = PV[i] + cb_gain(PW, PS, i, j);
           if (v > best) {
             best = v;
             bi = i;
           }
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
+        for (int o = (L < 32 ? L : 32) >> 1; o > 0; o >>= 1) {  // within the group's lanes
           const double ob = __shfl_xor_sync(0xffffffffu, best, o);
           const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
           if (ob > best || (ob == best && oi < bi)) {
@@ -363,11 +373,42 @@ __global__ void __launch_bounds__(kCbSolveThreads, 1)
             bi = oi;
           }
         }
-        if (lane == 0) {
-          cur[j] = best;
+        if (L > 32) {  // count < 32: a single pass, so the barrier is uniform
+          if (lane == 0) {
+            slot_v[warp] = best;
+            slot_i[warp] = bi;
+          }
+          __syncthreads();
+          if (warp == 0) {  // lane q holds warp q's result; midpoint lane / nw owns nw lanes
+            const int nw = L >> 5;
+            double bb = slot_v[lane];
+            int ii = slot_i[lane];
+            for (int o = nw >> 1; o > 0; o >>= 1) {
+              const double ob = __shfl_xor_sync(0xffffffffu, bb, o);
+              const int oi = __shfl_xor_sync(0xffffffffu, ii, o);
+              if (ob > bb || (ob == bb && oi < ii)) {
+                bb = ob;
+                ii = oi;
+              }
+            }
+            if ((lane & (nw - 1)) == 0) {
+              const int mm = lane / nw;
+              const int jj = (s == NB) ? NB : s * (2 * mm + 1);
+              drow[jj] = bb;
+              A[jj] = ii;
+              A16[jj] = (unsigned short)ii;
+            }
+          }
+        } else if (r == 0) {
+          drow[j] = best;
           A[j] = bi;
+          A16[j] = (unsigned short)bi;
         }
       }
+      __syncthreads();
+    }
+    if (l < K) {
+      for (int j = t; j <= NB; j += kCbSolveThreads) PV[j] = drow[j];
       __syncthreads();
     }
   }
@@ -423,23 +464,28 @@ __global__ void __launch_bounds__(kCbRefineThreads) cb_refine_kernel(
 }
 
 // 5b. New centres = old + sum w*(x - c) / sum w (an empty cluster keeps its centre).
-__global__ void cb_finalize_kernel(const double* __restrict__ part, int G, int K,
-                                   double* __restrict__ centres, float* __restrict__ out,
-                                   const int32_t* __restrict__ status) {
+// One warp per cluster (lanes stride the CTAs' partials), kCbMaxK warps.
+__global__ void __launch_bounds__(32 * kCbMaxK) cb_finalize_kernel(
+    const double* __restrict__ part, int G, int K, double* __restrict__ centres,
+    float* __restrict__ out, const int32_t* __restrict__ status) {
   if (status[0]) return;
   __shared__ double cn[kCbMaxK];
-  const int k = threadIdx.x;
+  const int k = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (k < K) {
     double W = 0.0, D = 0.0;
-    for (int g = 0; g < G; ++g) {
+    for (int g = lane; g < G; g += 32) {
       W += part[(size_t)g * 2 * K + k];
       D += part[(size_t)g * 2 * K + K + k];
     }
-    const double c = (double)(float)centres[k];
-    cn[k] = W > 0.0 ? c + D / W : centres[k];
+    W = warp_sum_d(W);
+    D = warp_sum_d(D);
+    if (lane == 0) {
+      const double c = (double)(float)centres[k];
+      cn[k] = W > 0.0 ? c + D / W : centres[k];
+    }
   }
   __syncthreads();
-  if (k == 0) {  // a Lloyd step keeps 1-D centres in order; sort anyway for the output
+  if (threadIdx.x == 0) {  // a Lloyd step keeps 1-D centres in order; sort anyway for the output
     for (int a = 1; a < K; ++a) {
       const double v = cn[a];
       int b = a - 1;
@@ -463,7 +509,7 @@ int launch_refine(const float* x, const float* w, int64_t n, int Gm, const CbLay
   double* ref = reinterpret_cast<double*>(ws + L.ref);
   for (int r = 0; r < iters; ++r) {
     cb_refine_kernel<K><<<Gm, kCbRefineThreads, 0, s>>>(x, w, n, cen, ref, status);
-    cb_finalize_kernel<<<1, 32, 0, s>>>(ref, Gm, K, cen, out, status);
+    cb_finalize_kernel<<<1, 32 * kCbMaxK, 0, s>>>(ref, Gm, K, cen, out, status);
   }
   return check_launch("fit_codebook(refine)");
 }
@@ -507,7 +553,7 @@ extern "C" int kvq_fit_codebook(const float* x, const float* weights, int64_t n,
   double* ssum = reinterpret_cast<double*>(ws + L.ssum);
   CbBins* bins = reinterpret_cast<CbBins*>(ws + L.bins);
   const size_t hist_smem = sizeof(float) * 2 * kCbBins;
-  const size_t solve_smem = sizeof(double) * 2 * (kCbBins + 1);
+  const size_t solve_smem = kCbSolveSmem;
   cudaFuncSetAttribute(cb_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)hist_smem);
   cudaFuncSetAttribute(cb_solve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
