@@ -100,3 +100,13 @@ def test_gpu_fit_rejects_host_tensors():
 
     with pytest.raises(RuntimeError, match="CUDA"):
         fit_nuq_codebook_cuda(torch.zeros(10), torch.ones(10), 2)
+
+
+def test_padding_helper_matches_the_reference_rule():
+    """The host helper that applies nuq.py:26-37 to the GPU path's inputs."""
+    from kvquant.quant.nuq import _pad_sorted
+
+    for x in (np.array([0.3, -0.2, 0.7], np.float32), np.array([0.5], np.float32),
+              np.array([-1.0, 1.0, 0.0, 0.25], np.float32)):
+        got = _pad_sorted(torch.from_numpy(x), 8).numpy()
+        np.testing.assert_array_equal(got, O.codebook_degenerate(x, 3))

@@ -104,3 +104,15 @@ def test_train_nuq_codebook_runs_on_the_device_for_cuda_tensors(cuda):
     c = train_nuq_codebook(torch.from_numpy(x).to(cuda), torch.from_numpy(w).to(cuda), n_bits=2)
     assert c.is_cuda
     np.testing.assert_allclose(c.cpu().numpy(), _fit(x, w, 2, cuda), rtol=0, atol=1e-6)
+
+
+def test_zero_weights_are_ignored(cuda):
+    """Samples of weight 0 move no centre (the reference passes the weights to
+    KMeans as sample_weight)."""
+    x, w = _data(50, 1500, "bimodal")
+    w[np.random.default_rng(51).random(x.size) < 0.4] = 0.0
+    wn = w / w.sum()
+    got = _fit(x, w, 3, cuda)
+    opt = O.kmeans_1d_optimal(x[w > 0], wn[w > 0], 8)
+    assert O.kmeans_1d_inertia(x, wn, got) <= O.kmeans_1d_inertia(x, wn, opt) * (1 + 1e-5)
+    np.testing.assert_allclose(got, opt, rtol=0, atol=2e-4)
