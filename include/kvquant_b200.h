@@ -302,8 +302,9 @@ int kvq_value_output_noalloc(const uint8_t* codes, const uint32_t* out_ent,
  * into 2^bits intervals (dynamic programming), then refine_iters (0..64)
  * Lloyd steps on the samples. centres: fp32 [2^bits], ascending.
  * status: int32 [2] (device), written by the call: status[1] = occupied bins;
- * status[0] = 1 when fewer than 2^bits bins are occupied, in which case
- * `centres` is not written (the caller applies the reference's few-distinct-
+ * status[0] = 0, or flags with `centres` left unwritten: 2 = a sample is NaN
+ * or infinite, 4 = a weight is negative or not finite, 1 (alone) = fewer than
+ * 2^bits bins are occupied (the caller applies the reference's few-distinct-
  * values rule, nuq.py:26-37). bits 1..4; n >= 1; workspace 256-byte aligned,
  * kvq_fit_codebook_workspace(n) bytes. The reference's degenerate cases
  * (n = 0, n < 2^bits) are the caller's. */

@@ -154,15 +154,15 @@ __device__ __forceinline__ void cb_for_each(const float* __restrict__ x,
   for (int64_t i = start + gid; i < n; i += stride) f(x[i], w[i]);
 }
 
-// 1. Per-CTA min / max; block 0 also clears the status words for this fit.
+// Bits of status[0] (status words cleared by the host before the range kernel).
+enum CbStatus : int { kCbFewBins = 1, kCbBadSample = 2, kCbBadWeight = 4 };
+
+// 1. Per-CTA min / max; flags a NaN or infinite sample.
 __global__ void __launch_bounds__(256) cb_range_kernel(const float* __restrict__ x, int64_t n,
                                                        float2* __restrict__ mm,
                                                        int32_t* __restrict__ status) {
-  if (blockIdx.x == 0 && threadIdx.x == 0) {
-    status[0] = 0;
-    status[1] = 0;
-  }
   float lo = INFINITY, hi = -INFINITY;
+  bool bad = false;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   int64_t start = 0;
@@ -173,6 +173,7 @@ __global__ void __launch_bounds__(256) cb_range_kernel(const float* __restrict__
       const float4 a = x4[i];
       lo = fminf(fminf(lo, a.x), fminf(a.y, fminf(a.z, a.w)));
       hi = fmaxf(fmaxf(hi, a.x), fmaxf(a.y, fmaxf(a.z, a.w)));
+      bad |= !(isfinite(a.x) && isfinite(a.y) && isfinite(a.z) && isfinite(a.w));
     }
     start = n4 << 2;
   }
@@ -180,7 +181,9 @@ __global__ void __launch_bounds__(256) cb_range_kernel(const float* __restrict__
     const float v = x[i];
     lo = fminf(lo, v);
     hi = fmaxf(hi, v);
+    bad |= !isfinite(v);
   }
+  if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(&status[0], kCbBadSample);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
@@ -208,19 +211,22 @@ __global__ void __launch_bounds__(kCbHistThreads) cb_hist_kernel(const float* __
                                                                  int64_t n,
                                                                  const float2* __restrict__ mm,
                                                                  int Gm, CbBins* __restrict__ bins_out,
-                                                                 float* __restrict__ part) {
+                                                                 float* __restrict__ part,
+                                                                 int32_t* __restrict__ status) {
   extern __shared__ float cb_hist_sh[];  // [2][kCbBins]
   float* sw = cb_hist_sh;
   float* sd = cb_hist_sh + kCbBins;
   for (int i = threadIdx.x; i < 2 * kCbBins; i += blockDim.x) cb_hist_sh[i] = 0.f;
   const CbBins bins = cb_bins_block(mm, Gm);  // ends with a block barrier
   if (blockIdx.x == 0 && threadIdx.x == 0) *bins_out = bins;
+  bool bad = false;
   cb_for_each(x, w, n, [&](float v, float wt) {
     const int k = cb_bin(bins, v);
+    bad |= !(wt >= 0.f && wt < INFINITY);
     atomicAdd(&sw[k], wt);
     atomicAdd(&sd[k], wt * __fsub_rn(v, cb_centre(bins, k)));
   });
-  __syncthreads();
+  if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(&status[0], kCbBadWeight);
   float* out = part + (size_t)blockIdx.x * 2 * kCbBins;
   for (int i = threadIdx.x; i < 2 * kCbBins; i += blockDim.x) out[i] = cb_hist_sh[i];
 }
@@ -271,8 +277,9 @@ __global__ void __launch_bounds__(kCbSolveThreads, 1)
   __shared__ double wtot[32], stot[32], slot_v[32];
   __shared__ int slot_i[32];
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  if (status[1] < K) {  // fewer occupied bins than clusters: the host decides
-    if (t == 0) status[0] = 1;
+  const int flags = status[0];
+  if (flags || status[1] < K) {  // bad input, or fewer occupied bins than clusters
+    if (t == 0 && !flags) status[0] = kCbFewBins;
     return;
   }
   // Exclusive block scan of the per-thread totals of `per` consecutive bins.
@@ -558,8 +565,12 @@ extern "C" int kvq_fit_codebook(const float* x, const float* weights, int64_t n,
                        (int)hist_smem);
   cudaFuncSetAttribute(cb_solve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)solve_smem);
+  if (cudaMemsetAsync(status, 0, 2 * sizeof(int32_t), s) != cudaSuccess) {
+    set_error("fit_codebook: clearing status: %s", cudaGetErrorString(cudaGetLastError()));
+    return KVQ_ERR_CUDA;
+  }
   cb_range_kernel<<<Gm, 256, 0, s>>>(x, n, mm, status);
-  cb_hist_kernel<<<G, kCbHistThreads, hist_smem, s>>>(x, weights, n, mm, Gm, bins, hist);
+  cb_hist_kernel<<<G, kCbHistThreads, hist_smem, s>>>(x, weights, n, mm, Gm, bins, hist, status);
   cb_reduce_kernel<<<kCbBins / 256, 256, 0, s>>>(hist, G, bins, wsum, ssum, status);
   cb_solve_kernel<<<1, kCbSolveThreads, solve_smem, s>>>(
       wsum, ssum, K, bins, reinterpret_cast<double*>(ws + L.drow),

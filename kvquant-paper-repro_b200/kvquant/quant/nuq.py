@@ -30,8 +30,10 @@ def fit_nuq_codebook_cuda(activations: torch.Tensor, fisher: torch.Tensor, n_bit
     -> sorted fp32 centres [2^n_bits] on the same device.
 
     Minimises the objective of nuq.py:39-42 (the weights' normalisation to sum 1,
-    nuq.py:23, does not move the centres). n_bits 1..4. Raises RuntimeError when
-    the library is missing, and when at least 2^n_bits distinct values fall into
+    nuq.py:23, does not move the centres). n_bits 1..4. Raises ValueError for NaN or
+    infinite activations (as the reference's KMeans input check does) and for weights
+    that are negative or not finite; RuntimeError when the library is missing, and
+    when at least 2^n_bits distinct values fall into
     fewer than 2^n_bits of the 8192 histogram bins (values bunched far below the
     bin width of their range), which the GPU method does not resolve.
     """
@@ -59,6 +61,10 @@ def fit_nuq_codebook_cuda(activations: torch.Tensor, fisher: torch.Tensor, n_bit
                                     _ptr(out), _ptr(ws), ws.numel(), _ptr(status),
                                     _stream(x)), lib)
     flag, occupied = (int(v) for v in status.cpu())
+    if flag & 2:
+        raise ValueError("activations contain NaN or infinity")
+    if flag & 4:
+        raise ValueError("fisher weights must be finite and non-negative")
     if flag:
         uniq = torch.unique(x)
         if uniq.numel() < n_clusters:

@@ -116,3 +116,17 @@ def test_zero_weights_are_ignored(cuda):
     opt = O.kmeans_1d_optimal(x[w > 0], wn[w > 0], 8)
     assert O.kmeans_1d_inertia(x, wn, got) <= O.kmeans_1d_inertia(x, wn, opt) * (1 + 1e-5)
     np.testing.assert_allclose(got, opt, rtol=0, atol=2e-4)
+
+
+def test_non_finite_samples_and_bad_weights_raise(cuda):
+    x, w = _data(60, 5000, "normal")
+    for bad_x, bad_w in ((np.nan, None), (np.inf, None), (None, np.inf), (None, -1.0),
+                         (None, np.nan)):
+        xx, ww = x.copy(), w.copy()
+        if bad_x is not None:
+            xx[1234] = bad_x
+        if bad_w is not None:
+            ww[4321] = bad_w
+        with pytest.raises(ValueError):
+            _fit(xx, ww, 3, cuda)
+    _fit(x, w, 3, cuda)  # a clean call after the flagged ones
