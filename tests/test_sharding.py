@@ -76,10 +76,11 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_two_rank_gather_matches_single_process(tmp_path):
+@pytest.mark.parametrize("world", [2, 4])
+def test_multi_rank_gather_matches_single_process(tmp_path, world):
     import torch.multiprocessing as mp
     out_path = str(tmp_path / "gathered.npy")
-    mp.spawn(_rank_main, args=(2, _free_port(), out_path), nprocs=2, join=True)
+    mp.spawn(_rank_main, args=(world, _free_port(), out_path), nprocs=world, join=True)
     got = np.load(out_path)
     q, kh, vh, Hkv, G = _case()
     _, _, ref = O.decode_attention(q, kh, vh, Hkv, O.rope_inv_freq(128, 10000.0))
@@ -110,6 +111,10 @@ def test_oracle_shard_merge_is_the_whole_decode():
     np.testing.assert_allclose(got, ref, rtol=1e-10, atol=1e-12)
 
 
+def _token_case_tokens(world):
+    return 600 if world <= 2 else 1100  # every rank's range starts on a 256-token boundary
+
+
 def _token_rank_main(rank, world, port, out_path):
     import torch.distributed as dist
     from kvquant.sharding import shard_tokens, gather_shard_partials
@@ -117,7 +122,7 @@ def _token_rank_main(rank, world, port, out_path):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        q, kh, vh, Hkv, G = _case(T=600)
+        q, kh, vh, Hkv, G = _case(T=_token_case_tokens(world))
         t0, t1 = shard_tokens(kh.shape[1], world, rank)
         o, m, l = O.decode_shard(q, kh[:, t0:t1], vh[:, t0:t1], Hkv,
                                  O.rope_inv_freq(128, 10000.0), t0)
@@ -136,16 +141,19 @@ def _token_rank_main(rank, world, port, out_path):
         dist.destroy_process_group()
 
 
-def test_two_rank_token_shards_match_single_process(tmp_path):
+@pytest.mark.parametrize("world", [2, 4])
+def test_multi_rank_token_shards_match_single_process(tmp_path, world):
     """Each rank decodes its token range (positions offset), the shard outputs
     and row stats are all-gathered with the helper bench.py uses and merged."""
     import torch.multiprocessing as mp
     out_path = str(tmp_path / "merged.npy")
-    mp.spawn(_token_rank_main, args=(2, _free_port(), out_path), nprocs=2, join=True)
+    mp.spawn(_token_rank_main, args=(world, _free_port(), out_path), nprocs=world, join=True)
     got = np.load(out_path)
-    q, kh, vh, Hkv, G = _case(T=600)
+    q, kh, vh, Hkv, G = _case(T=_token_case_tokens(world))
     _, _, ref = O.decode_attention(q, kh, vh, Hkv, O.rope_inv_freq(128, 10000.0))
-    np.testing.assert_allclose(got, ref, rtol=2e-6, atol=1e-6)
+    # the shard outputs and row stats travel as fp32 (as on the GPU path): a row max
+    # of a few tens carries ~3e-6 absolute error into exp(m - M)
+    np.testing.assert_allclose(got, ref, rtol=2e-5, atol=1e-5)
 
 
 def test_bench_shard_mode():
