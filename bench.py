@@ -292,6 +292,19 @@ def algorithmic_bytes(wl, pk, pv, hl, T):
     return {"key_scores": key, "value_output": value}
 
 
+def kernel_rates(batch, tokens, heads, key_ms, value_ms):
+    """Per-rank rates of one layer's decode kernels: cached positions (all of the
+    rank's KV heads) and (head, position) pairs per second, for the key kernel, the
+    value path (prep + value + combine) and the two together."""
+    out = {}
+    for name, ms in (("key_scores", key_ms), ("value_output", value_ms),
+                     ("combined", key_ms + value_ms)):
+        sec = ms / 1e3
+        out[name] = {"tokens_per_s": batch * tokens / sec,
+                     "head_tokens_per_s": batch * tokens * heads / sec}
+    return out
+
+
 def run_gpu(args):
     import torch
     import torch.distributed as dist
@@ -513,6 +526,7 @@ def run_gpu(args):
                          "bytes_per_launch": ab[dom], "launch_ms": dom_ms},
             "step_bandwidth_gbs": step_bytes / (ms_step / 1e3) / 1e9,
             "kernels_ms": {"key_scores": k_avg, "value_output": v_avg},
+            "kernel_rates": kernel_rates(wl.batch, T, hl, k_avg, v_avg),
             "algorithmic_bytes_per_launch": ab,
             "cpu_baseline": cpu,
             "quantize_append": qstat,

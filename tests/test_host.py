@@ -87,3 +87,12 @@ def test_hf_cache_install_and_uninstall():
     uninstall(m)
     assert m.config._attn_implementation == "sdpa" and not m._kvq_hooks
     assert not any(hasattr(layer.self_attn, "_kvq_state") for layer in m.model.layers)
+
+
+def test_bench_kernel_rates():
+    """Per-kernel rates in the bench line: positions and (head, position) pairs per second."""
+    import bench
+    r = bench.kernel_rates(2, 1000, 32, 1.0, 0.5)
+    assert r["key_scores"]["tokens_per_s"] == pytest.approx(2e6)
+    assert r["value_output"]["head_tokens_per_s"] == pytest.approx(2 * 1000 * 32 / 0.5e-3)
+    assert r["combined"]["tokens_per_s"] == pytest.approx(2000 / 1.5e-3)
