@@ -96,3 +96,17 @@ def test_bench_kernel_rates():
     assert r["key_scores"]["tokens_per_s"] == pytest.approx(2e6)
     assert r["value_output"]["head_tokens_per_s"] == pytest.approx(2 * 1000 * 32 / 0.5e-3)
     assert r["combined"]["tokens_per_s"] == pytest.approx(2000 / 1.5e-3)
+
+
+def test_hf_cache_layer_counts_positions_only():
+    """The Cache layer stores no key or value tensor: it counts positions so the
+    model's masks and positions come out as with its dynamic cache."""
+    from kvquant.hf_cache import _layer_cls
+    layer = _layer_cls()()
+    k = torch.zeros(1, 2, 5, 128, dtype=torch.float16)
+    out_k, out_v = layer.update(k, k)
+    assert out_k is k and out_v is k
+    assert layer.get_seq_length() == 5 and layer.get_mask_sizes(1) == (6, 0)
+    layer.update(k[:, :, :1], k[:, :, :1])
+    assert layer.get_seq_length() == 6 and layer.get_max_cache_shape() == -1
+    assert not hasattr(layer, "keys") or layer.keys is None
