@@ -110,3 +110,17 @@ def test_padding_helper_matches_the_reference_rule():
               np.array([-1.0, 1.0, 0.0, 0.25], np.float32)):
         got = _pad_sorted(torch.from_numpy(x), 8).numpy()
         np.testing.assert_array_equal(got, O.codebook_degenerate(x, 3))
+
+
+def test_oracle_optimum_is_equivariant():
+    """Scaling the weights leaves the optimum; shifting / scaling the samples moves
+    it with them (properties of the weighted 1-D k-means objective)."""
+    x, w = _data(7, 400, "bimodal")
+    base = O.kmeans_1d_optimal(x, w, 4)
+    # a power-of-two weight scale is exact in fp32, so the optimum must not move at all
+    np.testing.assert_array_equal(O.kmeans_1d_optimal(x, w * np.float32(32.0), 4), base)
+    np.testing.assert_allclose(O.kmeans_1d_optimal(x.astype(np.float64) * 2.0 + 0.5, w, 4),
+                               base * 2.0 + 0.5, rtol=1e-12, atol=1e-12)
+    # mirrored samples give mirrored centres
+    np.testing.assert_allclose(O.kmeans_1d_optimal(-x.astype(np.float64), w, 4), -base[::-1],
+                               rtol=1e-12, atol=1e-12)
