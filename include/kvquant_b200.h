@@ -284,7 +284,11 @@ int kvq_decode_attention(const uint8_t* k_codes, const uint32_t* k_out_ent,
  *     that first call before any stream capture begins.
  *   - All calls on one device share the array: calls whose work overlaps in
  *     time (other streams, or unordered host threads) race on it; calls in
- *     order on one stream are safe. */
+ *     order on one stream are safe.
+ *   - The address cached by the first call belongs to the device's primary
+ *     context: it does not survive cudaDeviceReset, and callers that drive
+ *     the device through a context other than the primary one must not use
+ *     this entry point. */
 int kvq_value_output_noalloc(const uint8_t* codes, const uint32_t* out_ent,
                              const int32_t* out_ptr, const float* v_scale, const float* v_zero,
                              int64_t ld_stats, const void* v_sink, const float* codebook,

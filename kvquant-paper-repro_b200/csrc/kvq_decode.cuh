@@ -1175,7 +1175,13 @@ static int value_impl(const uint8_t* codes, const uint32_t* out_ent, const int32
   a.stat_scale = stat_scale;
   a.partial = reinterpret_cast<float*>(workspace);
   float* row_max = reinterpret_cast<float*>((char*)workspace + part_bytes);
-  cudaMemsetAsync(row_max, 0, (size_t)B * sizeof(float), st);
+  {
+    const cudaError_t me = cudaMemsetAsync(row_max, 0, (size_t)B * sizeof(float), st);
+    if (me != cudaSuccess) {
+      set_error("value_output: clearing the row maxima failed: %s", cudaGetErrorString(me));
+      return KVQ_ERR_CUDA;
+    }
+  }
   const unsigned n_chunks = (unsigned)((T + kRowMaxChunk - 1) / kRowMaxChunk);
   if (stats) {
     // one launch: the row maxima and the merge of the key kernel's partials

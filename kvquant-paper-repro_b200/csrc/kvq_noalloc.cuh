@@ -17,7 +17,11 @@
 //
 // Set-up: the first call on a device looks the array's address up with
 // cudaGetSymbolAddress (with that device current) and caches it; make that
-// first call before any stream capture begins.
+// first call before any stream capture begins. The cached address belongs to
+// the device's primary context: it does not survive cudaDeviceReset (which
+// unloads the module and its array), and a caller that runs the library
+// under a context of its own other than the primary one must not use this
+// entry point.
 //
 // Concurrency: all calls on one device share the one array. Two calls whose
 // work overlaps in time (different streams, or different host threads with

@@ -17,8 +17,17 @@ codes instead, and decode steps attend over them with the decode kernels:
 
 The Cache object stores no key or value tensor; it only counts positions, so the
 model's masks and positions come out as with its dynamic cache.
+
+Supported call pattern: one prefill call, then one-token decode calls, unpadded
+batches, the model's default attention scaling 1/sqrt(128). Anything else raises
+RuntimeError rather than attending over the wrong positions: a decode step whose
+attention mask hides a cached position (a padded batch), a scaling other than
+1/sqrt(128), a second multi-token call (chunked prefill, assisted decoding) after
+the prefill, and a decode call before any prefill.
 """
 from __future__ import annotations
+
+import math
 
 import torch
 
@@ -80,6 +89,35 @@ class KVQuantState:
         return torch.zeros(pk["n_heads"] * 128, dtype=torch.float32, device=pk["q_idx"].device)
 
 
+def check_decode_call(state: "KVQuantState", layer: int, attention_mask, scaling) -> None:
+    """Raises RuntimeError for a decode step the packed cache cannot serve.
+
+    The decode kernels attend over every cached position with softmax scale
+    1/sqrt(128); a mask that hides cached positions (left padding) or another
+    scaling would silently change the result. The mask is the same for every
+    layer, so it is read back (one small device-to-host copy) at layer 0 only.
+    """
+    if state.pk[layer] is None or state.pv[layer] is None:
+        raise RuntimeError("kvquant hf_cache: decode call before the prefill")
+    if scaling is not None and abs(float(scaling) * math.sqrt(128.0) - 1.0) > 1e-6:
+        raise RuntimeError(f"kvquant hf_cache: attention scaling {scaling} is not 1/sqrt(128), "
+                           "the decode kernels' softmax scale")
+    if attention_mask is not None and layer == 0:
+        m = attention_mask
+        hidden = ~m if m.dtype == torch.bool else (m < 0)
+        if bool(hidden.any()):
+            raise RuntimeError("kvquant hf_cache: the attention mask hides cached positions "
+                               "(padded batch); the packed cache attends over all of them")
+
+
+def check_prefill_call(state: "KVQuantState", layer: int) -> None:
+    """Raises RuntimeError for a multi-token call after the prefill: the packed
+    cache takes one prefill block, then one token per call."""
+    if state.pk[layer] is not None or state.pv[layer] is not None:
+        raise RuntimeError("kvquant hf_cache: a multi-token call after the prefill (chunked "
+                           "prefill or assisted decoding) is not supported; install a new cache")
+
+
 def _attention(module, query, key, value, attention_mask, scaling=None, dropout=0.0, **kwargs):
     """Prefill: the model's SDPA path on the fake-quant chunk; decode: the packed cache."""
     state: KVQuantState = module._kvq_state
@@ -88,6 +126,7 @@ def _attention(module, query, key, value, attention_mask, scaling=None, dropout=
         return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout,
                                       scaling=scaling, **kwargs)
     layer = module.layer_idx
+    check_decode_call(state, layer, attention_mask, scaling)
     q = query[:, :, 0, :]
     out = decode_attention(q, state.pk[layer], state.pv[layer], state.inv_freq)
     return out[:, None], None  # [B, 1, Hq, 128], the layout the model reshapes
@@ -113,16 +152,21 @@ def install(model, quantizer, max_new_tokens: int, key_thresholds=None,
 
         def k_hook(module, inp, out, idx=i):
             if out.shape[1] > 1:
+                check_prefill_call(state, idx)
                 p = quantizer.pack_k(idx, out, dequant=state.fake_quant_prefill)
                 deq = p.pop("dequant", None)
                 state.pk[idx] = make_appendable(p, state.max_new_tokens)
                 return deq.to(out.dtype) if deq is not None else out
             pk = state.pk[idx]
+            if pk is None:
+                raise RuntimeError("kvquant hf_cache: decode call before the prefill")
             append_keys(pk, out, state.thresholds(idx, pk), check=False)
             return out
 
         def v_hook(module, inp, out, idx=i):
             if out.shape[1] > 1:
+                if state.pv[idx] is not None:
+                    check_prefill_call(state, idx)
                 p = quantizer.pack_v(idx, out, dequant=state.fake_quant_prefill)
                 deq = p.pop("dequant", None)
                 state.pv[idx] = make_appendable(p, state.max_new_tokens)

@@ -9,12 +9,22 @@ the reference's signature and rules:
 * CUDA tensors: ``fit_nuq_codebook_cuda``, the same objective solved on the GPU
   by the library's exact 1-D method (weighted histogram, optimal interval split,
   Lloyd refinement; ``kvq_fit_codebook``), with the same degenerate-input rules.
-  The centres come back on the input's device.
+  The centres come back as a CPU tensor, as the reference's do (its calibration
+  pickles them, so a codebook must not be tied to a device index). Values
+  bunched into fewer histogram bins than clusters go to the reference's solver.
+
+``fit_nuq_codebook_cuda`` keeps its centres on the device for callers that feed
+them straight to the quantize kernels.
 """
 from __future__ import annotations
 
 import numpy as np
 import torch
+
+
+class CodebookBinsError(RuntimeError):
+    """At least 2^n_bits distinct values fall into fewer than 2^n_bits of the
+    GPU fit's histogram bins (values bunched far below the bin width)."""
 
 
 def _pad_sorted(vals: torch.Tensor, n_clusters: int) -> torch.Tensor:
@@ -69,7 +79,7 @@ def fit_nuq_codebook_cuda(activations: torch.Tensor, fisher: torch.Tensor, n_bit
         uniq = torch.unique(x)
         if uniq.numel() < n_clusters:
             return _pad_sorted(uniq, n_clusters)
-        raise RuntimeError(
+        raise CodebookBinsError(
             f"fit_nuq_codebook_cuda: {uniq.numel()} distinct values fall into {occupied} "
             f"of the 8192 histogram bins, fewer than the {n_clusters} clusters")
     return out
@@ -78,7 +88,10 @@ def fit_nuq_codebook_cuda(activations: torch.Tensor, fisher: torch.Tensor, n_bit
 def train_nuq_codebook(activations: torch.Tensor, fisher: torch.Tensor, n_bits: int = 3):
     """activations [N] in [-1, 1], fisher [N] weights -> sorted fp32 centers [2^n_bits]."""
     if activations.is_cuda:
-        return fit_nuq_codebook_cuda(activations, fisher, n_bits)
+        try:
+            return fit_nuq_codebook_cuda(activations, fisher, n_bits).cpu()
+        except CodebookBinsError:
+            activations, fisher = activations.cpu(), fisher.cpu()
     from sklearn.cluster import KMeans
 
     n_clusters = 2 ** n_bits

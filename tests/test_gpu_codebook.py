@@ -102,8 +102,22 @@ def test_train_nuq_codebook_runs_on_the_device_for_cuda_tensors(cuda):
 
     x, w = _data(40, 20_000, "normal")
     c = train_nuq_codebook(torch.from_numpy(x).to(cuda), torch.from_numpy(w).to(cuda), n_bits=2)
-    assert c.is_cuda
-    np.testing.assert_allclose(c.cpu().numpy(), _fit(x, w, 2, cuda), rtol=0, atol=1e-6)
+    # a CPU tensor, as the reference returns (calibration pickles the codebooks)
+    assert not c.is_cuda and c.dtype == torch.float32
+    np.testing.assert_allclose(c.numpy(), _fit(x, w, 2, cuda), rtol=0, atol=1e-6)
+
+
+def test_train_nuq_codebook_bunched_values_use_the_reference_solver(cuda):
+    """Where the GPU fit reports bunched values, train_nuq_codebook returns
+    the reference solver's codebook instead of raising."""
+    from kvquant.quant.nuq import train_nuq_codebook
+    x = np.concatenate([np.float32(0.5) + np.arange(20, dtype=np.float32) * np.float32(1e-6),
+                        np.float32([1000.0])]).astype(np.float32)
+    w = np.ones_like(x)
+    got = train_nuq_codebook(torch.from_numpy(x).to(cuda), torch.from_numpy(w).to(cuda), n_bits=3)
+    ref = train_nuq_codebook(torch.from_numpy(x), torch.from_numpy(w), n_bits=3)
+    assert not got.is_cuda
+    np.testing.assert_array_equal(got.numpy(), ref.numpy())
 
 
 def test_zero_weights_are_ignored(cuda):

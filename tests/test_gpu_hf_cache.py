@@ -87,3 +87,34 @@ def test_quantized_cache_decodes_like_the_reference_hooks(cuda):
     for s, (a, b) in enumerate(zip(got[1:], ref_logits[1:])):
         err = ((a - b).norm() / b.norm()).item()
         assert err <= 2e-3, (s, err)
+
+
+def test_padded_batch_and_second_prefill_raise(cuda):
+    """A left-padded batch of 2 reaches the decode step with cached pad
+    positions masked, which the packed cache cannot honour: it raises. So does
+    a second multi-token call after the prefill."""
+    from kvquant.hf_cache import install, uninstall
+    model = _model(cuda)
+    g = torch.Generator().manual_seed(2)
+    prompt = torch.randint(0, 512, (2, 64), generator=g).to(cuda)
+    quantizer = _quantizer(model, prompt[:1])
+    mask = torch.ones_like(prompt)
+    mask[1, :5] = 0  # left padding of the second sequence
+    kv = install(model, quantizer, max_new_tokens=4)
+    try:
+        with torch.no_grad():
+            out = model(prompt, attention_mask=mask, past_key_values=kv, use_cache=True)
+            tok = out.logits[:, -1:].argmax(-1)
+            mask2 = torch.cat([mask, torch.ones_like(tok)], 1)
+            with pytest.raises(RuntimeError, match="hides cached positions"):
+                model(tok, attention_mask=mask2, past_key_values=kv, use_cache=True)
+    finally:
+        uninstall(model)
+    kv = install(model, quantizer, max_new_tokens=4)
+    try:
+        with torch.no_grad():
+            model(prompt[:1], past_key_values=kv, use_cache=True)
+            with pytest.raises(RuntimeError, match="after the prefill"):
+                model(prompt[:1, :8], past_key_values=kv, use_cache=True)
+    finally:
+        uninstall(model)

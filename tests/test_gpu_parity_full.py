@@ -1,0 +1,150 @@
+"""GPU decode parity where the benchmark runs: positions near 2^20, the
+configurations' full shapes, codebooks fit by train_nuq_codebook, and an error
+bound on every row as well as over the whole tensor.
+
+Reference: the oracle's float64 attention on the reference's own fake-quant
+K_hat / V_hat (kv_quantizer.py:72-122) with the fp32 RoPE angle tables of
+rope_fused.py:6-12 (pinned to the reference by test_oracle_golden.py).
+Tolerance: relative L2 error <= 2e-3 for scores and outputs, over the whole
+tensor and, separately, for each (batch row, query head) row.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import kvq_oracle as O
+import synth
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3
+
+
+def t(x, dev):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+
+
+def rel_l2(got, ref):
+    got, ref = np.asarray(got, np.float64), np.asarray(ref, np.float64)
+    return np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30)
+
+
+def worst_row(got, ref):
+    """Largest relative L2 error of a row (the last axis) and its index."""
+    g = np.asarray(got, np.float64).reshape(-1, np.shape(got)[-1])
+    r = np.asarray(ref, np.float64).reshape(-1, np.shape(ref)[-1])
+    e = np.linalg.norm(g - r, axis=1) / np.maximum(np.linalg.norm(r, axis=1), 1e-30)
+    i = int(np.argmax(e))
+    return float(e[i]), i
+
+
+def check(got, ref, what):
+    whole = rel_l2(got, ref)
+    row, i = worst_row(got, ref)
+    assert whole <= TOL, (what, "whole", whole)
+    assert row <= TOL, (what, "row", i, row, whole)
+
+
+def nuq_codebooks(k, v, scale, zero, bits, sink=True):
+    """Key and value codebooks fit by train_nuq_codebook (the reference's KMeans
+    solver on CPU tensors) on a sample of the normalized, clamped data."""
+    from kvquant.synthetic import fit_codebooks
+    cbk, cbv = fit_codebooks(torch.from_numpy(k), torch.from_numpy(v), torch.from_numpy(scale),
+                             torch.from_numpy(zero), bits, n_samples=20000,
+                             seed=bits if sink else bits + 100)
+    return cbk.numpy().astype(np.float32), cbv.numpy().astype(np.float32)
+
+
+@pytest.mark.parametrize("G", [1, 4])
+def test_positions_near_2_20(cuda, G):
+    """The last 4096 positions below 2^20 (the 1M-token benchmark's end) on a
+    small cache: fl32(t * inv_freq) there rounds by up to ~0.03 rad, which the
+    key kernel must reproduce as the reference's cos/sin tables do."""
+    from kvquant.kernels import (quantize_keys, quantize_values, qk_scores_stats,
+                                 decode_attention_shard, rope_inv_freq)
+    B, Hkv, T, bits, ratio = 1, 2, 4096, 4, 0.01
+    pos0 = (1 << 20) - T
+    k, v = synth.make_kv(B, T, Hkv * 128, seed=90 + G)
+    scale, zero = synth.key_calibration(k, sink=False)
+    cbk, cbv = nuq_codebooks(k, v, scale, zero, bits, sink=False)
+    pk = quantize_keys(t(k, cuda), t(scale, cuda), t(zero, cuda), t(cbk, cuda), bits, ratio,
+                       False)
+    pv = quantize_values(t(v, cuda), t(cbv, cuda), bits, ratio, False)
+    # a quarter-scale query keeps the softmax from collapsing onto one token
+    q = (synth.make_query(B, Hkv * G, 128, seed=91).astype(np.float32) * 0.25).astype(np.float16)
+    inv = rope_inv_freq(128, 10000.0)
+    s, _ = qk_scores_stats(t(q, cuda), pk, inv, pos0=pos0)
+    o, _ = decode_attention_shard(t(q, cuda), pk, pv, inv, pos0=pos0)
+    kh = O.quantize_k(k, cbk, scale, zero, ratio, False)["dequant"]
+    vh = O.quantize_v(v, cbv, ratio, False)["dequant"]
+    inv_np = O.rope_inv_freq(128, 10000.0)
+    check(s.cpu().numpy(), O.key_scores(q, kh, Hkv, inv_np, pos0), "scores")
+    ro, _, _ = O.decode_shard(q, kh, vh, Hkv, inv_np, pos0)
+    check(o.cpu().numpy(), ro, "output")
+    # the same cache decoded at position 0 gives other scores: the offset is used
+    s0, _ = qk_scores_stats(t(q, cuda), pk, inv, pos0=0)
+    assert rel_l2(s0.cpu().numpy(), s.cpu().numpy()) > 0.1
+
+
+def _full_config(cuda, B, Hkv, G, T, bits, ratio, base, seed, heads):
+    from kvquant.kernels import (quantize_keys, quantize_values, qk_scores, decode_attention,
+                                 rope_inv_freq)
+    C = Hkv * 128
+    k, v = synth.make_kv(B, T, C, seed=seed)
+    scale, zero = synth.key_calibration(k)
+    cbk, cbv = nuq_codebooks(k, v, scale, zero, bits)
+    pk = quantize_keys(t(k, cuda), t(scale, cuda), t(zero, cuda), t(cbk, cuda), bits, ratio, True)
+    pv = quantize_values(t(v, cuda), t(cbv, cuda), bits, ratio, True)
+    q = synth.make_query(B, Hkv * G, 128, seed=seed + 1)
+    inv = rope_inv_freq(128, base)
+    s = qk_scores(t(q, cuda), pk, inv).cpu().numpy()
+    o = decode_attention(t(q, cuda), pk, pv, inv).cpu().numpy()
+    del pk, pv
+    cs = np.concatenate([np.arange(h * 128, (h + 1) * 128) for h in heads])
+    kh = O.quantize_k(k[:, :, cs], cbk, scale[cs], zero[cs], ratio, True)["dequant"]
+    vh = O.quantize_v(v, cbv, ratio, True)["dequant"][:, :, cs]  # value stats span all C
+    qh = np.concatenate([np.arange(h * G, (h + 1) * G) for h in heads])
+    rs, _, ro = O.decode_attention(q[:, qh], kh, vh, len(heads), O.rope_inv_freq(128, base))
+    check(s[:, qh], rs, "scores")
+    check(o[:, qh], ro, "output")
+
+
+def test_cfg2_full_shape(cuda):
+    """GQA LLaMA-3-8B layer at full size: batch 16 x 8192 tokens, 32 query heads
+    over 8 KV heads, 2-bit, 1% outliers, theta 500000 (2 KV heads checked)."""
+    _full_config(cuda, 16, 8, 4, 8192, 2, 0.01, 500000.0, 12, [0, 5])
+
+
+def test_cfg1_32k(cuda):
+    """The context sweep's 32K point: 32 heads, 3-bit, 0.5% outliers (2 heads checked)."""
+    _full_config(cuda, 1, 32, 1, 32768, 3, 0.005, 10000.0, 13, [3, 30])
+
+
+def test_cfg0_full_shape_rows(cuda):
+    """LLaMA-7B layer, 4096 tokens, 32 heads, 4-bit, 1%: every row within the bar."""
+    _full_config(cuda, 1, 32, 1, 4096, 4, 0.01, 10000.0, 14, [0, 9, 17, 31])
+
+
+def test_quantize_full_width_nuq_codebook(cuda):
+    """Quantize-on-append at the full LLaMA-7B width (C = 4096, so value top-k
+    keeps 40 entries per token) with train_nuq_codebook codebooks: dequantized
+    values, packed codes, outlier positions and values bit-exact."""
+    from test_gpu_quantize import check_packed, run_quant
+    B, S, C, bits, ratio = 1, 4096, 4096, 4, 0.01
+    k, v = synth.make_kv(B, S, C, seed=15)
+    scale, zero = synth.key_calibration(k)
+    cbk, cbv = nuq_codebooks(k, v, scale, zero, bits)
+    g = dict(k=k, v=v, scale=scale, zero=zero, cb_k=cbk, cb_v=cbv, bits=bits, ratio=ratio,
+             sink=True, S=S, C=C)
+    pk, pv = run_quant(g, cuda)
+    kq = O.quantize_k(k, cbk, scale, zero, ratio, True)
+    vq = O.quantize_v(v, cbv, ratio, True)
+    assert O.outlier_count(C, ratio) == 40
+    exp = O.cache_from_reference_quant(kq, vq, k, v, C // 128, bits)
+    nt = -(-S // 32)
+    for p, qd, tag in ((pk, kq, "k"), (pv, vq, "v")):
+        np.testing.assert_array_equal(p["dequant"].cpu().numpy().view(np.uint16),
+                                      qd["dequant"].view(np.uint16))
+        check_packed(p, exp, tag, nt)
+    np.testing.assert_array_equal(pv["scale"].cpu().numpy()[:, 1:S], vq["scale"])
+    np.testing.assert_array_equal(pv["zero"].cpu().numpy()[:, 1:S], vq["zero"])
