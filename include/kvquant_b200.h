@@ -199,9 +199,9 @@ int kvq_value_output(const uint8_t* codes, const uint32_t* out_ent,
 /* Softmax fused into the key and value kernels (no counterpart in the
  * reference, which materializes the probabilities; the result is the same
  * softmax). kvq_key_scores_stats is kvq_key_scores that also writes, for
- * every row and 256-token chunk k of the token axis, stats[row, k] = (m, l):
- * m = max of scores*scale over the chunk, l = sum of exp(scores*scale - m);
- * stats is fp32 pairs [B*n_heads*group, ceil(T/256)] (kvq_key_stats_size
+ * every row and 16-token block k of the token axis, stats[row, k] = (m, l):
+ * m = max of scores*scale over the block, l = sum of exp(scores*scale - m);
+ * stats is fp32 pairs [B*n_heads*group, ceil(T/16)] (kvq_key_stats_size
  * bytes). kvq_value_output_scores takes the raw scores and those stats in
  * place of probabilities and forms softmax(scores * scale) itself (its
  * workspace: kvq_value_output_scores_workspace bytes); it reads `scores` and

@@ -532,19 +532,23 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
           if (tt < nvalid) dst[tt] = x[k];
         }
         if (a.stats) {
+          // partials per 16-token block (lanes 0-15 / 16-31 of each x[k]), with
           // the same rounding as the value kernel's (score * scale) on the stored score
-          float m = -INFINITY;
+          const int64_t nblk = (a.T + 15) / 16;
+          const int64_t b0 = (int64_t)tile0 * kTileTokens / 16;
 #pragma unroll
           for (int k = 0; k < kKeyTokens / 32; ++k) {
-            x[k] = lane + 32 * k < nvalid ? x[k] * f : -INFINITY;
-            m = fmaxf(m, x[k]);
-          }
-          m = warp_max(m);
-          float l = 0.f;
+            const bool valid = lane + 32 * k < nvalid;
+            const float v = valid ? x[k] * f : -INFINITY;
+            float m = v;
 #pragma unroll
-          for (int k = 0; k < kKeyTokens / 32; ++k) l += __expf(x[k] - m);  // exp(-inf) = 0
-          l = warp_sum(l);
-          if (lane == 0) a.stats[row * n_oct + tile0 / kKeyTiles] = make_float2(m, l);
+            for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            float l = valid ? __expf(v - m) : 0.f;
+#pragma unroll
+            for (int o = 1; o < 16; o <<= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+            if ((lane & 15) == 0 && 32 * k + (lane & 16) < nvalid)
+              a.stats[row * nblk + b0 + 2 * k + (lane >> 4)] = make_float2(m, l);
+          }
         }
       }
     }
@@ -1017,6 +1021,17 @@ inline int value_splits(int64_t U, int64_t nt, int64_t /*G*/) {
   return (int)best;
 }
 
+// Softmax partials of the key kernels: float2 [rows, key_items(T)], one per
+// 16-token block: (max of score * scale, sum of exp(score * scale - max)).
+inline int64_t key_items(int64_t T) { return (T + 15) / 16; }
+
+}  // namespace kvq
+
+#include "kvq_key_tc.cuh"
+#include "kvq_value_tc.cuh"
+
+namespace kvq {
+
 // ===========================================================================
 // Launchers and entry points
 // ===========================================================================
@@ -1066,6 +1081,13 @@ static int launch_value(const ValueArgs& a0, const float* row_max, cudaStream_t 
 
 template <int G>
 static int dispatch_key_bits(int bits, const KeyArgs& a, cudaStream_t st) {
+  if (G == 1 && use_key_tc()) {
+    switch (bits) {
+      case 2: return launch_key_tc<2>(a, st);
+      case 3: return launch_key_tc<3>(a, st);
+      case 4: return launch_key_tc<4>(a, st);
+    }
+  }
   switch (bits) {
     case 2: return launch_key<2, G>(a, st);
     case 3: return launch_key<3, G>(a, st);
@@ -1077,6 +1099,13 @@ static int dispatch_key_bits(int bits, const KeyArgs& a, cudaStream_t st) {
 
 template <int G>
 static int dispatch_value_bits(int bits, const ValueArgs& a, const float* row_max, cudaStream_t st) {
+  if (use_value_tc()) {
+    switch (bits) {
+      case 2: return launch_value_tc<2, G>(a, row_max, st);
+      case 3: return launch_value_tc<3, G>(a, row_max, st);
+      case 4: return launch_value_tc<4, G>(a, row_max, st);
+    }
+  }
   switch (bits) {
     case 2: return launch_value<2, G>(a, row_max, st);
     case 3: return launch_value<3, G>(a, row_max, st);
@@ -1190,7 +1219,7 @@ static int value_impl(const uint8_t* codes, const uint32_t* out_ent, const int32
                                                     align256((size_t)B * sizeof(float)));
     a.ml = ml;
     const int64_t rows = U * G;
-    const int n_oct = (int)((nt + kKeyTiles - 1) / kKeyTiles);
+    const int n_oct = (int)key_items(T);
     if (B >= 65535) {
       set_error("value_output_scores: batch %lld leaves no grid rows for the softmax merge",
                 (long long)B);
@@ -1215,10 +1244,7 @@ static int value_impl(const uint8_t* codes, const uint32_t* out_ent, const int32
   return check_launch("value_output");
 }
 
-// Softmax partials of the key kernel: float2 [rows, n_oct] (n_oct = 256-token items).
-inline int64_t key_items(int64_t T) {
-  return ((T + kTileTokens - 1) / kTileTokens + kKeyTiles - 1) / kKeyTiles;
-}
+
 inline size_t stats_ws(int64_t rows, int64_t T) {
   return align256((size_t)(rows > 0 ? rows : 0) * key_items(T > 0 ? T : 0) * sizeof(float2));
 }

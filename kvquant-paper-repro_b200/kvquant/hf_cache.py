@@ -141,6 +141,11 @@ def install(model, quantizer, max_new_tokens: int, key_thresholds=None,
     from transformers.cache_utils import Cache
 
     AttentionInterface.register(ATTN_NAME, _attention)
+    # the masks of the SDPA path (transformers builds none for an attention
+    # function it does not know): padding reaches the prefill's SDPA call and
+    # the decode check above
+    from transformers.masking_utils import ALL_MASK_ATTENTION_FUNCTIONS, sdpa_mask
+    ALL_MASK_ATTENTION_FUNCTIONS.register(ATTN_NAME, sdpa_mask)
     layers = model.model.layers
     inv = model.model.rotary_emb.inv_freq.detach()
     state = KVQuantState(quantizer, len(layers), max_new_tokens, inv, key_thresholds,

@@ -228,9 +228,9 @@ def qk_scores_stats(q: torch.Tensor, packed_k: dict, inv_freq: torch.Tensor,
                     pos0: int = 0):
     """qk_scores plus the key kernel's softmax partials of softmax(scores * scale).
 
-    Returns (scores fp32 [B, Hq, T], stats fp32 [B*Hq, ceil(T/256), 2]) where
-    stats[row, k] = (max over the k-th 256-token chunk of scores * scale,
-    sum over that chunk of exp(scores * scale - max)). pv_out_scores turns the
+    Returns (scores fp32 [B, Hq, T], stats fp32 [B*Hq, ceil(T/16), 2]) where
+    stats[row, k] = (max over the k-th 16-token block of scores * scale,
+    sum over that block of exp(scores * scale - max)). pv_out_scores turns the
     pair back into the softmax of the whole row. pos0: RoPE position of the
     cache's token 0 (a token-range shard of a longer context).
     """
@@ -243,7 +243,7 @@ def qk_scores_stats(q: torch.Tensor, packed_k: dict, inv_freq: torch.Tensor,
     f = inv_freq.to(qc.device, torch.float32).contiguous()
     scores = out if out is not None else torch.empty((B, Hq, T), dtype=torch.float32,
                                                       device=qc.device)
-    n_chunks = ceil_div(T, 256)
+    n_chunks = ceil_div(T, 16)
     if lib.kvq_key_stats_size(B * Hq, T) != B * Hq * n_chunks * 8:
         raise RuntimeError("qk_scores_stats: library disagrees on the stats size")
     stats = stats_out if stats_out is not None else torch.empty(

@@ -347,6 +347,34 @@ def decode_shard(q, k_hat, v_hat, n_kv_heads: int, inv_freq, pos0: int):
     return value_output(e / l, v_hat, n_kv_heads), m[..., 0], l[..., 0]
 
 
+def decode_fp16_path(q, k_hat, v_hat, n_kv_heads: int, inv_freq, pos0: int = 0):
+    """The reference's own precision for a decode step, as the yardstick of a
+    row's conditioning: K_hat (fp16, kv_quantizer.py:72-94) rotated by the
+    reference's RoPE op, whose output is fp16 (kvquant_ops.cu:27-55, via
+    rope_fused.py:29-34; rope_apply above), then scores, softmax and p.V in fp32
+    as an attention kernel keeps them, output rounded to fp16.
+
+    Returns (scores fp32 [B, Hq, T], output fp16 [B, Hq, D]). Where a row's
+    softmax falls on a few tokens, its output moves with the last bits of its
+    scores; this path's distance from the float64 decode measures that."""
+    q = np.asarray(q, dtype=F16)
+    B, Hq, D = q.shape
+    T = k_hat.shape[1]
+    cos, sin = rope_cos_sin(pos0 + T, D, inv_freq=inv_freq)
+    K = np.asarray(k_hat, dtype=F16).reshape(B, T, n_kv_heads, D).transpose(0, 2, 1, 3)
+    Kr = rope_apply(K, cos, sin, pos0).astype(F32)  # [B, Hkv, T, D]
+    G = Hq // n_kv_heads
+    kv_of = np.arange(Hq) // G
+    s = np.einsum("bhd,bhtd->bht", q.astype(F32), Kr[:, kv_of]).astype(F32)
+    z = s * F32(1.0 / math.sqrt(D))
+    z = z - z.max(axis=-1, keepdims=True)
+    e = np.exp(z)
+    p = e / e.sum(axis=-1, keepdims=True)
+    V = np.asarray(v_hat, dtype=F16).reshape(B, T, n_kv_heads, D).astype(F32)
+    o = np.einsum("bht,bthd->bhd", p, V[:, :, kv_of]).astype(F16)
+    return s, o
+
+
 def merge_shards(os_, ms, ls):
     """Softmax merge of range shards: sum_i w_i o_i / sum_i w_i, w_i = L_i e^(M_i - M)."""
     m = np.max(np.stack(ms), axis=0)

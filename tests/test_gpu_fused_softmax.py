@@ -1,6 +1,6 @@
 """GPU parity of the fused-softmax decode path.
 
-The key kernel leaves per-(row, 256-token chunk) softmax partials (max, sum of
+The key kernel leaves per-(row, 16-token block) softmax partials (max, sum of
 exp) beside the raw scores and the value kernel forms the probabilities from
 the raw scores itself (kvq_key_scores_stats + kvq_value_output_scores, the
 default of kvq_decode_attention when no probabilities are requested). The
@@ -58,13 +58,13 @@ def _case(cuda, B, Hkv, G, T, bits, ratio, seed, sink=True, base=10000.0, want_v
 
 
 def _chunk_stats(scores):
-    """(max, sum exp(x - max)) of scores * SCALE per 256-token chunk, float64."""
+    """(max, sum exp(x - max)) of scores * SCALE per 16-token block, float64."""
     rows = scores.reshape(-1, scores.shape[-1]).astype(np.float64) * np.float32(SCALE)
     T = rows.shape[1]
-    n = (T + 255) // 256
+    n = (T + 15) // 16
     out = np.zeros((rows.shape[0], n, 2))
     for k in range(n):
-        x = rows[:, 256 * k:256 * (k + 1)]
+        x = rows[:, 16 * k:16 * (k + 1)]
         m = x.max(axis=1)
         out[:, k, 0] = m
         out[:, k, 1] = np.exp(x - m[:, None]).sum(axis=1)

@@ -5,8 +5,18 @@ bound on every row as well as over the whole tensor.
 Reference: the oracle's float64 attention on the reference's own fake-quant
 K_hat / V_hat (kv_quantizer.py:72-122) with the fp32 RoPE angle tables of
 rope_fused.py:6-12 (pinned to the reference by test_oracle_golden.py).
-Tolerance: relative L2 error <= 2e-3 for scores and outputs, over the whole
-tensor and, separately, for each (batch row, query head) row.
+
+Tolerances (relative L2 error, over the whole tensor and for each (batch row,
+query head) row separately):
+* scores: 2e-3;
+* outputs: 2e-3 plus twice the error of the reference's own fp16 precision
+  (oracle.decode_fp16_path: fp16 rotated keys, fp32 scores and softmax, fp16
+  output) on the same row. With these synthetic distributions (keys scaled up
+  to 10, 1% of entries x20) many rows' softmax falls on one to three tokens,
+  where the output moves with the last bits of the scores: the reference's own
+  fp16 path is up to 2% off the float64 decode on such rows (and ~2e-4 on the
+  scores), so a fixed 2e-3 would demand more than the reference computes. Rows
+  whose softmax is spread keep the 2e-3 bar.
 """
 import numpy as np
 import pytest
@@ -29,20 +39,23 @@ def rel_l2(got, ref):
     return np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30)
 
 
-def worst_row(got, ref):
-    """Largest relative L2 error of a row (the last axis) and its index."""
+def row_errors(got, ref):
+    """Relative L2 error of every row (the last axis)."""
     g = np.asarray(got, np.float64).reshape(-1, np.shape(got)[-1])
     r = np.asarray(ref, np.float64).reshape(-1, np.shape(ref)[-1])
-    e = np.linalg.norm(g - r, axis=1) / np.maximum(np.linalg.norm(r, axis=1), 1e-30)
-    i = int(np.argmax(e))
-    return float(e[i]), i
+    return np.linalg.norm(g - r, axis=1) / np.maximum(np.linalg.norm(r, axis=1), 1e-30)
 
 
-def check(got, ref, what):
-    whole = rel_l2(got, ref)
-    row, i = worst_row(got, ref)
-    assert whole <= TOL, (what, "whole", whole)
-    assert row <= TOL, (what, "row", i, row, whole)
+def check(got, ref, what, yard=None):
+    """got vs ref: 2e-3, plus twice the yardstick's own error where one is given."""
+    whole, rows = rel_l2(got, ref), row_errors(got, ref)
+    bound_w, bound_r = TOL, np.full(rows.shape, TOL)
+    if yard is not None:
+        bound_w += 2 * rel_l2(yard, ref)
+        bound_r = bound_r + 2 * row_errors(yard, ref)
+    i = int(np.argmax(rows - bound_r))
+    assert whole <= bound_w, (what, "whole", whole, bound_w)
+    assert rows[i] <= bound_r[i], (what, "row", i, rows[i], bound_r[i], whole)
 
 
 def nuq_codebooks(k, v, scale, zero, bits, sink=True):
@@ -80,7 +93,8 @@ def test_positions_near_2_20(cuda, G):
     inv_np = O.rope_inv_freq(128, 10000.0)
     check(s.cpu().numpy(), O.key_scores(q, kh, Hkv, inv_np, pos0), "scores")
     ro, _, _ = O.decode_shard(q, kh, vh, Hkv, inv_np, pos0)
-    check(o.cpu().numpy(), ro, "output")
+    _, yard = O.decode_fp16_path(q, kh, vh, Hkv, inv_np, pos0)
+    check(o.cpu().numpy(), ro, "output", yard)
     # the same cache decoded at position 0 gives other scores: the offset is used
     s0, _ = qk_scores_stats(t(q, cuda), pk, inv, pos0=0)
     assert rel_l2(s0.cpu().numpy(), s.cpu().numpy()) > 0.1
@@ -104,9 +118,11 @@ def _full_config(cuda, B, Hkv, G, T, bits, ratio, base, seed, heads):
     kh = O.quantize_k(k[:, :, cs], cbk, scale[cs], zero[cs], ratio, True)["dequant"]
     vh = O.quantize_v(v, cbv, ratio, True)["dequant"][:, :, cs]  # value stats span all C
     qh = np.concatenate([np.arange(h * G, (h + 1) * G) for h in heads])
-    rs, _, ro = O.decode_attention(q[:, qh], kh, vh, len(heads), O.rope_inv_freq(128, base))
+    inv_np = O.rope_inv_freq(128, base)
+    rs, _, ro = O.decode_attention(q[:, qh], kh, vh, len(heads), inv_np)
+    _, yard = O.decode_fp16_path(q[:, qh], kh, vh, len(heads), inv_np)
     check(s[:, qh], rs, "scores")
-    check(o[:, qh], ro, "output")
+    check(o[:, qh], ro, "output", yard)
 
 
 def test_cfg2_full_shape(cuda):
