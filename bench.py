@@ -55,6 +55,11 @@ def parse():
     ap.add_argument("--codebook", action="store_true",
                     help="benchmark NUQ codebook fitting (offline calibration) instead of decode")
     ap.add_argument("--codebook-samples", type=int, default=1 << 24)
+    ap.add_argument("--config3", action="store_true",
+                    help="full decode of a random-init LLaMA-2-7B through the Hugging Face "
+                         "packed cache (32K-token prefill, then one-token steps)")
+    ap.add_argument("--prefill", type=int, default=32768, help="--config3: prompt tokens")
+    ap.add_argument("--new-tokens", type=int, default=128, help="--config3: decode steps")
     ap.add_argument("--shard", choices=["auto", "heads", "tokens"], default="auto",
                     help="multi-GPU split: KV heads, or token ranges of all heads (auto: heads "
                          "while every rank keeps at least 16 KV heads)")
@@ -765,8 +770,134 @@ def run_codebook(args):
         "gpu_launches": args.steps * (4 + 2 * CB_REFINE)}), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# Config 3: a whole LLaMA-2-7B decoding over the packed quantized cache
+# ---------------------------------------------------------------------------
+C3_METRIC = "LLaMA-2-7B decode over a 4-bit packed KV cache: generated tokens/s"
+
+
+def run_config3(args):
+    """Random-init LLaMA-2-7B (fp16 weights ~ N(0, 0.02)), a uniform-random prompt,
+    per-layer key calibration and NUQ codebooks from the first 4096 prompt tokens,
+    then kvquant.hf_cache: the prefill quantized into appendable packed caches and
+    one-token decode steps attending over the codes (4-bit, 1% outliers)."""
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM
+    from kvquant.hf_cache import install, uninstall
+    from kvquant.quant.kv_quantizer import KVQuantizer
+    from kvquant.quant.nuq import fit_nuq_codebook_cuda
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    dev = torch.device("cuda", 0)
+    log = (lambda m: print(f"[config3] {m}", file=sys.stderr, flush=True))
+    S, N, bits = args.prefill, args.new_tokens, 4
+    cfg = LlamaConfig(vocab_size=32000, hidden_size=4096, intermediate_size=11008,
+                      num_hidden_layers=32, num_attention_heads=32, num_key_value_heads=32,
+                      max_position_embeddings=S + N + 16, rope_theta=10000.0,
+                      initializer_range=0.02)
+    torch.manual_seed(0)
+    t0 = time.time()
+    with torch.device(dev):
+        torch.set_default_dtype(torch.float16)
+        model = LlamaForCausalLM(cfg).eval()
+        torch.set_default_dtype(torch.float32)
+    model.set_attn_implementation("sdpa")
+    weight_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
+    log(f"model built ({weight_bytes / 1e9:.1f} GB, {time.time() - t0:.0f} s)")
+    g = torch.Generator().manual_seed(1)
+    prompt = torch.randint(0, cfg.vocab_size, (1, S), generator=g).to(dev)
+    # calibration on the first 4096 prompt tokens (kvquant/calibration.py's statistics:
+    # per-channel key min/max, codebooks fit to normalized values, scale^2 weights)
+    L = cfg.num_hidden_layers
+    kcal, vcal = {}, {}
+    hooks = []
+    for i, layer in enumerate(model.model.layers):
+        hooks.append(layer.self_attn.k_proj.register_forward_hook(
+            lambda m, inp, out, i=i: kcal.__setitem__(i, out.detach())))
+        hooks.append(layer.self_attn.v_proj.register_forward_hook(
+            lambda m, inp, out, i=i: vcal.__setitem__(i, out.detach())))
+    with torch.no_grad():
+        model(prompt[:, :4096])
+    for h in hooks:
+        h.remove()
+    scales, zeros, cbk, cbv = [], [], [], []
+    for i in range(L):
+        x = kcal[i][0, 1:].float()
+        lo, hi = x.amin(0), x.amax(0)
+        sc, zr = (hi - lo) / 2, (hi + lo) / 2
+        scales.append(sc)
+        zeros.append(zr)
+        kn = ((x - zr) / (sc + 1e-8)).clamp(-1, 1).reshape(-1)
+        cbk.append(fit_nuq_codebook_cuda(kn, (sc ** 2).expand_as(x).reshape(-1), bits))
+        v = vcal[i][0, 1:].float()
+        vmin, vmax = v.amin(1, keepdim=True), v.amax(1, keepdim=True)
+        vs, vz = (vmax - vmin) / 2, (vmax + vmin) / 2
+        vn = ((v - vz) / (vs + 1e-8)).reshape(-1)
+        cbv.append(fit_nuq_codebook_cuda(vn, (vs ** 2).expand_as(v).reshape(-1), bits))
+    del kcal, vcal
+    quantizer = KVQuantizer(cbk, cbv, scales, zeros, k_bits=bits, v_bits=bits,
+                            outlier_ratio=0.01, sink_token=True)
+    kv = install(model, quantizer, max_new_tokens=N + 1)
+    try:
+        with torch.no_grad():
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            out = model(prompt, past_key_values=kv, use_cache=True)
+            e1.record()
+            e1.synchronize()
+            prefill_ms = e0.elapsed_time(e1)
+            log(f"prefill {S} tokens: {prefill_ms:.0f} ms")
+            tok = out.logits[:, -1:].argmax(-1)
+            state = model.model.layers[0].self_attn._kvq_state
+            kv_bytes = sum(sum(t.numel() * t.element_size() for t in (p["q_idx"],
+                                                                      p["outlier_entries"]))
+                           for p in state.pk + state.pv)
+            clocks = ClockSampler(0)
+            clocks.start()
+            time.sleep(0.2)
+            steps = []
+            for n in range(N):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                out = model(tok, past_key_values=kv, use_cache=True)
+                tok = out.logits[:, -1:].argmax(-1)
+                tok.item()  # the generated token back on the host every step
+                e1.record()
+                e1.synchronize()
+                steps.append(e0.elapsed_time(e1))
+            clk = clocks.stop()
+        assert kv.get_seq_length() == S + N
+    finally:
+        uninstall(model)
+    ms = statistics.mean(steps[3:]) if N > 6 else statistics.mean(steps)
+    print(json.dumps({
+        "metric": C3_METRIC, "value": 1e3 / ms, "unit": "tokens/s", "n_gpus": 1,
+        "steps": N, "warmup": 0, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "none", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"llama2-7b-{S}tok-prefill-{N}-decode-4bit",
+                   "model": "LLaMA-2-7B shape, random init N(0, 0.02), fp16",
+                   "prefill_tokens": S, "new_tokens": N, "bits": bits, "outlier_ratio": 0.01,
+                   "attention": "kvquant.hf_cache (prefill: fake-quant keys/values through SDPA, "
+                                "cache packed; decode: decode_attention on the codes, tokens "
+                                "appended per step)"},
+        "prefill_ms": prefill_ms,
+        "decode_ms_per_token": ms, "decode_ms_first3": steps[:3],
+        "kv_cache_bytes_per_step": kv_bytes, "weight_bytes_per_step": weight_bytes,
+        "kv_fraction_of_step_bytes": kv_bytes / (kv_bytes + weight_bytes),
+        "e2e": {"value": 1e3 / ms, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 8},
+        "clocks": clk,
+    }), flush=True)
+
+
 def main():
     args = parse()
+    if args.config3:
+        run_config3(args)
+        return
     if args.codebook:
         if int(os.environ.get("RANK", "0")) == 0:
             run_codebook(args)

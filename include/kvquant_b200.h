@@ -317,6 +317,16 @@ int kvq_fit_codebook(const float* x, const float* weights, int64_t n, int bits,
                      int refine_iters, float* centres, void* workspace,
                      size_t workspace_bytes, int32_t* status, void* stream);
 
+/* Decode kernel choice, process-wide (no counterpart in the reference, whose
+ * decode is unfused torch ops): 0 = warp-level mma.sync kernels (default),
+ * 1 = tcgen05 kernels with TMEM accumulators (key kernel: one query head per
+ * KV head; other groups keep the mma.sync key kernel), -1 = leave unchanged.
+ * The initial choice comes from the environment variables KVQ_KEY_KERNEL /
+ * KVQ_VALUE_KERNEL ("tc" = tcgen05). Both kernels compute the same values to
+ * fp32 summation order. kvq_decode_kernels returns key | value << 1. */
+int kvq_set_decode_kernels(int key_kernel, int value_kernel);
+int kvq_decode_kernels(void);
+
 /* Reads and clears the device-side error flag set by kernels that skip
  * out-of-range accesses (synchronizes `stream`). */
 int kvq_check_status(void* stream);

@@ -75,6 +75,28 @@ struct PairLut {
   }
 };
 
+// Pair LUT with the code values split into fp16 high and low parts (cb = hi +
+// lo to ~2^-22 relative): entry v (a code pair, first code in the low bits) of
+// lane l at byte (v << 8) | (l << 3) holds {half2(hi, hi), half2(lo, lo)}, so a
+// lane's 8-byte lookups hit distinct bank pairs. The low parts keep the
+// dequantized value exact where s * cb and the zero point nearly cancel.
+template <int BITS>
+struct PairLutHiLo {
+  static constexpr int kEntries = 1 << (2 * BITS);
+  static constexpr int kBytes = kEntries * 256;
+  __device__ static void build(uint8_t* smem, const float* cb) {
+    constexpr int mask = (1 << BITS) - 1;
+    for (int idx = threadIdx.x; idx < kEntries * 32; idx += blockDim.x) {
+      const int v = idx >> 5, lane = idx & 31;
+      const float c0 = cb[v & mask], c1 = cb[v >> BITS];
+      const __half h0 = __float2half_rn(c0), h1 = __float2half_rn(c1);
+      const uint32_t hi = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+      const uint32_t lo = half2_bits(c0 - __half2float(h0), c1 - __half2float(h1));
+      *reinterpret_cast<uint2*>(smem + (v << 8) + (lane << 3)) = make_uint2(hi, lo);
+    }
+  }
+};
+
 __device__ __forceinline__ float entry_value(uint32_t ent) {
   return __half2float(__ushort_as_half((unsigned short)(ent >> 16)));
 }
@@ -742,12 +764,12 @@ __global__ void __launch_bounds__(256) value_prep_kernel(const float* __restrict
 template <int BITS, int G>
 struct ValSmem {
   static constexpr bool kWarpAcc = G <= 4;
-  static constexpr int kLut = PairLut<BITS>::kBytes;
+  static constexpr int kLut = PairLutHiLo<BITS>::kBytes;
   static constexpr int kAcc = kLut;
   static constexpr int kAccFloats = (kWarpAcc ? kValWarps : 1) * G * kHeadDim;
   static constexpr int kZ = kAcc + kAccFloats * 4;
-  static constexpr int kW = kZ + 64;  // fp16 token weights [warp][G][32]
-  static constexpr int kPtr = kW + kValWarps * G * 64;
+  static constexpr int kW = kZ + 64;  // fp16 token weights [warp][2G][32]: high parts, low parts
+  static constexpr int kPtr = kW + kValWarps * 2 * G * 64;
   // ring and stages on 128-byte boundaries, so that a warp's 512-byte copies
   // cover whole shared-memory lines
   static constexpr int kRing = (kPtr + (kValMaxTiles + 4) * 4 + 127) / 128 * 128;
@@ -777,9 +799,9 @@ __global__ void __launch_bounds__(kValThreads, 1)
   int32_t* tptr = reinterpret_cast<int32_t*>(smem + S::kPtr);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
-  const uint32_t lane4 = (uint32_t)lane << 2;
+  const uint32_t lane8 = (uint32_t)lane << 3;
   float* wacc = acc + (S::kWarpAcc ? warp * G * kHeadDim : 0);
-  PairLut<BITS>::build(smem, a.cb);
+  PairLutHiLo<BITS>::build(smem, a.cb);
   for (int idx = threadIdx.x; idx < S::kAccFloats; idx += blockDim.x) acc[idx] = 0.f;
   if (threadIdx.x < G) zacc[threadIdx.x] = 0.f;
 
@@ -807,13 +829,18 @@ __global__ void __launch_bounds__(kValThreads, 1)
   if (a.ml && threadIdx.x < G) s_ml[threadIdx.x] = a.ml[b * HG + h * G + threadIdx.x];
   __syncthreads();
 
-  float d[8][4];
+  // d: the weights' high parts (G <= 4: columns 4..4+G-1 hold their low parts);
+  // d2 (G = 8): the low parts
+  constexpr bool kSplitB = G > 4;
+  float d[8][4], d2[kSplitB ? 8 : 1][4];
 #pragma unroll
   for (int mb = 0; mb < 8; ++mb) d[mb][0] = d[mb][1] = d[mb][2] = d[mb][3] = 0.f;
+#pragma unroll
+  for (int mb = 0; mb < (kSplitB ? 8 : 1); ++mb) d2[mb][0] = d2[mb][1] = d2[mb][2] = d2[mb][3] = 0.f;
   float zs[G];
 #pragma unroll
   for (int hd = 0; hd < G; ++hd) zs[hd] = 0.f;
-  __half* wbuf = reinterpret_cast<__half*>(smem + S::kW) + warp * G * 32;
+  __half* wbuf = reinterpret_cast<__half*>(smem + S::kW) + warp * 2 * G * 32;
 
   const int64_t tbytes = kTileTokens * kHeadDim * BITS / 8;
   const uint8_t* src = a.codes + (u * a.nt_cap + ta + warp) * tbytes;
@@ -877,7 +904,10 @@ __global__ void __launch_bounds__(kValThreads, 1)
           const_cast<float*>(fp)[hd * S::kPRow + lane] = p;
         }
         zs[hd] = fmaf(p, szl.y, zs[hd]);
-        wbuf[hd * 32 + lane] = __float2half_rn(p * szl.x * e_scale);
+        const float wv = p * szl.x * e_scale;
+        const __half wh = __float2half_rn(wv);
+        wbuf[hd * 32 + lane] = wh;
+        wbuf[(G + hd) * 32 + lane] = __float2half_rn(wv - __half2float(wh));
       }
     }
     __syncwarp();
@@ -885,20 +915,37 @@ __global__ void __launch_bounds__(kValThreads, 1)
     for (int blk = 0; blk < 2; ++blk) {
       LaneSlab<BITS> sl;
       sl.read(st + blk * S::kBlockSlab + lane * 16, st + blk * S::kBlockSlab + 512 + lane * 16);
-      // B fragment of head g: weights of tokens 2c, 2c+1 (b0) and 2c+8, 2c+9 (b1)
-      uint32_t b0 = 0u, b1 = 0u;
-      if (g < G) {
-        const __half* wg = wbuf + g * 32 + 16 * blk + 2 * c;
-        b0 = *reinterpret_cast<const uint32_t*>(wg);
-        b1 = *reinterpret_cast<const uint32_t*>(wg + 8);
+      // B fragment of column g: weights of tokens 2c, 2c+1 (b0) and 2c+8, 2c+9 (b1).
+      // G <= 4: column g < 4 = head g's high parts, column 4 + h = head h's low
+      // parts; G = 8: column g = head g, high parts in (b0, b1), low in (l0, l1).
+      uint32_t b0 = 0u, b1 = 0u, l0 = 0u, l1 = 0u;
+      {
+        const int row = kSplitB ? g : (g < 4 ? (g < G ? g : -1) : (g - 4 < G ? G + g - 4 : -1));
+        if (row >= 0) {
+          const __half* wg = wbuf + row * 32 + 16 * blk + 2 * c;
+          b0 = *reinterpret_cast<const uint32_t*>(wg);
+          b1 = *reinterpret_cast<const uint32_t*>(wg + 8);
+        }
+        if (kSplitB) {
+          const __half* wl = wbuf + (G + g) * 32 + 16 * blk + 2 * c;
+          l0 = *reinterpret_cast<const uint32_t*>(wl);
+          l1 = *reinterpret_cast<const uint32_t*>(wl + 8);
+        }
       }
 #pragma unroll
       for (int mb = 0; mb < 8; ++mb) {
-        uint32_t af[4];
+        // code values split into fp16 high and low parts: the low parts keep
+        // the dequantized value exact where s * cb and the zero point cancel
+        uint32_t ah[4], al[4];
 #pragma unroll
-        for (int ii = 0; ii < 4; ++ii)
-          af[ii] = *reinterpret_cast<const uint32_t*>(lut + sl.addr(4 * mb + ii, lane4));
-        mma_16816(d[mb], af, b0, b1);
+        for (int ii = 0; ii < 4; ++ii) {
+          const uint2 e = *reinterpret_cast<const uint2*>(lut + sl.addr(4 * mb + ii, lane8));
+          ah[ii] = e.x;
+          al[ii] = e.y;
+        }
+        mma_16816(d[mb], ah, b0, b1);
+        mma_16816(d[mb], al, b0, b1);
+        if (kSplitB) mma_16816(d2[kSplitB ? mb : 0], ah, l0, l1);
       }
     }
     // Outliers: p s o into channel ch, fp32.
@@ -933,6 +980,17 @@ __global__ void __launch_bounds__(kValThreads, 1)
   }
   __syncthreads();  // all warps are done with their rings and accumulators
   float* red = reinterpret_cast<float*>(smem + S::kRing);  // [warp][G][128]
+#pragma unroll
+  for (int mb = 0; mb < 8; ++mb) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (kSplitB) {
+        d[mb][i] += d2[kSplitB ? mb : 0][i];
+      } else {  // add the low-part columns (lanes c + 2) to the high-part ones
+        d[mb][i] += __shfl_xor_sync(0xffffffffu, d[mb][i], 2);
+      }
+    }
+  }
 #pragma unroll
   for (int mb = 0; mb < 8; ++mb) {
     const int ch = 16 * mb + g;
@@ -1298,6 +1356,20 @@ static int key_impl(const uint8_t* codes, const uint32_t* out_ent, const int32_t
   return KVQ_ERR_UNSUPPORTED;
 }
 }  // namespace kvq
+
+extern "C" int kvq_set_decode_kernels(int key_kernel, int value_kernel) {
+  if (key_kernel < -1 || key_kernel > 1 || value_kernel < -1 || value_kernel > 1) {
+    kvq::set_error("kvq_set_decode_kernels: kernels are -1 (keep), 0 (mma.sync), 1 (tcgen05)");
+    return KVQ_ERR_INVALID;
+  }
+  if (key_kernel >= 0) kvq::g_key_kernel().store(key_kernel);
+  if (value_kernel >= 0) kvq::g_value_kernel().store(value_kernel);
+  return KVQ_OK;
+}
+
+extern "C" int kvq_decode_kernels(void) {
+  return kvq::g_key_kernel().load() | (kvq::g_value_kernel().load() << 1);
+}
 
 extern "C" int kvq_key_scores(const uint8_t* codes, const uint32_t* out_ent,
                               const int32_t* out_ptr, const float* k_scale, const float* k_zero,

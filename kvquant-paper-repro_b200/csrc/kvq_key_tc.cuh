@@ -34,6 +34,7 @@
 // A/D buffers while the block warps dequantize the next unit and run the
 // rotation epilogue of the previous one.
 #pragma once
+#include <atomic>
 #include <cstdlib>
 
 #include "kvq_decode.cuh"
@@ -42,15 +43,16 @@
 namespace kvq {
 
 constexpr int kTcBlockWarps = 8;                       // 16-token blocks per M-tile
-constexpr int kTcThreads = (kTcBlockWarps + 1) * 32;   // + the copy / MMA warp
+constexpr int kTcMmaWarp = kTcBlockWarps;              // issues the MMAs, rebuilds tables
+constexpr int kTcCopyWarp = kTcBlockWarps + 1;         // streams the code tiles
+constexpr int kTcThreads = (kTcBlockWarps + 2) * 32;
 constexpr int kTcTiles = 4;                            // 32-token code tiles per M-tile
 constexpr int kTcTokens = kTcTiles * kTileTokens;      // 128
-constexpr int kTcMaxUnits = 16;                        // units per group
-constexpr int kTcStages = 3;                           // code ring stages
+constexpr int kTcMaxUnits = 8;                         // units per group
 constexpr uint32_t kTcCols = 512;                      // TMEM columns
-constexpr uint32_t kTcAConst = 0;                      // [0, 8): constant A of the zero-point MMA
-constexpr uint32_t kTcA = 64;                          // A buffers: [64, 128), [128, 192)
-constexpr uint32_t kTcD = 256;                         // D buffers: [256, 384), [384, 512)
+constexpr uint32_t kTcA = 0;                           // A buffers: [0, 64), [64, 128)
+constexpr uint32_t kTcD = 128;                         // D buffers: [128, 256), [256, 384), [384, 512)
+constexpr int kTcDBufs = 3;
 constexpr uint32_t kTcIdescStep = sm100::idesc_f16_f32(128, 16);
 constexpr uint32_t kTcIdescZero = sm100::idesc_f16_f32(128, 128);
 
@@ -58,24 +60,30 @@ template <int BITS>
 struct KeyTcSmem {
   static constexpr int kBlockBytes = 256 * BITS;                 // one 16-token block of a unit
   static constexpr int kStageBytes = kTcTiles * 2 * kBlockBytes;  // one unit's M-tile
-  static constexpr int kLut = 0;
-  static constexpr int kRing = PairLut<BITS>::kBytes;
-  static constexpr int kBMain = kRing + kTcStages * kStageBytes;  // [unit][step][512 B]
+  static constexpr int kBMain = PairLut<BITS>::kBytes;           // [unit][step][512 B]
   static constexpr int kBZero = kBMain + kTcMaxUnits * 4096;     // [unit][2048 B]
   static constexpr int kZeros = kBZero + kTcMaxUnits * 2048;     // 2048 B of zeros
-  static constexpr int kPQ = kZeros + 2048;                      // [unit][128] half2 (P, Q)
+  static constexpr int kAConst = kZeros + 2048;                  // 128 x 16 fp16: K 0, 1 = 256
+  static constexpr int kPQ = kAConst + 4096;                     // [unit][128] half2 (P, Q)
   static constexpr int kSigma = kPQ + kTcMaxUnits * 512;         // [unit] float
   static constexpr int kSink = kSigma + kTcMaxUnits * 4;         // [unit] float, sink score / sigma
   static constexpr int kInv = kSink + kTcMaxUnits * 4;           // [64] float
   static constexpr int kSlots = kInv + kPairs * 4;               // [warp][16] u64 outlier sums
   static constexpr int kBars = kSlots + kTcBlockWarps * 16 * 8;
-  // codes_full[S], codes_empty[S], a_full[2], d_empty[2], mma_done[2], drained, tables
-  static constexpr int kNumBars = 2 * kTcStages + 8;
+  // codes_full[S], codes_empty[S], a_full[2], d_empty[3], mma_done[3], drained, tables;
+  // the code ring fills the rest of shared memory (up to 24 stages)
+  static constexpr int kFixed = kBars + (2 * 24 + 10) * 8 + 16;
+  static constexpr int kStagesFit = (232448 - kFixed) / kStageBytes;
+  static constexpr int kStages = kStagesFit > 24 ? 24 : kStagesFit;
+  static constexpr int kNumBars = 2 * kStages + 10;
   static constexpr int kTmemPtr = kBars + kNumBars * 8;
   static constexpr int kAbort = kTmemPtr + 4;
-  static constexpr int kBytes = kAbort + 12;
+  static constexpr int kRing = (kAbort + 12 + 127) / 128 * 128;
+  static constexpr int kBytes = kRing + kStages * kStageBytes;
+  static_assert(kStages >= 4, "key code ring");
   static_assert(kBytes <= 232448, "tcgen05 key kernel shared memory");
-  static_assert(kBars % 8 == 0 && kRing % 16 == 0 && kBMain % 16 == 0, "alignment");
+  static_assert(kBars % 8 == 0 && kRing % 16 == 0 && kBMain % 16 == 0 && kAConst % 16 == 0,
+                "alignment");
 };
 
 template <int BITS>
@@ -195,11 +203,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) key_scores_tc_kernel(KeyArgs a)
   const int g = lane >> 2, c = lane & 3;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBars);
   uint64_t* codes_full = bars;
-  uint64_t* codes_empty = bars + kTcStages;
-  uint64_t* a_full = bars + 2 * kTcStages;
+  uint64_t* codes_empty = bars + L::kStages;
+  uint64_t* a_full = bars + 2 * L::kStages;
   uint64_t* d_empty = a_full + 2;
-  uint64_t* mma_done = d_empty + 2;
-  uint64_t* drained = mma_done + 2;
+  uint64_t* mma_done = d_empty + kTcDBufs;
+  uint64_t* drained = mma_done + kTcDBufs;
   uint64_t* tables = drained + 1;
   uint32_t* tmem_ptr = reinterpret_cast<uint32_t*>(smem + L::kTmemPtr);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kAbort);
@@ -218,12 +226,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) key_scores_tc_kernel(KeyArgs a)
   PairLut<BITS>::build(smem, a.cb);
   if (threadIdx.x < kPairs) invf[threadIdx.x] = a.inv_freq[threadIdx.x];
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
+    for (int s = 0; s < L::kStages; ++s) {
       mbar_init(codes_full + s, 1);
       mbar_init(codes_empty + s, kTcBlockWarps);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(a_full + b, kTcBlockWarps);
+    for (int b = 0; b < 2; ++b) mbar_init(a_full + b, kTcBlockWarps);
+    for (int b = 0; b < kTcDBufs; ++b) {
       mbar_init(d_empty + b, kTcBlockWarps);
       mbar_init(mma_done + b, 1);
     }
@@ -235,8 +243,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) key_scores_tc_kernel(KeyArgs a)
   {
     uint2* zr = reinterpret_cast<uint2*>(smem + L::kZeros);
     for (int i = threadIdx.x; i < 2048 / 8; i += blockDim.x) zr[i] = make_uint2(0, 0);
+    // constant A of the zero-point MMA: every row (K-major core matrices) has K 0, 1 = 256
+    uint32_t* ac = reinterpret_cast<uint32_t*>(smem + L::kAConst);
+    for (int i = threadIdx.x; i < 4096 / 4; i += blockDim.x)
+      ac[i] = ((i & 3) == 0 && ((i >> 5) & 1) == 0) ? kA256 : 0u;
   }
-  if (warp == kTcBlockWarps) tmem_alloc(tmem_ptr, kTcCols);
+  if (warp == kTcMmaWarp) tmem_alloc(tmem_ptr, kTcCols);
   int64_t cur_grp = w0 < w1 ? w0 / n_mt : -1;
   int cur_nu = 0;
   if (cur_grp >= 0) {
@@ -248,36 +260,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) key_scores_tc_kernel(KeyArgs a)
   tc_fence_after();
   const uint32_t tbase = *tmem_ptr;
   if (cur_grp >= 0) key_tc_fill<BITS>(a, smem, cur_grp * UG, cur_nu, 0, blockDim.x);
-  if (warp < 4) {  // constant A: K elements 0, 1 = 256 in every lane, the rest 0
-    const uint32_t v[8] = {kA256, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-    tmem_st_32x32b_x8(tbase + ((uint32_t)(32 * warp) << 16) + kTcAConst, v);
-    tmem_wait_st();
-  }
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
 
-  if (warp == kTcBlockWarps) {
-    // ================= copy / MMA warp =================
-    TcCursor cc, cm;  // next unit to copy, next unit to multiply
-    int64_t jc = 0, jm = 0;
-    const int64_t total = [&] {
-      int64_t n = 0;
-      for (int64_t w = w0; w < w1; ++w) n += min((int64_t)UG, U - (w / n_mt) * UG);
-      return n;
-    }();
-    if (w0 < w1) {
-      tc_cursor_begin(cc, w0, n_mt, UG, U);
-      tc_cursor_begin(cm, w0, n_mt, UG, U);
-    }
-    int64_t grp_m = cur_grp;
-    int n_change = 0;
-    bool ok = true;
-    auto copy_next = [&]() -> bool {
-      const int st = (int)(jc % kTcStages);
-      if (jc >= kTcStages && !mbar_wait(codes_empty + st, (uint32_t)(((jc / kTcStages) + 1) & 1), abort))
-        return false;
+  const int64_t total = [&] {  // units of this CTA's items
+    int64_t n = 0;
+    for (int64_t w = w0; w < w1; ++w) n += min((int64_t)UG, U - (w / n_mt) * UG);
+    return n;
+  }();
+  if (warp == kTcCopyWarp) {
+    // ================= copy warp: keeps every ring stage in flight =================
+    TcCursor cc;
+    int64_t jc = 0;
+    if (w0 < w1) tc_cursor_begin(cc, w0, n_mt, UG, U);
+    for (; jc < total; ++jc) {
+      const int st = (int)(jc % L::kStages);
+      if (jc >= L::kStages &&
+          !mbar_wait(codes_empty + st, (uint32_t)(((jc / L::kStages) + 1) & 1), abort))
+        break;
       const int64_t grp = cc.w / n_mt;
       const int tile0 = kTcTiles * (int)(cc.w % n_mt);
       const int64_t u = grp * UG + cc.ui;
@@ -289,33 +291,40 @@ __global__ void __launch_bounds__(kTcThreads, 1) key_scores_tc_kernel(KeyArgs a)
                  bytes, codes_full + st);
       }
       __syncwarp();
-      ++jc;
       tc_cursor_next(cc, n_mt, UG, U);
-      return true;
-    };
-    for (int k = 0; k < kTcStages - 1 && jc < total && ok; ++k) ok = copy_next();
+    }
+    // drain: every copy issued has landed (bounded) before the CTA exits
+    for (int64_t j = (jc > L::kStages ? jc - L::kStages : 0); j < jc; ++j)
+      mbar_wait(codes_full + (int)(j % L::kStages), (uint32_t)((j / L::kStages) & 1), abort, false);
+  } else if (warp == kTcMmaWarp) {
+    // ================= MMA warp =================
+    TcCursor cm;
+    int64_t jm = 0;
+    if (w0 < w1) tc_cursor_begin(cm, w0, n_mt, UG, U);
+    int64_t grp_m = cur_grp;
+    int n_change = 0;
+    bool ok = true;
+    const uint32_t ac = smem_addr(smem + L::kAConst);
+    const uint32_t zr = smem_addr(smem + L::kZeros);
     while (ok && jm < total) {
-      if (jc < total) {
-        ok = copy_next();
-        if (!ok) break;
-      }
       const int64_t grp = cm.w / n_mt;
       if (grp != grp_m) {
         // the block warps' epilogues of the previous group are done: new tables
         if (!mbar_wait(drained, (uint32_t)(n_change & 1), abort)) { ok = false; break; }
         grp_m = grp;
         const int nu = (int)min((int64_t)UG, U - grp * UG);
-        key_tc_tables<BITS>(a, smem, grp * UG, nu, kTcBlockWarps * 32, 32);
+        key_tc_tables<BITS>(a, smem, grp * UG, nu, kTcMmaWarp * 32, 32);
         __syncwarp();
-        key_tc_fill<BITS>(a, smem, grp * UG, nu, kTcBlockWarps * 32, 32);
+        key_tc_fill<BITS>(a, smem, grp * UG, nu, kTcMmaWarp * 32, 32);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(tables);
         ++n_change;
       }
-      const int buf = (int)(jm & 1);
-      if (!mbar_wait(a_full + buf, (uint32_t)((jm >> 1) & 1), abort)) { ok = false; break; }
-      if (jm >= 2 && !mbar_wait(d_empty + buf, (uint32_t)(((jm >> 1) + 1) & 1), abort)) {
+      const int ab = (int)(jm & 1), db = (int)(jm % kTcDBufs);
+      if (!mbar_wait(a_full + ab, (uint32_t)((jm >> 1) & 1), abort)) { ok = false; break; }
+      if (jm >= kTcDBufs &&
+          !mbar_wait(d_empty + db, (uint32_t)(((jm / kTcDBufs) + 1) & 1), abort)) {
         ok = false;
         break;
       }
@@ -323,25 +332,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) key_scores_tc_kernel(KeyArgs a)
       if (lane == 0) {
         const uint32_t bm = smem_addr(smem + L::kBMain + cm.ui * 4096);
         const uint32_t bz = smem_addr(smem + L::kBZero + cm.ui * 2048);
-        const uint32_t zr = smem_addr(smem + L::kZeros);
-        const uint32_t d = tbase + kTcD + 128u * buf;
-        const uint32_t av = tbase + kTcA + 64u * buf;
-        mma_f16_ts(d, tbase + kTcAConst, smem_desc(bz, zr - bz, 128), kTcIdescZero, 0u);
+        const uint32_t d = tbase + kTcD + 128u * db;
+        const uint32_t av = tbase + kTcA + 64u * ab;
+        mma_f16_ss(d, smem_desc(ac, 128, 256), smem_desc(bz, zr - bz, 128), kTcIdescZero, 0u);
 #pragma unroll
         for (int s = 0; s < 8; ++s)
           mma_f16_ts(d + 16u * s, av + 8u * s, smem_desc(bm + 512u * s, 128, 256), kTcIdescStep, 1u);
-        mma_commit(mma_done + buf);
+        mma_commit(mma_done + db);
       }
       __syncwarp();
       ++jm;
       tc_cursor_next(cm, n_mt, UG, U);
     }
-    // drain: every copy issued has landed and every MMA issued has completed
-    // (bounded waits) before the tensor memory is released
-    for (int64_t j = (jc > kTcStages ? jc - kTcStages : 0); j < jc; ++j)
-      mbar_wait(codes_full + (int)(j % kTcStages), (uint32_t)((j / kTcStages) & 1), abort, false);
+    // drain: every MMA issued has completed (bounded) before the tensor memory is released
     if (jm > 0)
-      mbar_wait(mma_done + (int)((jm - 1) & 1), (uint32_t)(((jm - 1) >> 1) & 1), abort, false);
+      mbar_wait(mma_done + (int)((jm - 1) % kTcDBufs), (uint32_t)(((jm - 1) / kTcDBufs) & 1), abort,
+                false);
   } else {
     // ================= block warps =================
     const int q4 = warp & 3, half = warp >> 2;  // TMEM quadrant, 16-lane half
@@ -360,20 +366,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) key_scores_tc_kernel(KeyArgs a)
     int n_change = 0;
     bool ok = true;
 
-    // pending unit for the epilogue
+    // units waiting for their epilogue (two behind the one being stored)
     struct Pending {
       int64_t j, w;
       int ui;
       int32_t e0, e1;
       uint32_t ent;
-    } pend;
-    pend.j = -1;
+      bool drain;  // the last unit of its group with a unit of another group after it
+    };
+    Pending pend[2];
+    pend[0].j = pend[1].j = -1;
 
     auto epilogue = [&](Pending& pd) -> bool {
-      const int buf = (int)(pd.j & 1);
+      const int db = (int)(pd.j % kTcDBufs);
       const int64_t grp = pd.w / n_mt;
       const int tile0 = kTcTiles * (int)(pd.w % n_mt);
-      if (grp != grp_e) {  // the control warp rebuilt the tables for this group
+      if (grp != grp_e) {  // the copy / MMA warp rebuilt the tables for this group
         if (!mbar_wait(tables, (uint32_t)(n_change & 1), abort)) return false;
         grp_e = grp;
         ++n_change;
@@ -391,29 +399,34 @@ __global__ void __launch_bounds__(kTcThreads, 1) key_scores_tc_kernel(KeyArgs a)
           tw[kb][1] = f2pack(c8, s8);
         }
       }
-      if (!mbar_wait(mma_done + buf, (uint32_t)((pd.j >> 1) & 1), abort)) return false;
+      if (!mbar_wait(mma_done + db, (uint32_t)((pd.j / kTcDBufs) & 1), abort)) return false;
       tc_fence_after();
-      const uint32_t dad = tbase + kTcD + 128u * buf + lane_off;
-      uint64_t acc0 = 0ull, acc1 = 0ull;
+      const uint32_t dad = tbase + kTcD + 128u * db + lane_off;
+      // (9 warps: a sub-partition holds three of them, so 168 registers per thread at most;
+      // the two halves of D are read one after the other)
+      uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};  // token g (kb even, odd), token g + 8 (even, odd)
       uint32_t d[32];
       tmem_ld_16x256b_x8(dad, d);
       tmem_wait_ld();
 #pragma unroll
       for (int kb = 0; kb < 8; ++kb) {
-        ffma2(acc0, tw[kb][0], f2pack(__uint_as_float(d[4 * kb]), __uint_as_float(d[4 * kb + 1])));
-        ffma2(acc1, tw[kb][1], f2pack(__uint_as_float(d[4 * kb + 2]), __uint_as_float(d[4 * kb + 3])));
+        ffma2(acc[kb & 1], tw[kb][0], f2pack(__uint_as_float(d[4 * kb]), __uint_as_float(d[4 * kb + 1])));
+        ffma2(acc[2 + (kb & 1)], tw[kb][1],
+              f2pack(__uint_as_float(d[4 * kb + 2]), __uint_as_float(d[4 * kb + 3])));
       }
       tmem_ld_16x256b_x8(dad + 64u, d);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(d_empty + buf);
+      if (lane == 0) mbar_arrive(d_empty + db);
 #pragma unroll
       for (int kb = 8; kb < 16; ++kb) {
-        ffma2(acc0, tw[kb][0], f2pack(__uint_as_float(d[4 * (kb - 8)]), __uint_as_float(d[4 * (kb - 8) + 1])));
-        ffma2(acc1, tw[kb][1], f2pack(__uint_as_float(d[4 * (kb - 8) + 2]), __uint_as_float(d[4 * (kb - 8) + 3])));
+        const int k8 = kb - 8;
+        ffma2(acc[kb & 1], tw[kb][0], f2pack(__uint_as_float(d[4 * k8]), __uint_as_float(d[4 * k8 + 1])));
+        ffma2(acc[2 + (kb & 1)], tw[kb][1],
+              f2pack(__uint_as_float(d[4 * k8 + 2]), __uint_as_float(d[4 * k8 + 3])));
       }
-      float x0 = f2sum(acc0), x1 = f2sum(acc1);
+      float x0 = f2sum(acc[0]) + f2sum(acc[1]), x1 = f2sum(acc[2]) + f2sum(acc[3]);
       x0 += __shfl_xor_sync(0xffffffffu, x0, 1);
       x1 += __shfl_xor_sync(0xffffffffu, x1, 1);
       x0 += __shfl_xor_sync(0xffffffffu, x0, 2);
@@ -469,6 +482,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) key_scores_tc_kernel(KeyArgs a)
         l += __shfl_xor_sync(0xffffffffu, l, 16);
         if (lane == 0) a.stats[row * nblk16 + t_blk / 16] = make_float2(m, l);
       }
+      if (pd.drain) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(drained);
+      }
       return true;
     };
 
@@ -478,23 +495,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) key_scores_tc_kernel(KeyArgs a)
       const int tile0 = kTcTiles * (int)(w % n_mt);
       const int nu = (int)min((int64_t)UG, U - grp * UG);
       const int my_tile = tile0 + tile_in_mt;
+      const bool next_item_other_group = w + 1 < w1 && (w + 1) / n_mt != grp;
       for (int ui = 0; ui < nu && ok; ++ui, ++j) {
         const int64_t u = grp * UG + ui;
-        // this unit's CSR rows (read now, used by its epilogue one iteration later)
+        // this unit's CSR rows (read now, used by its epilogue two iterations later)
         int32_t e0 = 0, e1 = 0;
         if (my_tile < nt) {
           const int64_t r = 2 * (u * a.nt_cap + my_tile) + blk;
           e0 = __ldg(a.out_ptr + r);
           e1 = __ldg(a.out_ptr + r + 1);
         }
-        // the pending unit's first entries (its row pointers arrived last iteration)
-        if (pend.j >= 0) {
-          const int32_t e = pend.e0 + lane;
-          pend.ent = e < pend.e1 ? __ldg(a.out_ent + e) : 0u;
+        // the oldest pending unit's first entries (its row pointers arrived earlier)
+        if (pend[0].j >= 0) {
+          const int32_t e = pend[0].e0 + lane;
+          pend[0].ent = e < pend[0].e1 ? __ldg(a.out_ent + e) : 0u;
         }
         // code values of this unit's block -> TMEM A
-        const int st = (int)(j % kTcStages);
-        if (!mbar_wait(codes_full + st, (uint32_t)((j / kTcStages) & 1), abort)) { ok = false; break; }
+        const int st = (int)(j % L::kStages);
+        if (!mbar_wait(codes_full + st, (uint32_t)((j / L::kStages) & 1), abort)) { ok = false; break; }
         const uint8_t* sb = smem + L::kRing + st * L::kStageBytes + tile_in_mt * (2 * L::kBlockBytes) +
                             blk * L::kBlockBytes;
         LaneSlab<BITS> sl;
@@ -512,49 +530,58 @@ __global__ void __launch_bounds__(kTcThreads, 1) key_scores_tc_kernel(KeyArgs a)
                   *reinterpret_cast<const uint32_t*>(lut + sl.addr(4 * rep + 2 * jj + r, lane4));
           }
         }
-        const int buf = (int)(j & 1);
-        tmem_st_16x256b_x8(tbase + kTcA + 64u * buf + lane_off, v);
+        // A buffer j & 1 was read by the MMAs of unit j - 2
+        if (j >= 2 && !mbar_wait(mma_done + (int)((j - 2) % kTcDBufs),
+                                 (uint32_t)(((j - 2) / kTcDBufs) & 1), abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        tmem_st_16x256b_x8(tbase + kTcA + 64u * (uint32_t)(j & 1) + lane_off, v);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(a_full + buf);
-        if (pend.j >= 0) {
-          const bool last_of_group = pend.w / n_mt != grp;
-          if (!epilogue(pend)) { ok = false; break; }
-          if (last_of_group) {
-            __syncwarp();
-            if (lane == 0) mbar_arrive(drained);
-          }
-        }
-        pend.j = j;
-        pend.w = w;
-        pend.ui = ui;
-        pend.e0 = e0;
-        pend.e1 = e1;
-        pend.ent = 0u;
+        if (lane == 0) mbar_arrive(a_full + (int)(j & 1));
+        if (pend[0].j >= 0 && !epilogue(pend[0])) { ok = false; break; }
+        pend[0] = pend[1];
+        pend[1].j = j;
+        pend[1].w = w;
+        pend[1].ui = ui;
+        pend[1].e0 = e0;
+        pend[1].e1 = e1;
+        pend[1].ent = 0u;
+        pend[1].drain = ui == nu - 1 && next_item_other_group;
       }
     }
-    if (ok && pend.j >= 0) {
-      const int32_t e = pend.e0 + lane;
-      pend.ent = e < pend.e1 ? __ldg(a.out_ent + e) : 0u;
-      epilogue(pend);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      if (ok && pend[k].j >= 0) {
+        const int32_t e = pend[k].e0 + lane;
+        pend[k].ent = e < pend[k].e1 ? __ldg(a.out_ent + e) : 0u;
+        ok = epilogue(pend[k]);
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == kTcBlockWarps) tmem_dealloc(tbase, kTcCols);
+  if (warp == kTcMmaWarp) tmem_dealloc(tbase, kTcCols);
 }
 
 // One query head per KV head runs on this kernel unless the environment sets
 // KVQ_KEY_KERNEL=mma (the mma.sync kernel, kept for group sizes > 1), read once.
-inline bool use_key_tc() {
-  static const bool tc = [] {
+// Kernel choice: 0 = warp-level mma.sync kernel (the default), 1 = tcgen05
+// kernel. Starts from KVQ_KEY_KERNEL ("tc" selects tcgen05), changed by
+// kvq_set_decode_kernels.
+inline std::atomic<int>& g_key_kernel() {
+  static std::atomic<int> k{[] {
     const char* e = getenv("KVQ_KEY_KERNEL");
-    return !(e && e[0] == 'm');
-  }();
-  return tc;
+    return (e && e[0] == 't') ? 1 : 0;
+  }()};
+  return k;
 }
+
+inline bool use_key_tc() { return g_key_kernel().load(std::memory_order_relaxed) == 1; }
 
 template <int BITS>
 static int launch_key_tc(const KeyArgs& a0, cudaStream_t st) {

@@ -27,6 +27,7 @@
 // 3-stage ring and issues the MMAs; A and B are double-buffered by chunk.
 // Two CTAs share an SM (256 TMEM columns each).
 #pragma once
+#include <atomic>
 #include <cstdlib>
 
 #include "kvq_decode.cuh"
@@ -35,31 +36,51 @@
 namespace kvq {
 
 constexpr int kVtWorkers = 8;
-constexpr int kVtThreads = (kVtWorkers + 1) * 32;
+constexpr int kVtMmaWarp = kVtWorkers;
+constexpr int kVtCopyWarp = kVtWorkers + 1;
+constexpr int kVtThreads = (kVtWorkers + 2) * 32;
 constexpr int kVtTiles = 4;                       // code tiles per chunk
-constexpr int kVtStages = 3;
-constexpr uint32_t kVtCols = 256;                 // TMEM: A [0, 128) (two buffers), D [128, 144)
-constexpr uint32_t kVtA = 0, kVtD = 128;
+constexpr int kVtBufs = 3;                        // A / B buffers (chunks in the MMA pipeline)
+constexpr uint32_t kVtCols = 512;                 // TMEM: A [0, 384) (three buffers), D [384, 400)
+constexpr uint32_t kVtA = 0, kVtD = 384;
+constexpr uint32_t kVtACols = 128;                // per buffer: A_hi [0, 64), A_lo [64, 128)
 constexpr int kVtMaxG = 8;
 constexpr uint32_t kVtIdesc = sm100::idesc_f16_f32(128, 16);
+
+constexpr int kVtEnt = 256;  // outlier entries of a chunk staged in shared memory
 
 template <int BITS, int G>
 struct ValTcSmem {
   static constexpr int kBlockBytes = 256 * BITS;
   static constexpr int kStageBytes = kVtTiles * 2 * kBlockBytes;
-  static constexpr int kRing = PairLut<BITS>::kBytes;
-  static constexpr int kB = kRing + kVtStages * kStageBytes;   // [2][8 blocks][512 B]
-  static constexpr int kAcc = kB + 2 * 8 * 512;                // [G][128] int64 outlier sums
+  // per-chunk side data staged with the codes: scores / probabilities [G][128],
+  // scale [128], zero [128], CSR row pointers [9] (+3 pad), entries [kVtEnt]
+  static constexpr int kSdP = 0;
+  static constexpr int kSdS = kSdP + G * 128 * 4;
+  static constexpr int kSdZ = kSdS + 512;
+  static constexpr int kSdR = kSdZ + 512;
+  static constexpr int kSdE = kSdR + 48;
+  static constexpr int kSideBytes = kSdE + kVtEnt * 4;
+  static constexpr int kB = PairLutHiLo<BITS>::kBytes;        // [kVtBufs][8 blocks][512 B]
+  static constexpr int kAcc = kB + kVtBufs * 8 * 512;          // [G][128] int64 outlier sums
   static constexpr int kZs = kAcc + G * 128 * 8;               // [8 warps][G] float zero terms
   static constexpr int kMl = kZs + kVtWorkers * G * 4;         // [G] float2 (M, 1/L)
   static constexpr int kBars = (kMl + G * 8 + 7) / 8 * 8;
-  // codes_full[S], codes_empty[S], a_full[2], mma_done[2]
-  static constexpr int kNumBars = 2 * kVtStages + 4;
+  // codes_full[S], codes_empty[S], a_full[kVtBufs], mma_done[kVtBufs]; the ring
+  // (code tiles + side data per stage) fills the rest of shared memory
+  static constexpr int kFixed = kBars + (2 * 24 + 2 * kVtBufs) * 8 + 16;
+  static constexpr int kStagesFit = (232448 - kFixed - 128) / (kStageBytes + kSideBytes);
+  static constexpr int kStages = kStagesFit > 24 ? 24 : kStagesFit;
+  static constexpr int kNumBars = 2 * kStages + 2 * kVtBufs;
   static constexpr int kTmemPtr = kBars + kNumBars * 8;
   static constexpr int kAbort = kTmemPtr + 4;
-  static constexpr int kBytes = kAbort + 12;
-  static_assert(kBytes <= 232448 / 2 - 1024, "two value CTAs per SM");
-  static_assert(kB % 16 == 0 && kRing % 16 == 0, "alignment");
+  static constexpr int kRing = (kAbort + 12 + 127) / 128 * 128;
+  static constexpr int kSide = kRing + kStages * kStageBytes;
+  static constexpr int kBytes = kSide + kStages * kSideBytes;
+  static_assert(kStages >= 4, "value code ring");
+  static_assert(kBytes <= 232448, "value kernel shared memory");
+  static_assert(kB % 16 == 0 && kRing % 16 == 0 && kSide % 16 == 0 && kSideBytes % 16 == 0,
+                "alignment");
 };
 
 // The 8 code pairs of TMEM quadrant qd (slab slots 8qd .. 8qd + 7, channel
@@ -87,17 +108,18 @@ __device__ __forceinline__ void vt_quadrant_pairs(const uint8_t* blk, int lane, 
   }
 }
 
-// Pair-LUT byte address of quadrant pair i (0..7) for this lane.
+// Pair-LUT byte address of quadrant pair i (0..7) for this lane (lane_off =
+// the lane's byte offset within a 256-byte entry row).
 template <int BITS>
-__device__ __forceinline__ uint32_t vt_pair_addr(uint32_t lo, uint32_t hi, int i, uint32_t lane4) {
-  if (BITS == 4) return prmt(lane4, i < 4 ? lo : hi, 0x1100u | ((4u + (i & 3)) << 4));
-  if (BITS == 2) return (((lo >> (4 * i)) & 15u) << 8) | lane4;
+__device__ __forceinline__ uint32_t vt_pair_addr(uint32_t lo, uint32_t hi, int i, uint32_t lane_off) {
+  if (BITS == 4) return prmt(lane_off, i < 4 ? lo : hi, 0x1100u | ((4u + (i & 3)) << 4));
+  if (BITS == 2) return (((lo >> (4 * i)) & 15u) << 8) | lane_off;
   const uint64_t v = ((uint64_t)hi << 32) | lo;
-  return ((uint32_t)((v >> (6 * i)) & 63u) << 8) | lane4;
+  return ((uint32_t)((v >> (6 * i)) & 63u) << 8) | lane_off;
 }
 
 template <int BITS, int G>
-__global__ void __launch_bounds__(kVtThreads, 2)
+__global__ void __launch_bounds__(kVtThreads, 1)
     value_tc_kernel(ValueArgs a, const float* __restrict__ row_max) {
   extern __shared__ __align__(16) uint8_t smem[];
   using L = ValTcSmem<BITS, G>;
@@ -105,9 +127,9 @@ __global__ void __launch_bounds__(kVtThreads, 2)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBars);
   uint64_t* codes_full = bars;
-  uint64_t* codes_empty = bars + kVtStages;
-  uint64_t* a_full = bars + 2 * kVtStages;
-  uint64_t* mma_done = a_full + 2;
+  uint64_t* codes_empty = bars + L::kStages;
+  uint64_t* a_full = bars + 2 * L::kStages;
+  uint64_t* mma_done = a_full + kVtBufs;
   uint32_t* tmem_ptr = reinterpret_cast<uint32_t*>(smem + L::kTmemPtr);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kAbort);
   unsigned long long* acc = reinterpret_cast<unsigned long long*>(smem + L::kAcc);
@@ -137,40 +159,47 @@ __global__ void __launch_bounds__(kVtThreads, 2)
   const int64_t tbytes = (int64_t)tile_bytes(BITS);
 
   // ---- set-up ----
-  PairLut<BITS>::build(smem, a.cb);
+  PairLutHiLo<BITS>::build(smem, a.cb);
   {
     uint4* z = reinterpret_cast<uint4*>(smem + L::kB);
-    for (int i = threadIdx.x; i < (2 * 8 * 512) / 16; i += blockDim.x) z[i] = make_uint4(0, 0, 0, 0);
+    for (int i = threadIdx.x; i < (kVtBufs * 8 * 512) / 16; i += blockDim.x) z[i] = make_uint4(0, 0, 0, 0);
     for (int i = threadIdx.x; i < G * 128; i += blockDim.x) acc[i] = 0ull;
   }
   if (a.ml && threadIdx.x < G) s_ml[threadIdx.x] = a.ml[b * HG + h * G + threadIdx.x];
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kVtStages; ++s) {
-      mbar_init(codes_full + s, 1);
+    for (int s = 0; s < L::kStages; ++s) {
+      mbar_init(codes_full + s, 1 + 32);  // the bulk copy's arrival + one per copying lane
       mbar_init(codes_empty + s, kVtWorkers);
     }
-    for (int k = 0; k < 2; ++k) {
+    for (int k = 0; k < kVtBufs; ++k) {
       mbar_init(a_full + k, kVtWorkers);
       mbar_init(mma_done + k, 1);
     }
     *abort = 0;
     fence_mbar_init();
   }
-  if (warp == kVtWorkers) tmem_alloc(tmem_ptr, kVtCols);
+  if (warp == kVtMmaWarp) tmem_alloc(tmem_ptr, kVtCols);
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_ptr;
 
-  if (warp == kVtWorkers) {
-    // ================= copy / MMA warp =================
+  if (warp == kVtCopyWarp) {
+    // ================= copy warp: code tiles + side data, every stage in flight =================
     int jc = 0;
-    bool ok = true;
+    // this lane's CSR row pointer (lanes 0..8) of chunks jc .. jc + 3, loaded ahead
+    auto rp_of = [&](int ch) -> int32_t {
+      if (ch >= n_chunks || lane > 8) return 0;
+      const int tile0 = ta + kVtTiles * ch;
+      const int ntl = min(kVtTiles, tb - tile0);
+      return __ldg(a.out_ptr + 2 * (u * a.nt_cap + tile0) + min(lane, 2 * ntl));
+    };
+    int32_t rpa = rp_of(0), rpb = rp_of(1), rpc = rp_of(2), rpd = rp_of(3);
     auto copy_next = [&]() -> bool {
-      const int st = jc % kVtStages;
-      if (jc >= kVtStages &&
-          !mbar_wait(codes_empty + st, (uint32_t)(((jc / kVtStages) + 1) & 1), abort))
+      const int st = jc % L::kStages;
+      if (jc >= L::kStages &&
+          !mbar_wait(codes_empty + st, (uint32_t)(((jc / L::kStages) + 1) & 1), abort))
         return false;
       const int tile0 = ta + kVtTiles * jc;
       const int ntl = min(kVtTiles, tb - tile0);
@@ -180,127 +209,159 @@ __global__ void __launch_bounds__(kVtThreads, 2)
         bulk_g2s(smem + L::kRing + st * L::kStageBytes, a.codes + (u * a.nt_cap + tile0) * tbytes,
                  bytes, codes_full + st);
       }
-      __syncwarp();
+      // side data of the chunk's 128 tokens (zero beyond the split and the cache)
+      uint8_t* sd = smem + L::kSide + st * L::kSideBytes;
+      const int t0 = tile0 * kTileTokens;
+      const int tend = min(T, tb * kTileTokens);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int t = t0 + lane + 32 * k;
+        const bool in = t < tend;
+        const int tc = in ? t : 0;
+#pragma unroll
+        for (int hd = 0; hd < G; ++hd)
+          cp_async_4(sd + L::kSdP + (hd * 128 + lane + 32 * k) * 4, prow + hd * a.T + tc, in ? 4u : 0u);
+        cp_async_4(sd + L::kSdS + (lane + 32 * k) * 4, vs + tc, in ? 4u : 0u);
+        cp_async_4(sd + L::kSdZ + (lane + 32 * k) * 4, vz + tc, in ? 4u : 0u);
+      }
+      // row pointers of the chunk's blocks (rows past the split repeat the last one)
+      const int64_t r0 = 2 * (u * a.nt_cap + tile0);
+      const int64_t rk = r0 + min(lane, 2 * ntl);
+      const int32_t rp_lane = rpa;
+      rpa = rpb;
+      rpb = rpc;
+      rpc = rpd;
+      rpd = rp_of(jc + 4);
+      if (lane <= 8) cp_async_4(sd + L::kSdR + lane * 4, a.out_ptr + rk, 4u);
+      const int32_t e_lo = __shfl_sync(0xffffffffu, rp_lane, 0);
+      const int32_t e_hi = __shfl_sync(0xffffffffu, rp_lane, 8);
+      const int32_t ne = min(e_hi - e_lo, kVtEnt);
+      for (int k = lane; k < ne; k += 32)
+        cp_async_4(sd + L::kSdE + k * 4, a.out_ent + e_lo + k, 4u);
+      cp_async_arrive(codes_full + st);
       ++jc;
       return true;
     };
-    for (int k = 0; k < kVtStages - 1 && jc < n_chunks && ok; ++k) ok = copy_next();
+    for (; jc < n_chunks;)
+      if (!copy_next()) break;
+    for (int j = (jc > L::kStages ? jc - L::kStages : 0); j < jc; ++j)
+      mbar_wait(codes_full + j % L::kStages, (uint32_t)((j / L::kStages) & 1), abort, false);
+  } else if (warp == kVtMmaWarp) {
+    // ================= MMA warp =================
     int jm = 0;
-    for (; ok && jm < n_chunks; ++jm) {
-      if (jc < n_chunks && !(ok = copy_next())) break;
-      const int buf = jm & 1;
-      if (!mbar_wait(a_full + buf, (uint32_t)((jm >> 1) & 1), abort)) { ok = false; break; }
+    for (; jm < n_chunks; ++jm) {
+      const int buf = jm % kVtBufs;
+      if (!mbar_wait(a_full + buf, (uint32_t)((jm / kVtBufs) & 1), abort)) break;
       tc_fence_after();
       if (lane == 0) {
         const uint32_t bb = smem_addr(smem + L::kB + buf * 4096);
+        const uint32_t ab = tbase + kVtA + kVtACols * buf;
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          mma_f16_ts(tbase + kVtD, tbase + kVtA + 64u * buf + 8u * k,
-                     smem_desc(bb + 512u * k, 128, 256), kVtIdesc, (jm > 0 || k > 0) ? 1u : 0u);
+        for (int k = 0; k < 8; ++k) {  // code values' high parts, then their low parts
+          mma_f16_ts(tbase + kVtD, ab + 8u * k, smem_desc(bb + 512u * k, 128, 256), kVtIdesc,
+                     (jm > 0 || k > 0) ? 1u : 0u);
+          mma_f16_ts(tbase + kVtD, ab + 64u + 8u * k, smem_desc(bb + 512u * k, 128, 256), kVtIdesc,
+                     1u);
+        }
         mma_commit(mma_done + buf);
       }
       __syncwarp();
     }
-    for (int j = (jc > kVtStages ? jc - kVtStages : 0); j < jc; ++j)
-      mbar_wait(codes_full + j % kVtStages, (uint32_t)((j / kVtStages) & 1), abort, false);
-    if (jm > 0) mbar_wait(mma_done + ((jm - 1) & 1), (uint32_t)(((jm - 1) >> 1) & 1), abort, false);
+    if (jm > 0)
+      mbar_wait(mma_done + (jm - 1) % kVtBufs, (uint32_t)(((jm - 1) / kVtBufs) & 1), abort, false);
   } else {
     // ================= worker warps =================
     const int qd = warp & 3, hw = warp >> 2;
     const int wblk = 4 * hw + qd;  // the block whose weights and outliers this warp handles
-    const uint32_t lane4 = (uint32_t)lane << 2;
+    const uint32_t lane8 = (uint32_t)lane << 3;
     const uint8_t* lut = smem;
     float zs[G];
 #pragma unroll
     for (int hd = 0; hd < G; ++hd) zs[hd] = 0.f;
-    // this lane's token inputs of the next chunk (lanes 0..15)
-    float nx_p[G], nx_s = 0.f, nx_z = 0.f;
-    int32_t nx_e0 = 0, nx_e1 = 0;
-    auto fetch = [&](int ch) {
-      const int tile = ta + kVtTiles * ch + (wblk >> 1);
-      const int t = tile * kTileTokens + 16 * (wblk & 1) + (lane & 15);
-      const bool live = ch < n_chunks && tile < tb && lane < 16 && t < T && !(sink && t == 0);
-#pragma unroll
-      for (int hd = 0; hd < G; ++hd) nx_p[hd] = live ? __ldg(prow + hd * a.T + t) : -INFINITY;
-      nx_s = live ? __ldg(vs + t) : 0.f;
-      nx_z = live ? __ldg(vz + t) : 0.f;
-      nx_e0 = nx_e1 = 0;
-      if (ch < n_chunks && tile < tb) {
-        const int64_t r = 2 * (u * a.nt_cap + tile) + (wblk & 1);
-        nx_e0 = __ldg(a.out_ptr + r);
-        nx_e1 = __ldg(a.out_ptr + r + 1);
-      }
-      if (!a.ml) {  // probabilities given: 0 for tokens outside the cache
-#pragma unroll
-        for (int hd = 0; hd < G; ++hd) nx_p[hd] = live ? nx_p[hd] : 0.f;
-      }
-    };
-    fetch(0);
+    const int wt = 16 * wblk + (lane & 15);  // this lane's token of the chunk (lanes 0..15)
     bool ok = true;
     for (int ch = 0; ch < n_chunks && ok; ++ch) {
-      const int buf = ch & 1;
+      const int buf = ch % kVtBufs;
+      const int st = ch % L::kStages;
+      if (!mbar_wait(codes_full + st, (uint32_t)((ch / L::kStages) & 1), abort)) { ok = false; break; }
+      const uint8_t* sd = smem + L::kSide + st * L::kSideBytes;
       // weights of block wblk: p (from the raw score when the stats are given), p s, p z
+      const int tile = ta + kVtTiles * ch + (wblk >> 1);
+      const int t = tile * kTileTokens + 16 * (wblk & 1) + (lane & 15);
+      const bool live = tile < tb && lane < 16 && t < T && !(sink && t == 0);
+      const float s_t = live ? reinterpret_cast<const float*>(sd + L::kSdS)[wt] : 0.f;
+      const float z_t = live ? reinterpret_cast<const float*>(sd + L::kSdZ)[wt] : 0.f;
+      const int32_t* srp = reinterpret_cast<const int32_t*>(sd + L::kSdR);
+      const int32_t ebase = srp[0], e0 = srp[wblk], e1 = srp[wblk + 1];
       float p[G], ps[G];
-      const float s_t = nx_s, z_t = nx_z;
-      const int32_t e0 = nx_e0, e1 = nx_e1;
 #pragma unroll
       for (int hd = 0; hd < G; ++hd) {
-        p[hd] = a.ml ? (nx_p[hd] == -INFINITY ? 0.f
-                                              : __expf(nx_p[hd] * a.stat_scale - s_ml[hd].x) * s_ml[hd].y)
-                     : nx_p[hd];
+        const float x = reinterpret_cast<const float*>(sd + L::kSdP)[hd * 128 + wt];
+        p[hd] = !live ? 0.f
+                      : (a.ml ? __expf(x * a.stat_scale - s_ml[hd].x) * s_ml[hd].y : x);
         ps[hd] = p[hd] * s_t;
         zs[hd] = fmaf(p[hd], z_t, zs[hd]);
       }
-      fetch(ch + 1);
-      // buffers of chunk ch: free once the MMAs of chunk ch - 2 are done
-      if (ch >= 2 && !mbar_wait(mma_done + buf, (uint32_t)(((ch >> 1) + 1) & 1), abort)) {
+      // buffers of chunk ch: free once the MMAs of chunk ch - kVtBufs are done
+      if (ch >= kVtBufs &&
+          !mbar_wait(mma_done + buf, (uint32_t)(((ch / kVtBufs) + 1) & 1), abort)) {
         ok = false;
         break;
       }
+      tc_fence_after();
       if (lane < 16) {
         // token tau = lane of the block sits at K index 2j + (tau & 1), j = 2((tau >> 1) & 3) + (tau >> 3)
         const int tau = lane;
         const int k = 2 * (2 * ((tau >> 1) & 3) + (tau >> 3)) + (tau & 1);
         __half* bw = reinterpret_cast<__half*>(smem + L::kB + buf * 4096 + wblk * 512);
+        // rows 0..G-1: the weights' fp16 high parts; rows 8..8+G-1: their low parts
 #pragma unroll
-        for (int hd = 0; hd < G; ++hd)
-          bw[((hd >> 3) * 256 + (k >> 3) * 128 + (hd & 7) * 16 + (k & 7) * 2) / 2] =
-              __float2half_rn(ps[hd] * e_scale);
+        for (int hd = 0; hd < G; ++hd) {
+          const float wv = ps[hd] * e_scale;
+          const __half wh = __float2half_rn(wv);
+          bw[((k >> 3) * 128 + hd * 16 + (k & 7) * 2) / 2] = wh;
+          bw[(256 + (k >> 3) * 128 + hd * 16 + (k & 7) * 2) / 2] =
+              __float2half_rn(wv - __half2float(wh));
+        }
       }
       fence_proxy_async_smem();
       // codes of blocks 4hw .. 4hw + 3, channel blocks 2qd, 2qd + 1 -> TMEM A
-      const int st = ch % kVtStages;
-      if (!mbar_wait(codes_full + st, (uint32_t)((ch / kVtStages) & 1), abort)) { ok = false; break; }
       const uint8_t* sb = smem + L::kRing + st * L::kStageBytes;
-      uint32_t va[16], vb[16];  // channel block 2qd, 2qd + 1
+      uint32_t qlo[4], qhi[4];  // the quadrant's code pairs of blocks 4hw .. 4hw + 3
 #pragma unroll
-      for (int rep = 0; rep < 4; ++rep) {
-        uint32_t lo, hi;
-        vt_quadrant_pairs<BITS>(sb + (4 * hw + rep) * L::kBlockBytes, lane, qd, lo, hi);
+      for (int rep = 0; rep < 4; ++rep)
+        vt_quadrant_pairs<BITS>(sb + (4 * hw + rep) * L::kBlockBytes, lane, qd, qlo[rep], qhi[rep]);
+      const uint32_t acol = tbase + kVtA + kVtACols * buf + 32u * hw;
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
+      for (int m = 0; m < 2; ++m) {  // channel blocks 2qd + m: TMEM lanes 32qd + 16m
+        uint32_t vh[16], vl[16];
 #pragma unroll
-          for (int jj = 0; jj < 2; ++jj) {
-            va[4 * rep + 2 * r + jj] =
-                *reinterpret_cast<const uint32_t*>(lut + vt_pair_addr<BITS>(lo, hi, r + 2 * jj, lane4));
-            vb[4 * rep + 2 * r + jj] =
-                *reinterpret_cast<const uint32_t*>(lut + vt_pair_addr<BITS>(lo, hi, 4 + r + 2 * jj, lane4));
+        for (int rep = 0; rep < 4; ++rep) {
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {
+              const uint2 e = *reinterpret_cast<const uint2*>(
+                  lut + vt_pair_addr<BITS>(qlo[rep], qhi[rep], 4 * m + r + 2 * jj, lane8));
+              vh[4 * rep + 2 * r + jj] = e.x;
+              vl[4 * rep + 2 * r + jj] = e.y;
+            }
           }
         }
+        const uint32_t lanes = (uint32_t)(32 * qd + 16 * m) << 16;
+        tmem_st_16x256b_x4(acol + lanes, vh);
+        tmem_st_16x256b_x4(acol + 64u + lanes, vl);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(codes_empty + st);
-      const uint32_t acol = tbase + kVtA + 64u * buf + 32u * hw;
-      tmem_st_16x256b_x4(acol + ((uint32_t)(32 * qd) << 16), va);
-      tmem_st_16x256b_x4(acol + ((uint32_t)(32 * qd + 16) << 16), vb);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(a_full + buf);
       // outliers of block wblk: p_t s_t o into (head, channel), fixed point
+      const uint32_t* sent = reinterpret_cast<const uint32_t*>(sd + L::kSdE);
       for (int32_t eb = e0; eb < e1; eb += 32) {
         const int32_t e = eb + lane;
-        const uint32_t en = e < e1 ? __ldg(a.out_ent + e) : 0u;
+        const int32_t rel = e - ebase;
+        const uint32_t en = e < e1 ? (rel < kVtEnt ? sent[rel] : __ldg(a.out_ent + e)) : 0u;
         const int tok = (int)((en >> 7) & 15), chn = (int)(en & 127);
         const float o = entry_value(en);
 #pragma unroll
@@ -310,6 +371,9 @@ __global__ void __launch_bounds__(kVtThreads, 2)
             atomicAdd(acc + hd * 128 + chn, (unsigned long long)__float2ll_rn(w * o * fix));
         }
       }
+      // every lane is done with the stage's side data and codes
+      __syncwarp();
+      if (lane == 0) mbar_arrive(codes_empty + st);
     }
     // zero terms of the warp's tokens
 #pragma unroll
@@ -323,8 +387,8 @@ __global__ void __launch_bounds__(kVtThreads, 2)
   __syncthreads();
   tc_fence_after();
   if (warp < 4 && n_chunks > 0) {
-    if (mbar_wait(mma_done + ((n_chunks - 1) & 1), (uint32_t)(((n_chunks - 1) >> 1) & 1), abort,
-                  false)) {
+    if (mbar_wait(mma_done + (n_chunks - 1) % kVtBufs,
+                  (uint32_t)(((n_chunks - 1) / kVtBufs) & 1), abort, false)) {
       tc_fence_after();
       uint32_t d[16];
       tmem_ld_32x32b_x16(tbase + kVtD + ((uint32_t)(32 * warp) << 16), d);
@@ -339,7 +403,7 @@ __global__ void __launch_bounds__(kVtThreads, 2)
           side = fmaf(p0, __half2float(a.v_sink[(b * a.H + h) * kHeadDim + dd]), side);
         }
         float* dst = a.partial + ((int64_t)split * (U * G) + u * G + hd) * 129;
-        dst[dd] = fmaf(__uint_as_float(d[hd]), inv_e, side);
+        dst[dd] = fmaf(__uint_as_float(d[hd]) + __uint_as_float(d[8 + hd]), inv_e, side);
         if (dd == 0) {
           float z = 0.f;
 #pragma unroll
@@ -359,18 +423,23 @@ __global__ void __launch_bounds__(kVtThreads, 2)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == kVtWorkers) tmem_dealloc(tbase, kVtCols);
+  if (warp == kVtMmaWarp) tmem_dealloc(tbase, kVtCols);
 }
 
 // Every group size runs on this kernel unless the environment sets
 // KVQ_VALUE_KERNEL=mma (the mma.sync kernel), read once.
-inline bool use_value_tc() {
-  static const bool tc = [] {
+// Kernel choice: 0 = warp-level mma.sync kernel (the default), 1 = tcgen05
+// kernel. Starts from KVQ_VALUE_KERNEL ("tc" selects tcgen05), changed by
+// kvq_set_decode_kernels.
+inline std::atomic<int>& g_value_kernel() {
+  static std::atomic<int> k{[] {
     const char* e = getenv("KVQ_VALUE_KERNEL");
-    return !(e && e[0] == 'm');
-  }();
-  return tc;
+    return (e && e[0] == 't') ? 1 : 0;
+  }()};
+  return k;
 }
+
+inline bool use_value_tc() { return g_value_kernel().load(std::memory_order_relaxed) == 1; }
 
 template <int BITS, int G>
 static int launch_value_tc(const ValueArgs& a, const float* row_max, cudaStream_t st) {

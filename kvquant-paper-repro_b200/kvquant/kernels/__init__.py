@@ -5,7 +5,7 @@ from .cuda_ops import get_cuda_ops, cuda_available
 from .decode import (quantize_keys, quantize_values, qk_scores, qk_scores_stats, softmax,
                      pv_out, pv_out_scores, decode_attention, make_appendable, append_keys,
                      append_values, key_outlier_thresholds, decode_attention_shard,
-                     merge_shards)
+                     merge_shards, set_decode_kernels)
 
 __all__ = [
     "apply_rope_elementwise",
@@ -30,4 +30,5 @@ __all__ = [
     "key_outlier_thresholds",
     "decode_attention_shard",
     "merge_shards",
+    "set_decode_kernels",
 ]

@@ -36,6 +36,8 @@ _SIGNATURES = {
     "kvq_last_error": (ctypes.c_char_p, []),
     "kvq_version": (_c_int, []),
     "kvq_check_status": (_c_int, [_c_p]),
+    "kvq_set_decode_kernels": (_c_int, [_c_int, _c_int]),
+    "kvq_decode_kernels": (_c_int, []),
     "kvq_rope_apply": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                                 _c_i64, _c_p]),
     "kvq_lut_matvec": (_c_int, [_c_p, _c_p, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_i64,

@@ -356,6 +356,27 @@ def merge_shards(o_shards: torch.Tensor, ml_shards: torch.Tensor,
     return out
 
 
+_KERNELS = {"mma": 0, "tc": 1}
+
+
+def set_decode_kernels(key: str | None = None, value: str | None = None) -> tuple[str, str]:
+    """Selects the decode kernels process-wide and returns the previous choice.
+
+    "mma" = warp-level mma.sync kernels (the default), "tc" = tcgen05 kernels
+    with TMEM accumulators (the key one serves one query head per KV head);
+    None keeps the current one. Both compute the same values up to fp32
+    summation order."""
+    lib = get_cuda_ops().lib
+    cur = lib.kvq_decode_kernels()
+    names = {v: k for k, v in _KERNELS.items()}
+    prev = (names[cur & 1], names[(cur >> 1) & 1])
+    for x in (key, value):
+        if x is not None and x not in _KERNELS:
+            raise ValueError(f"decode kernel must be one of {sorted(_KERNELS)}, got {x!r}")
+    _check(lib.kvq_set_decode_kernels(_KERNELS.get(key, -1), _KERNELS.get(value, -1)), lib)
+    return prev
+
+
 class DecodeWorkspace:
     """Reusable scratch for decode_attention (one per stream)."""
 
