@@ -264,6 +264,11 @@ DRAM_PER_ALGORITHMIC_BYTE = {"key_scores": 618100480 / 615776256,
                              "value_output": 622502400 / 608452480}
 
 
+TRAFFIC_SOURCE = ("not measured on this launch: the DRAM bytes per algorithmic byte of one "
+                  "ncu capture at 262144 tokens x 32 KV heads, 4-bit "
+                  "(profiles/decode_kernels_longctx-4bit_262144tok.md), times this launch's "
+                  "algorithmic bytes")
+
 L2_BYTES = 126 * 2**20  # B200 L2
 
 
@@ -548,6 +553,7 @@ def run_gpu(args):
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
                          "peak_source": peak_src, "unit": "GB/s", "frac": achieved / peak,
                          "traffic": ab[dom] * DRAM_PER_ALGORITHMIC_BYTE[dom],
+                         "traffic_source": TRAFFIC_SOURCE,
                          "bytes_per_launch": ab[dom], "launch_ms": dom_ms},
             "step_bandwidth_gbs": step_bytes / (ms_step / 1e3) / 1e9,
             "kernels_ms": {"key_scores": k_avg, "value_output": v_avg},

@@ -187,7 +187,11 @@ __global__ void __launch_bounds__(128) append_kernel(AppendArgs a) {
           out = a.outliers && selected(abs_bits(n), (int32_t)cfull, s_rs[i]);
         }
         const float dense = out ? 0.f : fminf(fmaxf(n, -1.f), 1.f);
-        s_code[i][c] = (uint8_t)nearest_centroid_sorted(dense, s_cbs, s_cbi, ncb);
+        const int code = nearest_centroid_sorted(dense, s_cbs, s_cbi, ncb);
+        s_code[i][c] = (uint8_t)code;
+        // an entry holds the dequantized value at its position (as the emit kernel's)
+        if (out)
+          n = dequant_ref(s_cb[code], n, KIND == 0 ? ks : s_vs[i], KIND == 0 ? kz : s_vz[i]);
       }
       nval[i] = n;
       if (out) omask |= 1u << i;
@@ -356,7 +360,7 @@ extern "C" int kvq_append_values(const void* v_new, int64_t B, int64_t S_new, in
   const size_t smem = C_full * sizeof(uint32_t);
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(value_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  value_plan_kernel<<<(unsigned)(B * S_new), 256, smem, st>>>(
+  value_plan_kernel<<<(unsigned)(B * S_new), plan_threads(C_full), smem, st>>>(
       (const __half*)v_new, B, S_new, C_full, 0, kv, v_scale + T_old, v_zero + T_old, ld_stats,
       sel);
   AppendArgs aa{};

@@ -97,8 +97,22 @@ struct PairLutHiLo {
   }
 };
 
+// An outlier entry's value: the reference's fp16 dequantized key / value at
+// its position (see outlier_entry). The decode kernels add (value - dense) *
+// coefficient, dense = cb[c0] * s + z being what the code tiles hold there.
 __device__ __forceinline__ float entry_value(uint32_t ent) {
   return __half2float(__ushort_as_half((unsigned short)(ent >> 16)));
+}
+
+// cb[c0], c0 = the code of a dense 0 (the code stored at outlier positions):
+// first minimum of |cb[k]| (kvquant_ops.cu:141-148 with v = 0).
+__device__ __forceinline__ float dense_zero_value(const float* cb, int n) {
+  float best = cb[0], bd = fabsf(cb[0]);
+  for (int k = 1; k < n; ++k) {
+    const float d = fabsf(cb[k]);
+    if (d < bd) { bd = d; best = cb[k]; }
+  }
+  return best;
 }
 
 // ---------------------------------------------------------------------------
@@ -168,18 +182,24 @@ struct LaneSlab {
 // ===========================================================================
 // Key kernel (tensor cores as the dot-product engine).
 //
-// Per 16-token block, pair block kb (4 RoPE pairs) and query head, one
-// m16n8k16 MMA computes, for the 16 tokens,
+// Per 16-token block, pair block kb (4 RoPE pairs) and query head, two
+// m16n8k16 MMAs compute, for the 16 tokens,
 //   X_p = L1 P1 + L2 P2 + OX   (columns 0..3, pairs 4kb..4kb+3)
 //   Y_p = L1 Q1 + L2 Q2 + OY   (columns 4..7)
-// with A columns 0..7 = the fp16 code values straight from the LUT (rows =
-// tokens, the two halves of each pair), B rows 0..7 = the block-diagonal
-// per-head constants, and the zero-point terms OX / OY entering as A columns
-// 8, 9 = 256 times B rows 8, 9 = the terms / 256 split into fp16 high and low
-// parts (exact to ~2^-22 relative), so the MMA needs no accumulator input.
+// Code values L and constants P, Q are split into fp16 high and low parts
+// (L = Lh + Ll, P = Ph + Pl to ~2^-22 relative): per-channel calibration puts
+// s * cb close to -z for most entries, so s * cb and the zero point cancel and
+// a single fp16 rounding of either would be amplified many times over the
+// dequantized key's own fp16 rounding. The first MMA takes A columns 0..7 =
+// Lh (rows = tokens, the two halves of each pair) twice against B rows 0..7 =
+// Ph, Qh (block-diagonal per head) and rows 8..15 = Pl, Ql; the second takes
+// A columns 0..7 = Ll against Ph, Qh plus the zero-point terms OX / OY as A
+// columns 8, 9 = 256 times B rows 8, 9 = the terms / 256 split into fp16 high
+// and low parts. Ll * (Pl, Ql) (~2^-22) is dropped.
 // The epilogue adds cos * X + sin * Y in fp32 with the token's exact-angle
-// cos/sin held in registers. Outliers add o * (cos P + sin Q) per entry with exact
-// trig; a block's entries (ordered by token) are summed per token with a warp
+// cos/sin held in registers. Outliers add (d - dense) (cos qa + sin qb) / sigma
+// per entry with exact trig (d = the entry's dequantized key, dense = the
+// MMA's cb[c0] s + z there); a block's entries (ordered by token) are summed per token with a warp
 // segmented scan, so every score has exactly one writer and no shared-memory
 // float atomics are needed.
 //
@@ -216,7 +236,8 @@ constexpr int kKeyTokens = kKeyTiles * kTileTokens;  // 256
 constexpr int kKeyRows = 2 * kKeyTiles;              // CSR rows per unit and item
 constexpr int kMaxSlots = 32;                        // query heads per group
 constexpr int kKeyStages = 3;                        // units in flight per thread
-constexpr int kBRow = 9;  // B words per (slot, kb): half2(P) x4, half2(Q) x4, zero
+constexpr int kBRow = 9;  // B words per (slot, kb): half2(P) x4, half2(Q) x4, zero (high
+                          // parts; the low parts follow at the same offset in their own table)
 constexpr int kZRow = 8;  // zero-point words per (slot, kb): half2(hi, lo) of column n's term / 256
 constexpr uint32_t kA256 = 0x5C005C00u;  // half2(256, 256)
 
@@ -227,14 +248,17 @@ constexpr uint32_t kA256 = 0x5C005C00u;  // half2(256, 256)
 // slab and one entry).
 template <int BITS>
 struct KeySmem {
-  static constexpr int kLut = PairLut<BITS>::kBytes;
+  static constexpr int kLut = PairLutHiLo<BITS>::kBytes;
   static constexpr int kZ = kLut;
   static constexpr int kB = kZ + kMaxSlots * 16 * kZRow * 4;
-  static constexpr int kSc = kB + kMaxSlots * 16 * kBRow * 4;
+  static constexpr int kBL = kB + kMaxSlots * 16 * kBRow * 4;  // low parts of the B words
+  static constexpr int kSc = kBL + kMaxSlots * 16 * kBRow * 4;
   static constexpr int kSigma = kSc + kMaxSlots * kKeyTokens * 4;
   static constexpr int kInv = kSigma + kMaxSlots * 4;
   static constexpr int kPtr = kInv + kPairs * 4;
-  static constexpr int kRing = (kPtr + kMaxSlots * (kKeyRows + 1) * 4 + 15) / 16 * 16;
+  static constexpr int kQh = kPtr + kMaxSlots * (kKeyRows + 1) * 4;  // [slots][128] fp16 query
+  static constexpr int kISig = kQh + kMaxSlots * kHeadDim * 2;        // [slots] 1 / sigma
+  static constexpr int kRing = (kISig + kMaxSlots * 4 + 15) / 16 * 16;
   static constexpr int kStage = kKeyThreads * (16 + 16 + 4);
   static constexpr int kBytes = kRing + kKeyStages * kStage;
   static_assert(kBytes <= 232448, "key kernel shared memory");
@@ -284,6 +308,7 @@ __device__ void key_build_tables(const KeyArgs& a, uint8_t* smem, int u0, int nu
   float* sigma = reinterpret_cast<float*>(smem + L::kSigma);
   uint32_t* zt = reinterpret_cast<uint32_t*>(smem + L::kZ);
   uint32_t* bt = reinterpret_cast<uint32_t*>(smem + L::kB);
+  uint32_t* btl = reinterpret_cast<uint32_t*>(smem + L::kBL);
   const int64_t HG = a.H * G;
   for (int s = threadIdx.x; s < kMaxSlots; s += blockDim.x) sigma[s] = 0.f;
   __syncthreads();
@@ -317,19 +342,34 @@ __device__ void key_build_tables(const KeyArgs& a, uint8_t* smem, int u0, int nu
       zt[(s * 16 + kb) * kZRow + j] = (uint32_t)__half_as_ushort(hi) | ((uint32_t)__half_as_ushort(lo) << 16);
     } else {      // B word jj: half2(P1, P2) of pair 4kb+jj (jj < 4), half2(Q1, Q2) of 4kb+jj-4
       const int jj = j - kZRow;
-      uint32_t w = 0u;
+      uint32_t w = 0u, wl = 0u;
       if (jj < 8) {
         const int p = 4 * kb + (jj & 3);
         const float q1 = __half2float(qv[p]), q2 = __half2float(qv[p + 64]);
         const float s1 = scl[p], s2 = scl[p + 64];
-        w = jj < 4 ? half2_bits(s1 * q1 * inv, s2 * q2 * inv)
-                   : half2_bits(s1 * q2 * inv, -s2 * q1 * inv);
+        const float v1 = jj < 4 ? s1 * q1 * inv : s1 * q2 * inv;
+        const float v2 = jj < 4 ? s2 * q2 * inv : -s2 * q1 * inv;
+        const __half h1 = __float2half_rn(v1), h2 = __float2half_rn(v2);
+        w = (uint32_t)__half_as_ushort(h1) | ((uint32_t)__half_as_ushort(h2) << 16);
+        wl = half2_bits(v1 - __half2float(h1), v2 - __half2float(h2));
       }
       bt[(s * 16 + kb) * kBRow + jj] = w;
+      btl[(s * 16 + kb) * kBRow + jj] = wl;
     }
   }
   __syncthreads();
-  if (threadIdx.x < kMaxSlots) sigma[threadIdx.x] = ldexpf(1.f, pow2_exponent(sigma[threadIdx.x]));
+  if (threadIdx.x < kMaxSlots) {
+    const int e = pow2_exponent(sigma[threadIdx.x]);
+    sigma[threadIdx.x] = ldexpf(1.f, e);
+    reinterpret_cast<float*>(smem + L::kISig)[threadIdx.x] = ldexpf(1.f, -e);
+  }
+  // the slots' queries (fp16) for the outlier pass
+  __half* qh = reinterpret_cast<__half*>(smem + L::kQh);
+  for (int idx = threadIdx.x; idx < nu * G * kHeadDim; idx += blockDim.x) {
+    const int sl = idx / kHeadDim;
+    const int64_t u = u0 + sl / G;
+    qh[idx] = a.q[((u / a.H) * HG + (u % a.H) * G + sl % G) * kHeadDim + idx % kHeadDim];
+  }
 }
 
 template <int BITS, int G>
@@ -344,17 +384,20 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
-  const uint32_t lane4 = (uint32_t)lane << 2;
+  const uint32_t lane8 = (uint32_t)lane << 3;
   // B word of this lane: column g of the block-diagonal B is X of pair g
   // (g < 4) or Y of pair g - 4; lane (g, c) holds rows 2c, 2c+1 of it.
   const int jl = (g == c) ? c : ((g == c + 4) ? 4 + c : 8);
   const uint8_t* bbase = smem + L::kB + jl * 4;
+  constexpr int kLoOff = L::kBL - L::kB;  // B low-part words sit this far after the high ones
   const uint8_t* zbase = smem + L::kZ + g * 4;  // zero-point word of column g
   // A columns 8, 9 = 256 (lanes c == 0 hold them), columns 10..15 = 0
   const uint32_t a23 = c == 0 ? kA256 : 0u;
   float* invf = reinterpret_cast<float*>(smem + L::kInv);
-  PairLut<BITS>::build(smem, a.cb);
+  __shared__ float s_cb0;
+  PairLutHiLo<BITS>::build(smem, a.cb);
   if (threadIdx.x < kPairs) invf[threadIdx.x] = a.inv_freq[threadIdx.x];
+  if (threadIdx.x == 0) s_cb0 = dense_zero_value(a.cb, 1 << BITS);
 
   const int nt = (int)((a.T + kTileTokens - 1) / kTileTokens);
   const int n_oct = (nt + kKeyTiles - 1) / kKeyTiles;
@@ -445,14 +488,18 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
       for (int gg = 0; gg < G; ++gg) accA[gg] = accB[gg] = 0ull;
 #pragma unroll
       for (int kb = 0; kb < 16; ++kb) {
-        const uint32_t a0 = *reinterpret_cast<const uint32_t*>(lut + sl.addr(2 * kb, lane4));
-        const uint32_t a1 = *reinterpret_cast<const uint32_t*>(lut + sl.addr(2 * kb + 1, lane4));
+        const uint2 e0 = *reinterpret_cast<const uint2*>(lut + sl.addr(2 * kb, lane8));
+        const uint2 e1 = *reinterpret_cast<const uint2*>(lut + sl.addr(2 * kb + 1, lane8));
 #pragma unroll
         for (int gg = 0; gg < G; ++gg) {
-          const uint32_t b0 = *reinterpret_cast<const uint32_t*>(brow + (gg * 16 + kb) * (kBRow * 4));
-          const uint32_t b1 = *reinterpret_cast<const uint32_t*>(zrow + (gg * 16 + kb) * (kZRow * 4));
+          const uint8_t* bw = brow + (gg * 16 + kb) * (kBRow * 4);
+          const uint32_t bh = *reinterpret_cast<const uint32_t*>(bw);
+          const uint32_t bl = *reinterpret_cast<const uint32_t*>(bw + kLoOff);
+          const uint32_t bz = *reinterpret_cast<const uint32_t*>(zrow + (gg * 16 + kb) * (kZRow * 4));
           float d[4];
-          mma_16816_zc(d, a0, a1, a23, a23, b0, b1);
+          mma_16816_zc(d, e0.x, e1.x, e0.x, e1.x, bh, bl);  // Lh (Ph, Qh) + Lh (Pl, Ql)
+          const uint32_t al[4] = {e0.y, e1.y, a23, a23};
+          mma_16816(d, al, bh, bz);                          // + Ll (Ph, Qh) + (OX, OY)
           ffma2(accA[gg], tw[kb][0], f2pack(d[0], d[1]));
           ffma2(accB[gg], tw[kb][1], f2pack(d[2], d[3]));
         }
@@ -469,9 +516,15 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
           sc[(slot0 + gg) * kKeyTokens + 16 * warp + g + 8] = y;
         }
       }
-      // Outliers of the block: o * (cos P + sin Q) of the channel's half of the pair.
+      // Outliers of the block: (d - dense) * (cos qa + sin qb) / sigma for the
+      // channel's half of the pair, d the entry's dequantized key, dense =
+      // cb[c0] s + z the MMA's term there, (qa, qb) = (q1, q2) for channels
+      // p < 64 and (q2, -q1) for p + 64.
       const int32_t e0 = uptr[ui * (kKeyRows + 1) + warp], e1 = uptr[ui * (kKeyRows + 1) + warp + 1];
       if (e0 < e1) {
+        const int64_t ho = (u0 + ui) % a.H;
+        const __half* qrow = reinterpret_cast<const __half*>(smem + L::kQh) + slot0 * kHeadDim;
+        const float* isig = reinterpret_cast<const float*>(smem + L::kISig) + slot0;
         __syncwarp();
         for (int32_t eb = e0; eb < e1; eb += 32) {
           const int32_t e = eb + lane;
@@ -481,7 +534,10 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
           const int ch = (int)(en & 127), p = ch & 63;
           float sv, cv;
           __sincosf(rope_reduce(tok0 + (tok & 15), invf[p]), &sv, &cv);
-          const float ov = valid ? entry_value(en) : 0.f;
+          const float ov =
+              valid ? entry_value(en) - fmaf(s_cb0, a.k_scale[ho * kHeadDim + ch],
+                                             a.k_zero[ho * kHeadDim + ch])
+                    : 0.f;
           // Entries are ordered by token: suffix sums within runs of equal
           // tokens; runs are almost always at most 4 long (two steps), longer
           // ones take the remaining steps.
@@ -493,14 +549,10 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
           const bool longer = __any_sync(0xffffffffu, head && lane + 4 < 32 && tn4 == tok);
 #pragma unroll
           for (int gg = 0; gg < G; ++gg) {
-            // the fp16 constants of the MMA (the reference rounds each
-            // dequantized key to fp16; fp16 constants track it more closely)
-            const uint32_t* bw = reinterpret_cast<const uint32_t*>(
-                smem + L::kB + ((slot0 + gg) * 16 + (p >> 2)) * (kBRow * 4));
-            const uint32_t pw = bw[p & 3], qw = bw[4 + (p & 3)];
-            const float P = ch >= 64 ? half_hi(pw) : half_lo(pw);
-            const float Q = ch >= 64 ? half_hi(qw) : half_lo(qw);
-            float v = ov * fmaf(cv, P, sv * Q);
+            const float q1 = __half2float(qrow[gg * kHeadDim + p]);
+            const float q2 = __half2float(qrow[gg * kHeadDim + p + 64]);
+            const float qa = ch >= 64 ? q2 : q1, qb = ch >= 64 ? -q1 : q2;
+            float v = ov * fmaf(cv, qa, sv * qb) * isig[gg];
             float o = __shfl_down_sync(0xffffffffu, v, 1);
             if (lane + 1 < 32 && tn1 == tok) v += o;
             o = __shfl_down_sync(0xffffffffu, v, 2);
@@ -802,6 +854,8 @@ __global__ void __launch_bounds__(kValThreads, 1)
   const uint32_t lane8 = (uint32_t)lane << 3;
   float* wacc = acc + (S::kWarpAcc ? warp * G * kHeadDim : 0);
   PairLutHiLo<BITS>::build(smem, a.cb);
+  __shared__ float s_cb0;
+  if (threadIdx.x == 0) s_cb0 = dense_zero_value(a.cb, 1 << BITS);
   for (int idx = threadIdx.x; idx < S::kAccFloats; idx += blockDim.x) acc[idx] = 0.f;
   if (threadIdx.x < G) zacc[threadIdx.x] = 0.f;
 
@@ -948,7 +1002,8 @@ __global__ void __launch_bounds__(kValThreads, 1)
         if (kSplitB) mma_16816(d2[kSplitB ? mb : 0], ah, l0, l1);
       }
     }
-    // Outliers: p s o into channel ch, fp32.
+    // Outliers: p (d - dense) into channel ch, fp32; d = the entry's
+    // dequantized value, dense = cb[c0] s + z the code tile's value there.
     const int k = warp + i * kValWarps;
     const int32_t e0 = tptr[k], e1 = tptr[k + 1];
     const uint32_t* fe = reinterpret_cast<const uint32_t*>(st + S::kE);
@@ -957,7 +1012,7 @@ __global__ void __launch_bounds__(kValThreads, 1)
       if (e < e1) {
         const uint32_t en = eb == e0 ? fe[lane] : __ldg(a.out_ent + e);
         const int tok = (int)((en >> 7) & 31), ch = (int)(en & 127);
-        const float so = sz[tok].x * entry_value(en);
+        const float so = entry_value(en) - fmaf(s_cb0, sz[tok].x, sz[tok].y);
 #pragma unroll
         for (int hd = 0; hd < G; ++hd) atomicAdd(wacc + hd * kHeadDim + ch, fp[hd * S::kPRow + tok] * so);
       }

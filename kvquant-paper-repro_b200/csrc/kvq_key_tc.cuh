@@ -9,7 +9,7 @@
 // with fp32 angles fl(t * inv_freq) (kvquant/kernels/rope_fused.py:6-12) and the
 // dequantization (cb[code] + o) * s + z of kvquant/quant/kv_quantizer.py:89.
 //
-// Work item = (group of up to 16 units, M-tile of 128 tokens = 4 code tiles).
+// Work item = (group of up to 8 units, M-tile of 128 tokens = 4 code tiles).
 // Per unit the CTA forms X and Y for all 128 tokens x 64 pairs as one
 // tcgen05.mma sequence, M = 128 tokens:
 //   * A (TMEM, 128 lanes x 64 columns) = the fp16 code values, written by the
@@ -27,12 +27,17 @@
 //     A block warp reads its 16 lanes back with tcgen05.ld.16x256b: lane
 //     4g + c receives X, Y of pairs 4kb + c for tokens g, g + 8 -- the pairs
 //     whose exact-angle cos/sin it holds in registers for the whole item.
-// Outliers add o * (cos P + sin Q) per entry (exact trig) into per-token
+// Outliers add (d - dense) (cos qa + sin qb) / sigma per entry (exact trig; d =
+// the entry's dequantized key, dense = the MMA's cb[c0] s + z) into per-token
 // 64-bit fixed-point shared-memory sums (integer atomics, no float CAS loop).
-// Pipeline: one copy/MMA warp streams each unit's 128-token code slab with a
-// bulk copy into a 3-stage ring and issues the MMAs into one of two TMEM
-// A/D buffers while the block warps dequantize the next unit and run the
-// rotation epilogue of the previous one.
+// Pipeline: a copy warp streams each unit's 128-token code slab with bulk
+// copies into a ring that fills the rest of shared memory (up to 24 stages);
+// an MMA warp issues the MMAs into one of two TMEM A buffers and three D
+// buffers; the block warps dequantize the next unit into A while running the
+// rotation epilogue of a unit two behind. Every mbarrier wait is bounded in
+// time, sets an abort flag and status bit 2, and the kernel frees its TMEM.
+// This kernel keeps single fp16 code values and constants (the mma.sync key
+// kernel splits both into high and low parts).
 #pragma once
 #include <atomic>
 #include <cstdlib>
@@ -64,8 +69,9 @@ struct KeyTcSmem {
   static constexpr int kBZero = kBMain + kTcMaxUnits * 4096;     // [unit][2048 B]
   static constexpr int kZeros = kBZero + kTcMaxUnits * 2048;     // 2048 B of zeros
   static constexpr int kAConst = kZeros + 2048;                  // 128 x 16 fp16: K 0, 1 = 256
-  static constexpr int kPQ = kAConst + 4096;                     // [unit][128] half2 (P, Q)
-  static constexpr int kSigma = kPQ + kTcMaxUnits * 512;         // [unit] float
+  static constexpr int kPQ = kAConst + 4096;                     // [unit][128] float2 (qa, qb) / sigma
+  static constexpr int kDense = kPQ + kTcMaxUnits * 1024;        // [unit][128] float cb[c0] s + z
+  static constexpr int kSigma = kDense + kTcMaxUnits * 512;      // [unit] float
   static constexpr int kSink = kSigma + kTcMaxUnits * 4;         // [unit] float, sink score / sigma
   static constexpr int kInv = kSink + kTcMaxUnits * 4;           // [64] float
   static constexpr int kSlots = kInv + kPairs * 4;               // [warp][16] u64 outlier sums
@@ -156,7 +162,9 @@ __device__ void key_tc_fill(const KeyArgs& a, uint8_t* smem, int64_t u0, int nu,
   using L = KeyTcSmem<BITS>;
   const int tid = (int)threadIdx.x - t0;
   const float* sigma = reinterpret_cast<const float*>(smem + L::kSigma);
-  uint32_t* pq = reinterpret_cast<uint32_t*>(smem + L::kPQ);
+  float2* pq = reinterpret_cast<float2*>(smem + L::kPQ);
+  float* dn = reinterpret_cast<float*>(smem + L::kDense);
+  const float cb0 = dense_zero_value(a.cb, 1 << BITS);
   for (int idx = tid; idx < nu * kPairs; idx += nthr) {
     const int ui = idx / kPairs, p = idx % kPairs;
     const int64_t u = u0 + ui;
@@ -188,9 +196,12 @@ __device__ void key_tc_fill(const KeyArgs& a, uint8_t* smem, int64_t u0, int nu,
       *reinterpret_cast<uint32_t*>(bz + (c >> 3) * 128 + (c & 7) * 16) =
           (uint32_t)__half_as_ushort(hi) | ((uint32_t)__half_as_ushort(lo) << 16);
     }
-    // outlier constants of channels p and p + 64: (P, Q) as the MMA's fp16 values
-    pq[ui * 128 + p] = (wp & 0xffffu) | (wq << 16);
-    pq[ui * 128 + p + 64] = (wp >> 16) | (wq & 0xffff0000u);
+    // outlier coefficients of channels p and p + 64 (cos, sin factors of the
+    // rotated query) and the code tiles' dense value cb[c0] s + z there
+    pq[ui * 128 + p] = make_float2(q1 * inv, q2 * inv);
+    pq[ui * 128 + p + 64] = make_float2(q2 * inv, -q1 * inv);
+    dn[ui * 128 + p] = fmaf(cb0, s1, z1);
+    dn[ui * 128 + p + 64] = fmaf(cb0, s2, z2);
   }
 }
 
@@ -358,7 +369,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) key_scores_tc_kernel(KeyArgs a)
     unsigned long long* slots = reinterpret_cast<unsigned long long*>(smem + L::kSlots) + warp * 16;
     const float* sigma = reinterpret_cast<const float*>(smem + L::kSigma);
     const float* sinks = reinterpret_cast<const float*>(smem + L::kSink);
-    const uint32_t* pqt = reinterpret_cast<const uint32_t*>(smem + L::kPQ);
+    const float2* pqt = reinterpret_cast<const float2*>(smem + L::kPQ);
+    const float* dnt = reinterpret_cast<const float*>(smem + L::kDense);
 
     uint64_t tw[16][2];
     int64_t tw_item = -1;
@@ -431,7 +443,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) key_scores_tc_kernel(KeyArgs a)
       x1 += __shfl_xor_sync(0xffffffffu, x1, 1);
       x0 += __shfl_xor_sync(0xffffffffu, x0, 2);
       x1 += __shfl_xor_sync(0xffffffffu, x1, 2);
-      // outliers of the block: o * (cos P + sin Q), summed per token in fixed point
+      // outliers of the block: (d - dense) * (cos qa + sin qb) / sigma, summed per
+      // token in fixed point
       if (pd.e0 < pd.e1) {
         if (lane < 16) slots[lane] = 0ull;
         __syncwarp();
@@ -443,8 +456,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) key_scores_tc_kernel(KeyArgs a)
             const int ch = (int)(en & 127), p = ch & 63;
             float sv, cv;
             __sincosf(rope_reduce(tok0 + tok, invf[p]), &sv, &cv);
-            const uint32_t w = pqt[pd.ui * 128 + ch];
-            const float v = entry_value(en) * fmaf(cv, half_lo(w), sv * half_hi(w));
+            const float2 co = pqt[pd.ui * 128 + ch];
+            const float v = (entry_value(en) - dnt[pd.ui * 128 + ch]) * fmaf(cv, co.x, sv * co.y);
             atomicAdd(slots + tok, (unsigned long long)__float2ll_rn(v * 4294967296.f));
           }
         }

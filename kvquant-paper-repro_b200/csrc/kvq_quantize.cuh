@@ -46,33 +46,52 @@ __device__ __forceinline__ float key_norm(const KeyShape& ks, int64_t b, int64_t
 
 constexpr int kHistCols = 32;  // columns per histogram CTA
 
+constexpr int kHistUnroll = 8;  // rows in flight per thread
+
 // Histogram of the radix digit at `shift` of |n| among entries matching the
-// prefix so far. grid = (CL/32 column groups, B, row blocks); block 256.
+// prefix so far. grid = (CL/32 column groups, B, row blocks); block 256: lane =
+// column (a warp reads 64 contiguous bytes of a row), warp w takes rows w,
+// w + 8, ... with 8 loads in flight. Rows of the shared histogram are padded
+// to 257 words so that lanes adding the same digit hit distinct banks.
 __global__ void __launch_bounds__(256) key_hist_kernel(KeyShape ks, int shift,
                                                        const Select* __restrict__ sel,
                                                        uint32_t* __restrict__ hist,
                                                        int64_t rows_per_block) {
-  __shared__ uint32_t h[kHistCols][256];
-  for (int i = threadIdx.x; i < kHistCols * 256; i += blockDim.x) (&h[0][0])[i] = 0;
+  __shared__ uint32_t h[kHistCols][257];
+  for (int i = threadIdx.x; i < kHistCols * 257; i += blockDim.x) (&h[0][0])[i] = 0;
   __syncthreads();
   const int64_t b = blockIdx.y;
   const int64_t cg = (int64_t)blockIdx.x * kHistCols;
   const int lc = threadIdx.x & 31;  // column inside the group
+  const int warp = threadIdx.x >> 5;
   const int64_t c = cg + lc;
   const int64_t col = b * ks.CL + c;
   const uint32_t mask_hi = shift >= 24 ? 0u : (0xffffffffu << (shift + 8));
   const uint32_t prefix = sel[col].thr & mask_hi;
+  const float z = ks.zero[ks.c0 + c], sc = ks.scale[ks.c0 + c];
   const int64_t n_rest = ks.S - ks.off;
   const int64_t r0 = (int64_t)blockIdx.z * rows_per_block;
   const int64_t r1 = min(n_rest, r0 + rows_per_block);
-  for (int64_t r = r0 + (threadIdx.x >> 5); r < r1; r += (blockDim.x >> 5)) {
-    const uint32_t ab = abs_bits(key_norm(ks, b, r + ks.off, c));
-    if ((ab & mask_hi) == prefix) atomicAdd(&h[lc][(ab >> shift) & 0xffu], 1u);
+  const __half* xcol = ks.k + (b * ks.S + ks.off) * ks.C_full + ks.c0 + c;
+  for (int64_t rb = r0 + warp; rb < r1; rb += 8 * kHistUnroll) {
+    __half xv[kHistUnroll];
+#pragma unroll
+    for (int i = 0; i < kHistUnroll; ++i) {
+      const int64_t r = rb + 8 * i;
+      xv[i] = r < r1 ? xcol[r * ks.C_full] : __float2half(0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < kHistUnroll; ++i) {
+      if (rb + 8 * i < r1) {
+        const uint32_t ab = abs_bits(normalize(__half2float(xv[i]), z, sc));
+        if ((ab & mask_hi) == prefix) atomicAdd(&h[lc][(ab >> shift) & 0xffu], 1u);
+      }
+    }
   }
   __syncthreads();
   for (int i = threadIdx.x; i < kHistCols * 256; i += blockDim.x) {
-    const uint32_t v = (&h[0][0])[i];
-    if (v) atomicAdd(&hist[(b * ks.CL + cg + i / 256) * 256 + (i & 255)], v);
+    const uint32_t v = h[i >> 8][i & 255];
+    if (v) atomicAdd(&hist[(b * ks.CL + cg + (i >> 8)) * 256 + (i & 255)], v);
   }
 }
 
@@ -97,175 +116,322 @@ __global__ void key_select_kernel(Select* __restrict__ sel, uint32_t* __restrict
   for (int i = 0; i < 256; ++i) hc[i] = 0;  // ready for the next pass
 }
 
-// Columns where only some of the entries equal to thr are taken: one warp per
-// such column walks the tokens in order and records the index of the last tie
-// taken. Other columns take every tie (tie_cut = INT_MAX).
-__global__ void key_ties_kernel(KeyShape ks, Select* __restrict__ sel, int64_t ncols) {
-  const int64_t col = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (col >= ncols) return;
-  Select s = sel[col];
-  if (s.kleft >= s.ties) {
-    if (lane == 0) { s.tie_cut = 0x7fffffff; sel[col] = s; }
+// Columns where only some of the entries equal to thr are taken
+// (kleft < ties): the tie cut is the token index of the kleft-th entry equal to
+// thr in token order; other columns take every tie (tie_cut = INT_MAX).
+// grid = (CL/32 column groups, B); block 256: lane = column, warp w takes rows
+// w*32 .. w*32+31 of each 256-row chunk and keeps a bit mask of its ties; the
+// per-column prefix over the warps finds the warp (and bit) holding the cut.
+// The CTA stops once every column of the group has its cut.
+__global__ void __launch_bounds__(256) key_ties_kernel(KeyShape ks, Select* __restrict__ sel) {
+  __shared__ int32_t s_cnt[8][32];
+  __shared__ int32_t s_need[32];   // ties still to pass, per column (0 = done)
+  __shared__ int32_t s_cut[32];
+  __shared__ int s_open;
+  const int64_t b = blockIdx.y;
+  const int64_t cg = (int64_t)blockIdx.x * kHistCols;
+  const int lc = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t c = cg + lc;
+  const int64_t col = b * ks.CL + c;
+  const Select s0 = sel[col];
+  if (warp == 0) {
+    const bool partial = s0.kleft < s0.ties;
+    s_need[lc] = partial ? s0.kleft : 0;
+    s_cut[lc] = partial ? -1 : 0x7fffffff;
+    const unsigned open = __ballot_sync(0xffffffffu, partial);
+    if (lc == 0) s_open = open != 0u;
+  }
+  __syncthreads();
+  const float z = ks.zero[ks.c0 + c], sc = ks.scale[ks.c0 + c];
+  const int64_t n_rest = ks.S - ks.off;
+  const __half* xcol = ks.k + (b * ks.S + ks.off) * ks.C_full + ks.c0 + c;
+  for (int64_t r0 = 0; r0 < n_rest && s_open; r0 += 256) {
+    uint32_t mask = 0u;
+    const int64_t rw = r0 + warp * 32;
+#pragma unroll 8
+    for (int i = 0; i < 32; ++i) {
+      const int64_t r = rw + i;
+      if (r < n_rest && abs_bits(normalize(__half2float(xcol[r * ks.C_full]), z, sc)) == s0.thr)
+        mask |= 1u << i;
+    }
+    s_cnt[warp][lc] = __popc(mask);
+    __syncthreads();
+    // the warp whose rows hold this column's cut, and the rank inside them
+    const int need = s_need[lc];
+    int before = 0, tot = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const int x = s_cnt[w][lc];
+      before += w < warp ? x : 0;
+      tot += x;
+    }
+    const int mine = s_cnt[warp][lc];
+    __syncthreads();  // every thread has read s_need and s_cnt
+    if (need > 0 && before < need && need <= before + mine) {
+      uint32_t m = mask;
+      for (int k = 1; k < need - before; ++k) m &= m - 1;
+      s_cut[lc] = (int32_t)(rw + __ffs(m) - 1);
+      s_need[lc] = 0;
+    } else if (warp == 7 && need > tot) {
+      s_need[lc] = need - tot;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      const unsigned open = __ballot_sync(0xffffffffu, s_need[lc] > 0);
+      if (lc == 0) s_open = open != 0u;
+    }
+    __syncthreads();
+  }
+  if (warp == 0) {
+    Select s = s0;
+    s.tie_cut = s_cut[lc];
+    sel[col] = s;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Values: one CTA per (b, token) row, thread i holding channels 16i..16i+15 in
+// registers: per-token min/max over all C_full channels, then the exact top-k
+// of |n| over those channels.
+// ---------------------------------------------------------------------------
+constexpr int kValRowMax = 16384;  // channels per value row
+constexpr int kPlanEPT = 16;       // channels per thread
+
+// Radix-select step shared by the plan kernels (warp 0): the digit holding the
+// kleft-th largest entry. Walking the bins from 255 down, the first d >= 1
+// whose suffix count reaches kleft (d = 0 if none). Lane L holds bins
+// 8L..8L+7; a suffix scan over the lanes finds the one lane where the count
+// crosses kleft, which then walks its own 8 bins.
+__device__ __forceinline__ void radix_pick(const uint32_t* hist, int32_t* sh_kleft,
+                                           int32_t* sh_digit, int32_t* sh_ties) {
+  const int L = threadIdx.x & 31;
+  const int32_t k0 = *sh_kleft;
+  int32_t h8[8], s8 = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    h8[j] = (int32_t)hist[8 * L + j];
+    s8 += h8[j];
+  }
+  int32_t suf = s8;  // bins 8L .. 255
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t v = __shfl_down_sync(0xffffffffu, suf, o);
+    if (L + o < 32) suf += v;
+  }
+  const int32_t above = suf - s8;  // bins 8L+8 .. 255
+  const bool mine = (k0 <= suf && (L == 31 || above < k0)) || (L == 0 && k0 > suf);
+  if (mine) {
+    int32_t k = k0 - above;
+    int d = 0;  // bin 0 is the fall-through: it is never tested
+#pragma unroll
+    for (int j = 7; j >= 0; --j) {
+      if (8 * L + j == 0) break;
+      if (k <= h8[j]) { d = 8 * L + j; break; }
+      k -= h8[j];
+    }
+    *sh_kleft = k;
+    *sh_digit = d;
+    *sh_ties = (int32_t)hist[d];
+  }
+}
+
+// Radix select of the kleft-th largest among n words u[0..n) that share
+// `prefix` (which has no bits below shift0 + 8), digits at shift0, shift0 - 8, ... 0; every
+// thread of the CTA takes part. Returns the threshold; sh_kleft / sh_ties end
+// as the remaining rank among the entries equal to it and their count.
+__device__ uint32_t radix_select_list(const uint32_t* u, int n, uint32_t prefix, int shift0,
+                                      uint32_t* hist, int32_t* sh_kleft, int32_t* sh_digit,
+                                      int32_t* sh_ties) {
+  for (int shift = shift0; shift >= 0; shift -= 8) {
+    const uint32_t mask_hi = shift >= 24 ? 0u : (0xffffffffu << (shift + 8));
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const uint32_t ab = u[i];
+      if ((ab & mask_hi) == prefix) atomicAdd(&hist[(ab >> shift) & 0xffu], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) radix_pick(hist, sh_kleft, sh_digit, sh_ties);
+    __syncthreads();
+    prefix |= (uint32_t)*sh_digit << shift;
+    __syncthreads();
+  }
+  return prefix;
+}
+
+// Block-wide reductions of the plan kernel (any blockDim multiple of 32).
+__device__ __forceinline__ float plan_block_max(float v, float* red) {
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  float r = -INFINITY;
+  for (int k = 0; k < (int)(blockDim.x >> 5); ++k) r = fmaxf(r, red[k]);
+  __syncthreads();
+  return r;
+}
+
+// Fast path: the threshold lies in one of the 8 highest occupied binades
+// (fp32 exponents) of |n|, found from per-thread counts; the entries of that
+// binade are compacted in channel order and radix-selected on their low 24
+// bits. Otherwise (or when the binade holds more than C_full / 2 entries) the
+// whole row is radix-selected from shared memory.
+__global__ void __launch_bounds__(1024) value_plan_kernel(
+    const __half* __restrict__ v, int64_t B, int64_t S, int64_t C_full, int64_t off,
+    int64_t kv, float* __restrict__ v_scale, float* __restrict__ v_zero, int64_t ld_stats,
+    Select* __restrict__ sel) {
+  extern __shared__ uint32_t vsm[];  // C_full words: the row's |n| bits, or a candidate list
+  __shared__ uint32_t hist[256];
+  __shared__ float red[32];
+  __shared__ int32_t s_bc[32][8];  // per-warp counts of the top binades
+  __shared__ int32_t sh_kleft, sh_digit, sh_ties, sh_cut, sh_bin, sh_m;
+  const int64_t row = blockIdx.x;  // over B * (S - off)
+  const int64_t n_rest = S - off;
+  const int64_t b = row / n_rest, t = row % n_rest + off;
+  const __half* x = v + (b * S + t) * C_full;
+  const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+  const int64_t c0 = (int64_t)kPlanEPT * tid;
+  uint4 raw[2];
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh)
+    raw[hh] = c0 + 8 * hh < C_full ? *reinterpret_cast<const uint4*>(x + c0 + 8 * hh)
+                                   : make_uint4(0u, 0u, 0u, 0u);
+  const __half* xh = reinterpret_cast<const __half*>(raw);
+  float mn = INFINITY, mx = -INFINITY;
+#pragma unroll
+  for (int e = 0; e < kPlanEPT; ++e) {
+    if (c0 + e < C_full) {
+      const float f = __half2float(xh[e]);
+      mn = fminf(mn, f);
+      mx = fmaxf(mx, f);
+    }
+  }
+  mn = -plan_block_max(-mn, red);
+  mx = plan_block_max(mx, red);
+  // kv_quantizer.py:106-107: scale = (max - min) / 2, zero = (max + min) / 2 (fp32).
+  const float scale = __fdiv_rn(__fsub_rn(mx, mn), 2.0f);
+  const float zero = __fdiv_rn(__fadd_rn(mx, mn), 2.0f);
+  if (tid == 0) {
+    v_scale[b * ld_stats + t] = scale;
+    v_zero[b * ld_stats + t] = zero;
+  }
+  uint32_t u[kPlanEPT];
+  int emax_t = -1;
+#pragma unroll
+  for (int e = 0; e < kPlanEPT; ++e) {
+    u[e] = c0 + e < C_full ? abs_bits(normalize(__half2float(xh[e]), zero, scale)) : 0u;
+    if (c0 + e < C_full) emax_t = max(emax_t, (int)(u[e] >> 23));
+  }
+  if (kv <= 0) {  // no outliers: a threshold nothing reaches
+    if (tid == 0) {
+      Select s;
+      s.thr = 0xffffffffu;
+      s.kleft = 0;
+      s.ties = 0;
+      s.tie_cut = 0x7fffffff;
+      sel[b * S + t] = s;
+    }
     return;
   }
-  const int64_t b = col / ks.CL, c = col % ks.CL;
-  const int64_t n_rest = ks.S - ks.off;
-  int32_t need = s.kleft;
-  int32_t cut = -1;
-  // 256 tokens per step, 8 consecutive ones per lane (8 loads in flight)
-  for (int64_t r0 = 0; r0 < n_rest && need > 0; r0 += 256) {
-    uint32_t m8 = 0;
+  const int emax = (int)plan_block_max((float)emax_t, red);
+  // counts of binades emax - j, j = 0..7 (8-bit fields; at most 16 per thread)
+  uint64_t pk = 0ull;
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const int64_t r = r0 + lane * 8 + q;
-      if (r < n_rest && abs_bits(key_norm(ks, b, r + ks.off, c)) == s.thr) m8 |= 1u << q;
+  for (int e = 0; e < kPlanEPT; ++e) {
+    const int j = emax - (int)(u[e] >> 23);
+    if (c0 + e < C_full && j < 8) pk += 1ull << (8 * j);
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int cj = __reduce_add_sync(0xffffffffu, (unsigned)((pk >> (8 * j)) & 0xffull));
+    if (lane == 0) s_bc[w][j] = cj;
+  }
+  __syncthreads();
+  const int cap = (int)(C_full / 2);
+  if (tid == 0) {
+    int cum = 0, bin = -1, m = 0;
+    for (int j = 0; j < 8 && bin < 0; ++j) {
+      int cj = 0;
+      for (int k = 0; k < (int)(blockDim.x >> 5); ++k) cj += s_bc[k][j];
+      if (cum + cj >= kv) { bin = j; m = cj; } else { cum += cj; }
     }
-    const int cnt = __popc(m8);
-    int incl = cnt;  // inclusive prefix of the tie counts in token order
+    if (bin >= 0 && m > cap) bin = -1;
+    sh_bin = bin;
+    sh_m = m;
+    sh_kleft = (int32_t)(bin >= 0 ? kv - cum : kv);  // the whole row from the top otherwise
+  }
+  __syncthreads();
+  const int bin = sh_bin;
+  uint32_t thr;
+  const uint32_t* list;
+  const uint32_t* chan = nullptr;  // channel of each list entry (fast path)
+  int n;
+  if (bin >= 0) {
+    // compact the binade's entries in channel order: u at vsm[0..m), channel at vsm[cap..)
+    const uint32_t eb = (uint32_t)(emax - bin);
+    int mc = 0;
+#pragma unroll
+    for (int e = 0; e < kPlanEPT; ++e) mc += (c0 + e < C_full && (u[e] >> 23) == eb) ? 1 : 0;
+    int incl = mc;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
       const int o = __shfl_up_sync(0xffffffffu, incl, d);
       if (lane >= d) incl += o;
     }
-    const int total = __shfl_sync(0xffffffffu, incl, 31);
-    if (total >= need) {
-      const int L = __ffs(__ballot_sync(0xffffffffu, incl >= need)) - 1;
-      const int before = __shfl_sync(0xffffffffu, incl - cnt, L);
-      uint32_t m = __shfl_sync(0xffffffffu, m8, L);
-      for (int i = 1; i < need - before; ++i) m &= m - 1;  // the (need - before)-th tie of lane L
-      cut = (int32_t)(r0 + L * 8 + (__ffs(m) - 1));
-      need = 0;
-    } else {
-      need -= total;
-    }
-  }
-  if (lane == 0) { s.tie_cut = cut; sel[col] = s; }
-}
-
-// ---------------------------------------------------------------------------
-// Values: one CTA per (b, token) row: per-token min/max over all C_full
-// channels, then radix select of the top-k |n| over those channels.
-// ---------------------------------------------------------------------------
-constexpr int kValRowMax = 16384;  // channels per value row held in smem
-
-__global__ void __launch_bounds__(256) value_plan_kernel(
-    const __half* __restrict__ v, int64_t B, int64_t S, int64_t C_full, int64_t off,
-    int64_t kv, float* __restrict__ v_scale, float* __restrict__ v_zero, int64_t ld_stats,
-    Select* __restrict__ sel) {
-  extern __shared__ uint32_t vsm[];  // C_full |n| bits
-  __shared__ uint32_t hist[256];
-  __shared__ float red_min[8], red_max[8];
-  __shared__ int32_t sh_kleft, sh_digit, sh_ties, sh_cut;
-  const int64_t row = blockIdx.x;  // over B * (S - off)
-  const int64_t n_rest = S - off;
-  const int64_t b = row / n_rest, t = row % n_rest + off;
-  const __half* x = v + (b * S + t) * C_full;
-  float mn = INFINITY, mx = -INFINITY;
-  for (int64_t c = threadIdx.x; c < C_full; c += blockDim.x) {
-    const float f = __half2float(x[c]);
-    mn = fminf(mn, f);
-    mx = fmaxf(mx, f);
-  }
-  mn = -warp_max(-mn);
-  mx = warp_max(mx);
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) { red_min[w] = mn; red_max[w] = mx; }
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    float a = lane < (int)(blockDim.x >> 5) ? red_min[lane] : INFINITY;
-    float m2 = lane < (int)(blockDim.x >> 5) ? red_max[lane] : -INFINITY;
-    a = -warp_max(-a);
-    m2 = warp_max(m2);
-    if (lane == 0) { red_min[0] = a; red_max[0] = m2; }
-  }
-  __syncthreads();
-  // kv_quantizer.py:106-107: scale = (max - min) / 2, zero = (max + min) / 2 (fp32).
-  const float scale = __fdiv_rn(__fsub_rn(red_max[0], red_min[0]), 2.0f);
-  const float zero = __fdiv_rn(__fadd_rn(red_max[0], red_min[0]), 2.0f);
-  if (threadIdx.x == 0) {
-    v_scale[b * ld_stats + t] = scale;
-    v_zero[b * ld_stats + t] = zero;
-  }
-  for (int64_t c = threadIdx.x; c < C_full; c += blockDim.x)
-    vsm[c] = abs_bits(normalize(__half2float(x[c]), zero, scale));
-  if (threadIdx.x == 0) sh_kleft = (int32_t)kv;
-  __syncthreads();
-  uint32_t prefix = 0;
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    const uint32_t mask_hi = shift >= 24 ? 0u : (0xffffffffu << (shift + 8));
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    if (lane == 31) s_bc[w][0] = incl;
     __syncthreads();
-    for (int64_t c = threadIdx.x; c < C_full; c += blockDim.x) {
-      const uint32_t ab = vsm[c];
-      if ((ab & mask_hi) == prefix) atomicAdd(&hist[(ab >> shift) & 0xffu], 1u);
-    }
-    __syncthreads();
-    // The digit holding the k-th largest entry: walking the bins from 255 down,
-    // the first d >= 1 whose suffix count reaches k (d = 0 if none). Warp 0:
-    // lane L holds bins 8L..8L+7; a suffix scan over the lanes finds the one
-    // lane where the count crosses k, which then walks its own 8 bins.
-    if (threadIdx.x < 32) {
-      const int L = threadIdx.x;
-      const int32_t k0 = sh_kleft;
-      int32_t h8[8], s8 = 0;
+    int pos = incl - mc;
+    for (int k = 0; k < w; ++k) pos += s_bc[k][0];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        h8[j] = (int32_t)hist[8 * L + j];
-        s8 += h8[j];
-      }
-      int32_t suf = s8;  // bins 8L .. 255
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int32_t v = __shfl_down_sync(0xffffffffu, suf, o);
-        if (L + o < 32) suf += v;
-      }
-      const int32_t above = suf - s8;  // bins 8L+8 .. 255
-      const bool mine = (k0 <= suf && (L == 31 || above < k0)) || (L == 0 && k0 > suf);
-      if (mine) {
-        int32_t k = k0 - above;
-        int d = 0;  // bin 0 is the fall-through: it is never tested
-#pragma unroll
-        for (int j = 7; j >= 0; --j) {
-          if (8 * L + j == 0) break;
-          if (k <= h8[j]) { d = 8 * L + j; break; }
-          k -= h8[j];
-        }
-        sh_kleft = k;
-        sh_digit = d;
-        sh_ties = (int32_t)hist[d];
+    for (int e = 0; e < kPlanEPT; ++e) {
+      if (c0 + e < C_full && (u[e] >> 23) == eb) {
+        vsm[pos] = u[e];
+        vsm[cap + pos] = (uint32_t)(c0 + e);
+        ++pos;
       }
     }
     __syncthreads();
-    prefix |= (uint32_t)sh_digit << shift;
+    list = vsm;
+    chan = vsm + cap;
+    n = sh_m;
+    // bits 31..24 are fixed by the binade; the first digit (bits 23..16) holds its
+    // exponent's low bit, the same for every entry of the list
+    thr = radix_select_list(list, n, (eb >> 1) << 24, 16, hist, &sh_kleft, &sh_digit, &sh_ties);
+  } else {
+#pragma unroll
+    for (int e = 0; e < kPlanEPT; ++e)
+      if (c0 + e < C_full) vsm[c0 + e] = u[e];
     __syncthreads();
+    list = vsm;
+    n = (int)C_full;
+    thr = radix_select_list(list, n, 0u, 24, hist, &sh_kleft, &sh_digit, &sh_ties);
   }
-  // Tie cut: the channel index of the kleft-th entry equal to the threshold.
-  if (threadIdx.x == 0) sh_cut = 0x7fffffff;
+  // Tie cut: the channel index of the kleft-th entry equal to the threshold
+  // (list order is channel order on both paths).
+  if (tid == 0) sh_cut = 0x7fffffff;
   __syncthreads();
-  if (sh_kleft < sh_ties) {
-    if (threadIdx.x < 32) {
-      int32_t need = sh_kleft;
-      for (int64_t c0 = 0; c0 < C_full && need > 0; c0 += 32) {
-        const int64_t c = c0 + lane;
-        const bool tie = c < C_full && vsm[c] == prefix;
-        const uint32_t bal = __ballot_sync(0xffffffffu, tie);
-        const int cnt = __popc(bal);
-        if (cnt >= need) {
-          uint32_t m = bal;
-          for (int i = 1; i < need; ++i) m &= m - 1;
-          if (lane == 0) sh_cut = (int32_t)(c0 + (__ffs(m) - 1));
-          need = 0;
-        } else {
-          need -= cnt;
-        }
+  if (sh_kleft < sh_ties && tid < 32) {
+    int32_t need = sh_kleft;
+    for (int i0 = 0; i0 < n && need > 0; i0 += 32) {
+      const int i = i0 + lane;
+      const bool tie = i < n && list[i] == thr;
+      const uint32_t bal = __ballot_sync(0xffffffffu, tie);
+      const int cnt = __popc(bal);
+      if (cnt >= need) {
+        uint32_t m = bal;
+        for (int k = 1; k < need; ++k) m &= m - 1;
+        const int at = i0 + (__ffs(m) - 1);
+        if (lane == 0) sh_cut = chan ? (int32_t)chan[at] : at;
+        need = 0;
+      } else {
+        need -= cnt;
       }
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     Select s;
-    s.thr = prefix;
+    s.thr = thr;
     s.kleft = sh_kleft;
     s.ties = sh_ties;
     s.tie_cut = sh_cut;
@@ -273,12 +439,93 @@ __global__ void __launch_bounds__(256) value_plan_kernel(
   }
 }
 
+// One packed outlier entry: position (token_in_tile << 7 | channel) in the low
+// 16 bits; in the high 16 bits the reference's dequantized value at that
+// position, fp16((cb[c0] + n) * s + z) (kv_quantizer.py:89,117; c0 = the code
+// of a dense 0, n the normalized outlier), which the decode kernels use in
+// place of the dequantized dense code there. An outlier key or value then
+// enters the attention exactly as the reference's fp16 K_hat / V_hat holds it
+// (for an unclamped input this is the input itself), where a rounded n would
+// be off by up to 2^-12 |n| s.
+__device__ __forceinline__ uint32_t outlier_entry(int token, int channel, float value) {
+  const __half h = __float2half_rn(value);
+  return (uint32_t)((token << 7) | channel) | ((uint32_t)__half_as_ushort(h) << 16);
+}
+
+// Nearest centroid of a clamped dense value v in [-1, 1] by exact switching
+// points. Sorted centroids sv[0..n-1] (original indices si); when every gap
+// between neighbours exceeds two ulps of (1 + max |c|), two distances
+// fl(|v - c|) to different centroids on the same side of v never round to the
+// same value, so the first-minimum rule of kvquant_ops.cu:141-148 picks one of
+// the two neighbours of v, and which one is monotone in v. tau[k] is then the
+// smallest fp32 v for which sorted position k + 1 wins over k (found by
+// bisection over the fp32 order), and the code is si[#(tau <= v)].
+struct NearestTable {
+  float tau[16];
+  uint8_t si[16];
+  int fast;  // 0: a gap is too small, use nearest_centroid_sorted
+};
+
+// Orders fp32 values as integers (monotone for all non-NaN floats).
+__device__ __forceinline__ int32_t f2ord(float f) {
+  const int32_t i = __float_as_int(f);
+  return i >= 0 ? i : (int32_t)(0x80000000u - (uint32_t)i);
+}
+__device__ __forceinline__ float ord2f(int32_t o) {
+  return __int_as_float(o >= 0 ? o : (int32_t)(0x80000000u - (uint32_t)o));
+}
+
+// Built by one warp from the sorted codebook (lane k bisects tau[k]).
+__device__ void build_nearest_table(const float* sv, const uint8_t* si, int n, NearestTable* t) {
+  const int k = threadIdx.x & 31;
+  float m = fmaxf(fabsf(sv[0]), fabsf(sv[n - 1])) + 1.f;
+  int ex;
+  frexpf(m, &ex);  // m < 2^ex: distances below m have ulp <= 2^(ex - 24)
+  const float ulp2 = ldexpf(1.f, ex - 23);
+  bool ok = true;
+  if (k < n - 1) ok = __fsub_rn(sv[k + 1], sv[k]) > ulp2;
+  const bool fast = __all_sync(0xffffffffu, ok);
+  if (k < n - 1 && fast) {
+    // predicate(v): position k + 1 chosen over k; false at sv[k], true at sv[k + 1]
+    const float lo_c = sv[k], hi_c = sv[k + 1];
+    const bool hi_first = si[k + 1] < si[k];  // wins ties
+    int64_t lo = f2ord(lo_c), hi = f2ord(hi_c);
+    while (hi - lo > 1) {
+      const int64_t mid = lo + (hi - lo) / 2;
+      const float v = ord2f((int32_t)mid);
+      const float dl = fabsf(__fsub_rn(v, lo_c)), dh = fabsf(__fsub_rn(v, hi_c));
+      const bool up = dh < dl || (dh == dl && hi_first);
+      if (up) hi = mid; else lo = mid;
+    }
+    t->tau[k] = ord2f((int32_t)hi);
+  }
+  if (k < n) t->si[k] = si[k];
+  if (k == 0) t->fast = fast ? 1 : 0;
+}
+
+template <int BITS>
+__device__ __forceinline__ int nearest_fast(float v, const NearestTable& t) {
+  int pos = 0;
+#pragma unroll
+  for (int step = 1 << (BITS - 1); step >= 1; step >>= 1)
+    if (t.tau[pos + step - 1] <= v) pos += step;
+  return t.si[pos];
+}
+
 // ---------------------------------------------------------------------------
-// Emit: one CTA (128 threads = 4 chunks x 32 tokens) per (b, tile, head).
-// KIND 0 = keys, 1 = values. COUNT_ONLY: write the outlier counts of the
-// tile's two 16-token blocks into out_ptr[2*(unit*nt_cap + tile) + blk + 1]
-// (prefix-summed afterwards into the CSR row pointer over (unit, tile, blk)).
+// Emit: one CTA of 256 threads per (kEmitTiles tiles, b, head). KIND 0 = keys,
+// 1 = values. Per 16-token block, thread (r, j) = (tid >> 4, tid & 15) takes
+// channels 8j..8j+7 of token r with one 16-byte load, so thread order is
+// (token, channel) order: a block-wide exclusive scan of the threads' outlier
+// counts gives every entry its place in the CSR row. COUNT_ONLY writes the
+// block's count into out_ptr[2*(unit*nt_cap + tile) + blk + 1] (prefix-summed
+// afterwards into the row pointer over (unit, tile, blk)). Codes go to a
+// shared (token, channel) byte tile, from which 128 threads pack the two
+// blocks' lane slabs in the decode kernels' fragment-native order.
 // ---------------------------------------------------------------------------
+constexpr int kEmitThreads = 256;
+constexpr int kEmitTiles = 4;
+
 struct EmitArgs {
   const __half* x;
   int64_t B, S, C_full, h0, H, off;
@@ -299,183 +546,217 @@ struct EmitArgs {
   __half* dequant_out;  // [B, S, H*128] or null
 };
 
-// One packed outlier entry: position (token_in_tile << 7 | channel) in the low
-// 16 bits, the fp16 normalized value in the high 16 bits.
-__device__ __forceinline__ uint32_t outlier_entry(int token, int channel, float value) {
-  const __half h = __float2half_rn(value);
-  return (uint32_t)((token << 7) | channel) | ((uint32_t)__half_as_ushort(h) << 16);
+// Inclusive scan of v over the CTA's 256 threads; also returns the total.
+__device__ __forceinline__ int emit_block_scan(int v, int* sh, int& total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int o = __shfl_up_sync(0xffffffffu, v, d);
+    if (lane >= d) v += o;
+  }
+  if (lane == 31) sh[w] = v;
+  __syncthreads();
+  int base = 0;
+  total = 0;
+#pragma unroll
+  for (int k = 0; k < kEmitThreads / 32; ++k) {
+    const int x = sh[k];
+    base += k < w ? x : 0;
+    total += x;
+  }
+  __syncthreads();  // sh is reused by the next scan
+  return base + v;
 }
 
-// One CTA of 128 threads per (tile, b, head); thread c owns channel c of the
-// head and walks the tile's 32 tokens, so every shared-memory access of a
-// warp is to consecutive channels. The tile's fp16 block (32 x 128) is staged
-// once with coalesced 16-byte loads; a key channel's zero / scale / selection
-// live in registers, a value token's in shared memory.
-template <int KIND, bool COUNT_ONLY>
-__global__ void __launch_bounds__(128) emit_kernel(EmitArgs a) {
-  __shared__ __align__(16) __half xs[kTileTokens][kHeadDim];  // the tile's inputs
-  __shared__ int32_t cnt[kTileTokens][8];  // outliers per (token, 16-channel group)
-  __shared__ float s_cb[16], s_cbs[16];  // codebook, and sorted ascending
-  __shared__ uint8_t s_cbi[16];          // original index of each sorted entry
-  __shared__ uint8_t s_code[kTileTokens][kHeadDim];  // codes of the tile (token, channel)
-  __shared__ float s_vs[kTileTokens], s_vz[kTileTokens];  // values: per-token scale / zero
-  __shared__ Select s_rs[kTileTokens];                   // values: per-token selection
-  const int64_t b = blockIdx.y;
-  const int64_t tile = blockIdx.x;
-  const int64_t h = blockIdx.z;  // local head
-  const int c = threadIdx.x;     // channel within the head
-  const int lane = c & 31, w = c >> 5;
+template <int KIND, bool COUNT_ONLY, int BITS>
+__global__ void __launch_bounds__(kEmitThreads) emit_kernel(EmitArgs a) {
+  __shared__ __align__(16) uint8_t s_code[kTileTokens][kHeadDim];  // codes of the tile
+  __shared__ float s_cb[16], s_cbs[16];
+  __shared__ uint8_t s_cbi[16];
+  __shared__ NearestTable s_nt;
+  __shared__ int s_scan[kEmitThreads / 32];
+  const int64_t b = blockIdx.y, h = blockIdx.z;
+  const int tid = threadIdx.x, r = tid >> 4, j = tid & 15;
   const int64_t unit = b * a.H + h;
-  const int ncb = 1 << a.bits;
   const int64_t CL = a.H * kHeadDim;
-  const int64_t cfull = (a.h0 + h) * kHeadDim + c;
-  const int64_t t0 = tile * kTileTokens;
-  if (!COUNT_ONLY && c == 0) {
-    for (int k = 0; k < ncb; ++k) s_cb[k] = a.cb[k];
-    sort_codebook(s_cb, ncb, s_cbs, s_cbi);
+  const int c0 = 8 * j;                                   // first channel of this thread
+  const int64_t cfull0 = (a.h0 + h) * kHeadDim + c0;     // ... in the full row
+  const int64_t nt = (a.S + kTileTokens - 1) / kTileTokens;
+  const bool with_out = a.nnz_cap >= 0;
+  constexpr int ncb = 1 << BITS;
+  if (!COUNT_ONLY) {
+    if (tid == 0) {
+      for (int k = 0; k < ncb; ++k) s_cb[k] = a.cb[k];
+      sort_codebook(s_cb, ncb, s_cbs, s_cbi);
+    }
+    __syncthreads();
+    if (tid < 32) build_nearest_table(s_cbs, s_cbi, ncb, &s_nt);
   }
-  // stage x[t0 .. t0+31][head channels] (rows beyond S read as 0)
-  for (int k = c; k < kTileTokens * (kHeadDim / 8); k += 128) {
-    const int i = k >> 4, ch8 = (k & 15) * 8;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (t0 + i < a.S)
-      v = *reinterpret_cast<const uint4*>(a.x + (b * a.S + t0 + i) * a.C_full + (a.h0 + h) * kHeadDim + ch8);
-    *reinterpret_cast<uint4*>(&xs[i][ch8]) = v;
-  }
-  float kz = 0.f, ks = 0.f;
-  Select cs{};
+  // keys: this thread's 8 channels' zero, scale and selection (threshold, tie cut)
+  float kz[8], ks[8];
+  Select kc[8];
   if (KIND == 0) {
-    kz = a.k_zero[cfull];
-    ks = a.k_scale[cfull];
-    cs = a.sel[b * CL + h * kHeadDim + c];
-  } else if (c < kTileTokens) {
-    const int64_t t = t0 + c;
-    const bool live = t < a.S && !(a.off == 1 && t == 0);
-    s_vs[c] = live ? a.v_scale[b * a.ld_stats + t] : 0.f;
-    s_vz[c] = live ? a.v_zero[b * a.ld_stats + t] : 0.f;
-    if (live) s_rs[c] = a.sel[b * a.S + t];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      kz[e] = a.k_zero[cfull0 + e];
+      ks[e] = a.k_scale[cfull0 + e];
+      kc[e] = Select{};
+      if (with_out) {
+        const Select* sp = a.sel + b * CL + h * kHeadDim + c0 + e;
+        kc[e].thr = sp->thr;
+        kc[e].tie_cut = sp->tie_cut;
+      }
+    }
   }
   __syncthreads();
+  const bool fast = COUNT_ONLY ? true : s_nt.fast != 0;
 
-  uint32_t omask = 0;  // outlier flag per token i
-  float nval[kTileTokens];
+  // this thread's 16-byte input chunk of token r of block blk of a tile
+  auto load = [&](int64_t tile, int blk) {
+    const int64_t t = tile * kTileTokens + 16 * blk + r;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (t < a.S) v = *reinterpret_cast<const uint4*>(a.x + (b * a.S + t) * a.C_full + cfull0);
+    return v;
+  };
+  const int64_t tile_begin = (int64_t)blockIdx.x * kEmitTiles;
+  const int64_t tile_end = min(nt, tile_begin + kEmitTiles);
+  uint4 nx0 = load(tile_begin, 0), nx1 = load(tile_begin, 1);  // one tile ahead
+  for (int64_t tile = tile_begin; tile < tile_end; ++tile) {
+    const uint4 cur[2] = {nx0, nx1};
+    if (tile + 1 < tile_end) {
+      nx0 = load(tile + 1, 0);
+      nx1 = load(tile + 1, 1);
+    }
 #pragma unroll
-  for (int i = 0; i < kTileTokens; ++i) {
-    const int64_t t = t0 + i;
-    const bool is_sink = a.off == 1 && t == 0;
-    const bool live = t < a.S && !is_sink;
-    float n = 0.f;
-    int code = 0;
-    bool out = false;
-    if (live) {
-      const float xv = __half2float(xs[i][c]);
-      if (KIND == 0) {
-        n = normalize(xv, kz, ks);
-        out = a.nnz_cap >= 0 && selected(abs_bits(n), (int32_t)(t - a.off), cs);
-      } else {
-        n = normalize(xv, s_vz[i], s_vs[i]);
-        out = a.nnz_cap >= 0 && selected(abs_bits(n), (int32_t)cfull, s_rs[i]);
+    for (int blk = 0; blk < 2; ++blk) {
+      const int ti = 16 * blk + r;  // token within the tile
+      const int64_t t = tile * kTileTokens + ti;
+      const bool in = t < a.S;
+      const bool is_sink = a.off == 1 && t == 0;
+      const bool live = in && !is_sink;
+      const uint4 raw = cur[blk];
+      float vz = 0.f, vs = 0.f;
+      Select vc{};
+      if (KIND == 1 && live) {
+        vs = a.v_scale[b * a.ld_stats + t];
+        vz = a.v_zero[b * a.ld_stats + t];
+        if (with_out) {
+          const Select* sp = a.sel + b * a.S + t;
+          vc.thr = sp->thr;
+          vc.tie_cut = sp->tie_cut;
+        }
+      }
+      const __half* xh = reinterpret_cast<const __half*>(&raw);
+      float nval[8];
+      uint32_t m8 = 0u;
+      uint32_t code_lo = 0u, code_hi = 0u;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float xv = __half2float(xh[e]);
+        const float n = KIND == 0 ? normalize(xv, kz[e], ks[e]) : normalize(xv, vz, vs);
+        nval[e] = n;
+        bool out = false;
+        if (live && with_out) {
+          out = KIND == 0 ? selected(abs_bits(n), (int32_t)(t - a.off), kc[e])
+                          : selected(abs_bits(n), (int32_t)(cfull0 + e), vc);
+        }
+        if (out) m8 |= 1u << e;
+        if (!COUNT_ONLY) {
+          int code = 0;
+          if (live) {
+            const float dense = out ? 0.f : fminf(fmaxf(n, -1.f), 1.f);
+            code = fast ? nearest_fast<BITS>(dense, s_nt)
+                        : nearest_centroid_sorted(dense, s_cbs, s_cbi, ncb);
+          }
+          if (e < 4) code_lo |= (uint32_t)code << (8 * e);
+          else code_hi |= (uint32_t)code << (8 * (e - 4));
+          if (out || (a.dequant_out && in)) {
+            const float dq = dequant_ref(s_cb[code], out ? n : 0.f, KIND == 0 ? ks[e] : vs,
+                                         KIND == 0 ? kz[e] : vz);
+            if (out) nval[e] = dq;  // the entry holds the dequantized value
+            if (a.dequant_out && in)
+              a.dequant_out[(b * a.S + t) * CL + h * kHeadDim + c0 + e] =
+                  is_sink ? xh[e] : __float2half_rn(dq);
+          }
+        }
       }
       if (!COUNT_ONLY) {
-        const float dense = out ? 0.f : fminf(fmaxf(n, -1.f), 1.f);
-        code = nearest_centroid_sorted(dense, s_cbs, s_cbi, ncb);
+        *reinterpret_cast<uint2*>(&s_code[ti][c0]) = make_uint2(code_lo, code_hi);
+        if (a.sink_out && is_sink)
+          *reinterpret_cast<uint4*>(a.sink_out + b * CL + h * kHeadDim + c0) = raw;
+      }
+      const int cnt = __popc(m8);
+      int total;
+      const int incl = emit_block_scan(cnt, s_scan, total);
+      const int64_t row = 2 * (unit * a.nt_cap + tile) + blk;
+      if (COUNT_ONLY) {
+        if (tid == 0) a.out_ptr[row + 1] = total;
+      } else if (m8) {
+        int64_t e_idx = (int64_t)a.out_ptr[row] + incl - cnt;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if ((m8 >> e) & 1u) {
+            if (e_idx < a.nnz_cap) a.out_ent[e_idx] = outlier_entry(ti, c0 + e, nval[e]);
+            ++e_idx;
+          }
+        }
       }
     }
-    nval[i] = n;
-    if (out) omask |= 1u << i;
-    const uint32_t bal = __ballot_sync(0xffffffffu, out);
-    if (lane == 0) {
-      cnt[i][2 * w] = __popc(bal & 0xffffu);  // channels 32w .. 32w+15
-      cnt[i][2 * w + 1] = __popc(bal >> 16);  // channels 32w+16 .. 32w+31
-    }
-    if (!COUNT_ONLY) {
-      s_code[i][c] = (uint8_t)code;
-      if (a.dequant_out && t < a.S) {
-        __half* drow = a.dequant_out + (b * a.S + t) * CL + h * kHeadDim;
-        drow[c] = is_sink ? xs[i][c]
-                          : __float2half_rn(dequant_ref(s_cb[code], out ? n : 0.f,
-                                                        KIND == 0 ? ks : s_vs[i],
-                                                        KIND == 0 ? kz : s_vz[i]));
+    if (COUNT_ONLY) continue;
+    __syncthreads();  // the tile's codes are in s_code
+    // Slab store: thread (slab, half) = (tid >> 1, tid & 1) packs slots
+    // 16*half .. 16*half+15 of the slab of (block, lane) = (slab >> 5, slab & 31).
+    if (tid < 128) {
+      const int slab = tid >> 1, half = tid & 1;
+      const int blk = slab >> 5, lane = slab & 31;
+      const int g = lane >> 2, cc = lane & 3;
+      uint32_t wd[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+      for (int qq = 0; qq < 16; ++qq) {
+        const int q = 16 * half + qq;
+        int ta, ca, tb, cb2;
+        if (KIND == 0) {  // keys: token 16*blk + g + 8*(q&1), RoPE pair 4*(q>>1) + cc
+          ta = tb = 16 * blk + g + 8 * (q & 1);
+          ca = 4 * (q >> 1) + cc;
+          cb2 = ca + 64;
+        } else {          // values: channel 16*(q>>2) + g + 8*(q&1), tokens (t, t+1)
+          ca = cb2 = 16 * (q >> 2) + g + 8 * (q & 1);
+          ta = 16 * blk + 2 * cc + 8 * ((q >> 1) & 1);
+          tb = ta + 1;
+        }
+        const uint32_t pair = (uint32_t)s_code[ta][ca] | ((uint32_t)s_code[tb][cb2] << BITS);
+        const int bit = 2 * BITS * qq;
+        wd[bit >> 5] |= pair << (bit & 31);
+        if ((bit & 31) + 2 * BITS > 32) wd[(bit >> 5) + 1] |= pair >> (32 - (bit & 31));
+      }
+      // The block is stored structure-of-arrays: bytes 0..15 of every lane's
+      // slab (512 B), then its remaining 8*BITS-16 bytes, so that the decode
+      // kernels' per-lane copies are coalesced. This half covers slab words
+      // half*BITS .. half*BITS + BITS - 1.
+      uint8_t* blk_base = a.codes + (unit * a.nt_cap + tile) * (int64_t)tile_bytes(BITS) +
+                          blk * (256 * BITS);
+#pragma unroll
+      for (int k = 0; k < BITS; ++k) {
+        const int wb = 4 * (half * BITS + k);  // byte offset in the slab
+        uint8_t* dst = wb < 16 ? blk_base + lane * 16 + wb
+                               : blk_base + 512 + lane * (8 * BITS - 16) + (wb - 16);
+        *reinterpret_cast<uint32_t*>(dst) = wd[k];
       }
     }
+    __syncthreads();  // s_code is rewritten by the next tile
   }
-  if (!COUNT_ONLY && a.sink_out && a.off == 1 && tile == 0) a.sink_out[b * CL + h * kHeadDim + c] = xs[0][c];
-  __syncthreads();
-  if (COUNT_ONLY) {
-    if (c < 2) {  // block c = tokens 16c .. 16c+15
-      int32_t tot = 0;
-      for (int r = 16 * 8 * c; r < 16 * 8 * (c + 1); ++r) tot += (&cnt[0][0])[r];
-      a.out_ptr[2 * (unit * a.nt_cap + tile) + c + 1] = tot;
-    }
-    return;
-  }
-  // Exclusive prefix over (token, group) in order -> entry offsets; thread c
-  // owns entries 2c, 2c+1 of the 256 (token, group) counts.
-  {
-    __shared__ int32_t s_wsum[4];
-    int32_t* flat = &cnt[0][0];
-    const int32_t v0 = flat[2 * c], v1 = flat[2 * c + 1];
-    int32_t incl = v0 + v1;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const int32_t o = __shfl_up_sync(0xffffffffu, incl, d);
-      if (lane >= d) incl += o;
-    }
-    if (lane == 31) s_wsum[w] = incl;
-    __syncthreads();
-    int32_t base_w = 0;
-    for (int k = 0; k < w; ++k) base_w += s_wsum[k];
-    const int32_t excl = base_w + incl - v0 - v1;
-    flat[2 * c] = excl;
-    flat[2 * c + 1] = excl + v0;
-  }
-  __syncthreads();
-  const int64_t base = a.out_ptr[2 * (unit * a.nt_cap + tile)];  // first entry of the tile
-  // Outlier entries in (token, channel) order: rank within the 16-channel group.
-  const uint32_t below = (1u << (lane & 15)) - 1u;
-#pragma unroll
-  for (int i = 0; i < kTileTokens; ++i) {
-    const bool out = (omask >> i) & 1u;
-    const uint32_t bal = __ballot_sync(0xffffffffu, out);
-    if (out) {
-      const uint32_t grp = lane < 16 ? (bal & 0xffffu) : (bal >> 16);
-      const int64_t e = base + cnt[i][c >> 4] + __popc(grp & below);
-      if (e < a.nnz_cap) a.out_ent[e] = outlier_entry(i, c, nval[i]);
-    }
-  }
-  // Slab store: threads 0..63 each pack the slab of (block, lane) = (tid >> 5,
-  // tid & 31) in the fragment-native order of the decode kernels.
-  if (c < 64) {
-    const int blk = c >> 5;
-    const int g = lane >> 2, cc = lane & 3;
-    uint32_t slab[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // up to 32 bytes (4-bit)
-#pragma unroll
-    for (int q = 0; q < 32; ++q) {
-      int ta, ca, tb, cb2;
-      if (KIND == 0) {  // keys: token 16*blk + g + 8*(q&1), RoPE pair 4*(q>>1) + cc
-        ta = tb = 16 * blk + g + 8 * (q & 1);
-        ca = 4 * (q >> 1) + cc;
-        cb2 = ca + 64;
-      } else {          // values: channel 16*(q>>2) + g + 8*(q&1), tokens (t, t+1)
-        ca = cb2 = 16 * (q >> 2) + g + 8 * (q & 1);
-        ta = 16 * blk + 2 * cc + 8 * ((q >> 1) & 1);
-        tb = ta + 1;
-      }
-      const uint32_t pair = (uint32_t)s_code[ta][ca] | ((uint32_t)s_code[tb][cb2] << a.bits);
-      const int bit = 2 * a.bits * q;
-      slab[bit >> 5] |= pair << (bit & 31);
-      if ((bit & 31) + 2 * a.bits > 32) slab[(bit >> 5) + 1] |= pair >> (32 - (bit & 31));
-    }
-    // The block is stored structure-of-arrays: bytes 0..15 of every lane's
-    // slab (512 B), then its remaining 8*bits-16 bytes, so that the decode
-    // kernels' per-lane copies are coalesced.
-    uint8_t* blk_base = a.codes + (unit * a.nt_cap + tile) * (int64_t)tile_bytes(a.bits) +
-                        blk * (256 * a.bits);
-    *reinterpret_cast<uint4*>(blk_base + lane * 16) = make_uint4(slab[0], slab[1], slab[2], slab[3]);
-    if (a.bits == 4)
-      *reinterpret_cast<uint4*>(blk_base + 512 + lane * 16) = make_uint4(slab[4], slab[5], slab[6], slab[7]);
-    else if (a.bits == 3)
-      *reinterpret_cast<uint2*>(blk_base + 512 + lane * 8) = make_uint2(slab[4], slab[5]);
+}
+
+// Clears code tiles nt .. nt_cap-1 of every unit (so stale codes never reach
+// the decode kernels). grid-stride over 16-byte words.
+__global__ void clear_tail_tiles_kernel(uint8_t* __restrict__ codes, int64_t units, int64_t nt,
+                                        int64_t nt_cap, int64_t tb) {
+  const int64_t per_unit = (nt_cap - nt) * tb / 16;
+  const int64_t total = units * per_unit;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t u = i / per_unit, w = i % per_unit;
+    reinterpret_cast<uint4*>(codes + (u * nt_cap + nt) * tb)[w] = make_uint4(0u, 0u, 0u, 0u);
   }
 }
 
@@ -595,6 +876,39 @@ inline size_t value_ws_bytes(int64_t B, int64_t S) {
 
 inline bool bits_ok(int bits) { return bits >= 2 && bits <= 4; }
 
+// Threads of value_plan_kernel for a row of C_full channels (16 per thread).
+inline int plan_threads(int64_t C_full) {
+  return (int)((C_full + kPlanEPT * 32 - 1) / (kPlanEPT * 32)) * 32;
+}
+
+inline dim3 emit_grid(int64_t S, int64_t B, int64_t n_heads) {
+  const int64_t nt = (S + kTileTokens - 1) / kTileTokens;
+  return dim3((unsigned)((nt + kEmitTiles - 1) / kEmitTiles), (unsigned)B, (unsigned)n_heads);
+}
+
+template <int KIND>
+static void launch_emit(const EmitArgs& ea, bool count_only, cudaStream_t st) {
+  const dim3 grid = emit_grid(ea.S, ea.B, ea.H);
+  if (count_only) {
+    emit_kernel<KIND, true, 2><<<grid, kEmitThreads, 0, st>>>(ea);
+    return;
+  }
+  switch (ea.bits) {
+    case 2: emit_kernel<KIND, false, 2><<<grid, kEmitThreads, 0, st>>>(ea); break;
+    case 3: emit_kernel<KIND, false, 3><<<grid, kEmitThreads, 0, st>>>(ea); break;
+    default: emit_kernel<KIND, false, 4><<<grid, kEmitThreads, 0, st>>>(ea); break;
+  }
+}
+
+// Clears the code tiles after the block's last tile, for every unit.
+static void clear_tail(uint8_t* codes, int64_t units, int64_t nt, int64_t nt_cap, int bits,
+                       cudaStream_t st) {
+  if (nt_cap <= nt) return;
+  const int64_t words = units * (nt_cap - nt) * tile_bytes(bits) / 16;
+  clear_tail_tiles_kernel<<<grid_for(words, 256), 256, 0, st>>>(codes, units, nt, nt_cap,
+                                                                tile_bytes(bits));
+}
+
 }  // namespace kvq
 
 extern "C" size_t kvq_quantize_keys_workspace(int64_t B, int64_t S, int64_t n_heads) {
@@ -674,7 +988,7 @@ extern "C" int kvq_quantize_keys_plan(const void* k, int64_t B, int64_t S, int64
       key_hist_kernel<<<hg, 256, 0, st>>>(ks, shift, sel, hist, rows_per_block);
       key_select_kernel<<<(unsigned)((ncols + 127) / 128), 128, 0, st>>>(sel, hist, ncols, shift);
     }
-    key_ties_kernel<<<(unsigned)((ncols + 7) / 8), 256, 0, st>>>(ks, sel, ncols);
+    key_ties_kernel<<<dim3((unsigned)(CL / kHistCols), (unsigned)B), 256, 0, st>>>(ks, sel);
   }
   // Outlier counts per (unit, tile, block), then the row pointer.
   const int64_t nrows = 2 * B * n_heads * nt_cap;  // (unit, tile, 16-token block)
@@ -683,9 +997,8 @@ extern "C" int kvq_quantize_keys_plan(const void* k, int64_t B, int64_t S, int64
   ea.x = ks.k; ea.B = B; ea.S = S; ea.C_full = C_full; ea.h0 = h0; ea.H = n_heads;
   ea.off = ks.off; ea.k_scale = scale; ea.k_zero = zero; ea.sel = sel; ea.bits = 2;
   ea.nt_cap = nt_cap; ea.out_ptr = out_ptr; ea.nnz_cap = outliers ? 0 : -1;
-  const int64_t nt = (S + kTileTokens - 1) / kTileTokens;
   ea.cb = nullptr;  // COUNT_ONLY never reads the codebook
-  emit_kernel<0, true><<<dim3((unsigned)nt, (unsigned)B, (unsigned)n_heads), 128, 0, st>>>(ea);
+  launch_emit<0>(ea, true, st);
   scan_counts(out_ptr, nrows, nnz_out, st);
   return check_launch("quantize_keys_plan");
 }
@@ -714,10 +1027,7 @@ extern "C" int kvq_quantize_keys_emit(const void* k, int64_t B, int64_t S, int64
   cudaStream_t st = as_stream(stream);
   const int64_t nt = (S + kTileTokens - 1) / kTileTokens;
   // Tiles beyond the block are cleared so stale codes never reach the decode kernels.
-  const int64_t tb = tile_bytes(bits);
-  if (nt_cap > nt)
-    for (int64_t u = 0; u < B * n_heads; ++u)
-      cudaMemsetAsync(codes + (u * nt_cap + nt) * tb, 0, (nt_cap - nt) * tb, st);
+  clear_tail(codes, B * n_heads, nt, nt_cap, bits, st);
   EmitArgs ea{};
   ea.x = (const __half*)k; ea.B = B; ea.S = S; ea.C_full = C_full; ea.h0 = h0;
   ea.H = n_heads; ea.off = (sink && S > 1) ? 1 : 0; ea.k_scale = scale; ea.k_zero = zero;
@@ -726,7 +1036,7 @@ extern "C" int kvq_quantize_keys_emit(const void* k, int64_t B, int64_t S, int64
   ea.out_ent = out_ent;
   ea.nnz_cap = outlier_ratio > 0 ? nnz_cap : -1;
   ea.sink_out = (__half*)sink_out; ea.dequant_out = (__half*)dequant_out;
-  emit_kernel<0, false><<<dim3((unsigned)nt, (unsigned)B, (unsigned)n_heads), 128, 0, st>>>(ea);
+  launch_emit<0>(ea, false, st);
   return check_launch("quantize_keys_emit");
 }
 
@@ -764,7 +1074,7 @@ extern "C" int kvq_quantize_values_plan(const void* v, int64_t B, int64_t S, int
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(value_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem);
-    value_plan_kernel<<<(unsigned)(B * n_rest), 256, smem, st>>>(
+    value_plan_kernel<<<(unsigned)(B * n_rest), plan_threads(C_full), smem, st>>>(
         (const __half*)v, B, S, C_full, off, kv, v_scale, v_zero, ld_stats, sel);
   }
   if (off) {  // the sink token carries no stats
@@ -780,8 +1090,7 @@ extern "C" int kvq_quantize_values_plan(const void* v, int64_t B, int64_t S, int
   ea.H = n_heads; ea.off = off; ea.v_scale = v_scale; ea.v_zero = v_zero;
   ea.ld_stats = ld_stats; ea.sel = sel; ea.cb = nullptr; ea.bits = 2; ea.nt_cap = nt_cap;
   ea.out_ptr = out_ptr; ea.nnz_cap = outliers ? 0 : -1;
-  const int64_t nt = (S + kTileTokens - 1) / kTileTokens;
-  emit_kernel<1, true><<<dim3((unsigned)nt, (unsigned)B, (unsigned)n_heads), 128, 0, st>>>(ea);
+  launch_emit<1>(ea, true, st);
   scan_counts(out_ptr, nrows, nnz_out, st);
   return check_launch("quantize_values_plan");
 }
@@ -810,10 +1119,7 @@ extern "C" int kvq_quantize_values_emit(const void* v, int64_t B, int64_t S, int
   }
   cudaStream_t st = as_stream(stream);
   const int64_t nt = (S + kTileTokens - 1) / kTileTokens;
-  const int64_t tb = tile_bytes(bits);
-  if (nt_cap > nt)
-    for (int64_t u = 0; u < B * n_heads; ++u)
-      cudaMemsetAsync(codes + (u * nt_cap + nt) * tb, 0, (nt_cap - nt) * tb, st);
+  clear_tail(codes, B * n_heads, nt, nt_cap, bits, st);
   EmitArgs ea{};
   ea.x = (const __half*)v; ea.B = B; ea.S = S; ea.C_full = C_full; ea.h0 = h0;
   ea.H = n_heads; ea.off = (sink && S > 1) ? 1 : 0; ea.v_scale = v_scale; ea.v_zero = v_zero;
@@ -822,6 +1128,6 @@ extern "C" int kvq_quantize_values_emit(const void* v, int64_t B, int64_t S, int
   ea.out_ptr = const_cast<int32_t*>(out_ptr); ea.out_ent = out_ent;
   ea.nnz_cap = outlier_ratio > 0 ? nnz_cap : -1;
   ea.sink_out = (__half*)sink_out; ea.dequant_out = (__half*)dequant_out;
-  emit_kernel<1, false><<<dim3((unsigned)nt, (unsigned)B, (unsigned)n_heads), 128, 0, st>>>(ea);
+  launch_emit<1>(ea, false, st);
   return check_launch("quantize_values_emit");
 }

@@ -160,6 +160,8 @@ __global__ void __launch_bounds__(kVtThreads, 1)
 
   // ---- set-up ----
   PairLutHiLo<BITS>::build(smem, a.cb);
+  __shared__ float s_cb0;
+  if (threadIdx.x == 0) s_cb0 = dense_zero_value(a.cb, 1 << BITS);
   {
     uint4* z = reinterpret_cast<uint4*>(smem + L::kB);
     for (int i = threadIdx.x; i < (kVtBufs * 8 * 512) / 16; i += blockDim.x) z[i] = make_uint4(0, 0, 0, 0);
@@ -356,17 +358,20 @@ __global__ void __launch_bounds__(kVtThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(a_full + buf);
-      // outliers of block wblk: p_t s_t o into (head, channel), fixed point
+      // outliers of block wblk: p_t (d - dense) into (head, channel), fixed point
       const uint32_t* sent = reinterpret_cast<const uint32_t*>(sd + L::kSdE);
       for (int32_t eb = e0; eb < e1; eb += 32) {
         const int32_t e = eb + lane;
         const int32_t rel = e - ebase;
         const uint32_t en = e < e1 ? (rel < kVtEnt ? sent[rel] : __ldg(a.out_ent + e)) : 0u;
         const int tok = (int)((en >> 7) & 15), chn = (int)(en & 127);
-        const float o = entry_value(en);
+        // the entry's dequantized value minus the code tile's cb[c0] s + z there
+        const float s_o = __shfl_sync(0xffffffffu, s_t, tok);
+        const float z_o = __shfl_sync(0xffffffffu, z_t, tok);
+        const float o = entry_value(en) - fmaf(s_cb0, s_o, z_o);
 #pragma unroll
         for (int hd = 0; hd < G; ++hd) {
-          const float w = __shfl_sync(0xffffffffu, ps[hd], tok);
+          const float w = __shfl_sync(0xffffffffu, p[hd], tok);
           if (e < e1)
             atomicAdd(acc + hd * 128 + chn, (unsigned long long)__float2ll_rn(w * o * fix));
         }

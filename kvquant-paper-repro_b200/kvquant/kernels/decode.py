@@ -111,7 +111,8 @@ def _quantize(kind: str, x: torch.Tensor, codebook: torch.Tensor, bits: int,
     packed = {
         "q_idx": codes,
         # one int32 per outlier: low half = (token_in_tile << 7) | channel, high
-        # half = fp16 value; the two halves are also exposed as strided views
+        # half = the fp16 dequantized value (cb[c0] + n) * s + z at that position
+        # (kv_quantizer.py:89,117); the two halves are also exposed as strided views
         "outlier_entries": ent,
         "outlier_values": pairs[:nnz, 1].view(torch.float16),
         "outlier_cols": pairs[:nnz, 0],

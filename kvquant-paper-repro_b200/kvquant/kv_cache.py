@@ -2,9 +2,10 @@
 
 Per-layer dict slots as in the reference (kv_cache.py:4-44), filled with the
 packed dicts that kvquant.kernels.quantize_keys / quantize_values return:
-q_idx (bit-packed codes in 32-token tiles), outlier_values (fp16),
-outlier_cols (int16 packed (token_in_tile, channel)), outlier_rowptr (int32
-per (head, tile)), scale and zero, plus the fp16 sink token. memory_bytes
+q_idx (bit-packed codes in 32-token tiles), outlier_values (fp16: the
+dequantized key / value at each outlier), outlier_cols (int16 packed
+(token_in_tile, channel)), outlier_rowptr (int32 per (head, tile, 16-token
+block)), scale and zero, plus the fp16 sink token. memory_bytes
 counts each tensor at its real element size (the reference counts int32
 columns as 2 bytes and fp32 scales as 2 bytes).
 """

@@ -547,8 +547,10 @@ def cache_from_reference_quant(kq: dict, vq: dict, k: np.ndarray, v: np.ndarray,
     """Expected packed cache for a prefill block, from quantize_k/quantize_v results.
 
     Token 0 is the fp16 sink (its code slots hold 0); tokens 1.. hold the
-    reference's centroid indices. Outlier values are the normalized raw
-    values (dense_sparse.py:31) rounded to fp16.
+    reference's centroid indices. An outlier entry holds the reference's fp16
+    dequantized value at its position (kv_quantizer.py:89,117: (cb[c0] + n) *
+    s + z with n the normalized outlier of dense_sparse.py:31 and c0 the code
+    of a dense 0), which a decoder uses in place of the dense code's value.
     """
     B, S, C = k.shape
     out = {}
@@ -559,7 +561,7 @@ def cache_from_reference_quant(kq: dict, vq: dict, k: np.ndarray, v: np.ndarray,
         off = 1 if qd["has_sink"] else 0
         idx[:, off:] = qd["idx"]
         mask[:, off:] = qd["mask"]
-        val[:, off:] = np.where(qd["mask"], qd["norm"], 0)
+        val[:, off:] = np.where(qd["mask"], qd["dequant"][:, off:].astype(F32), 0)
         iu = units_view(idx, n_kv_heads)
         mu = units_view(mask, n_kv_heads)
         vu = units_view(val, n_kv_heads)
@@ -577,23 +579,25 @@ def cache_from_reference_quant(kq: dict, vq: dict, k: np.ndarray, v: np.ndarray,
 def dequant_packed(codes, out_ent, out_ptr, scale, zero, codebook, bits: int,
                    kind: str, T: int, sink=None):
     """Packed cache of U units -> K_hat / V_hat [U, T, 128] fp16, the reference's
-    fake-quant dequantization (cb[q] + o) * s + z (kv_quantizer.py:89,117), with
-    the fp16 outlier values the cache stores. Keys: scale/zero [U, 128] per
-    channel; values: scale/zero [U, T] per token. sink: [U, 128] fp16 or None.
+    fake-quant dequantization cb[q] * s + z (kv_quantizer.py:89,117) at dense
+    positions and the entries' fp16 dequantized values at outliers. Keys:
+    scale/zero [U, 128] per channel; values: scale/zero [U, T] per token. sink:
+    [U, 128] fp16 or None.
     """
     U = codes.shape[0]
     idx = unpack_codes(codes, bits, kind, T)
     cb = np.asarray(codebook, F32)
     q = cb[idx]
     out_vals, out_pos = unpack_entries(out_ent)
-    o, _ = untile_outliers(out_vals, out_pos, out_ptr, U, T)
+    o, mask = untile_outliers(out_vals, out_pos, out_ptr, U, T)
     s = np.asarray(scale, F32)
     z = np.asarray(zero, F32)
     if kind == "k":
         s, z = s[:, None, :], z[:, None, :]
     else:
         s, z = s[:, :T, None], z[:, :T, None]
-    deq = ((((q + o).astype(F32)) * s).astype(F32) + z).astype(F16)
+    deq = ((((q + F32(0)).astype(F32)) * s).astype(F32) + z).astype(F16)
+    deq = np.where(mask, o.astype(F16), deq)
     if sink is not None:
         deq[:, 0, :] = np.asarray(sink, F16)
     return deq

@@ -83,7 +83,8 @@ def test_append_keys_threshold_parity(cuda, bits):
     exp = O.quantize_k_thresholds(k[:, T0:], cb, scale, zero, thr.cpu().numpy())
     e_idx = O.units_view(exp["idx"], H)
     e_mask = O.units_view(exp["mask"], H)
-    e_val = O.units_view(np.where(exp["mask"], exp["norm"], 0).astype(np.float16).astype(np.float32), H)
+    # an entry holds the dequantized key at its position
+    e_val = O.units_view(np.where(exp["mask"], exp["dequant"].astype(np.float32), 0), H)
     for g_, o_ in zip((idx, mask, vals), old):  # the prefill part is untouched
         np.testing.assert_array_equal(g_[:, :T0], o_)
     np.testing.assert_array_equal(idx[:, T0:], e_idx)
@@ -106,8 +107,7 @@ def test_append_keys_zero_thresholds_is_reference_one_token(cuda):
         np.testing.assert_array_equal(idx[:, a:a + 1], O.units_view(ref["idx"], pk["n_heads"]))
         assert mask[:, a].all()
         np.testing.assert_array_equal(
-            vals[:, a:a + 1], O.units_view(ref["norm"].astype(np.float16).astype(np.float32),
-                                           pk["n_heads"]))
+            vals[:, a:a + 1], O.units_view(ref["dequant"].astype(np.float32), pk["n_heads"]))
 
 
 def test_decode_after_appends(cuda):
