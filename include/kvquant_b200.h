@@ -80,6 +80,15 @@ int kvq_sparse_matvec_csr(const int32_t* row_ptr, const int32_t* col_idx, const 
                           const void* vec, void* out, int64_t R, int64_t nnz, int64_t vec_len,
                           void* stream);
 
+/* The normalization step of quantize_k / quantize_v (kvquant/quant/
+ * kv_quantizer.py:82,104): out = (x - zero) / (scale + 1e-8), each step an IEEE
+ * fp32 operation, computed as the quantize kernels compute it (from the
+ * correctly rounded reciprocal of the divisor with two corrections; results
+ * equal the IEEE quotient). x fp16 [rows, cols]; zero / scale fp32 [cols]
+ * (per_channel != 0) or [rows]; out fp32 [rows, cols]. */
+int kvq_normalize(const void* x, int64_t rows, int64_t cols, const float* zero,
+                  const float* scale, int per_channel, float* out, void* stream);
+
 /* Replaces lut_lookup (kvquant/kernels/csrc/kvquant_ops.cu:243-263):
  * nearest centroid (first minimum) of x fp32 [N] in codebook fp32 [lut_size];
  * idx_out int64 [N], dq_out fp32 [N]. */
@@ -89,16 +98,20 @@ int kvq_lut_lookup(const float* x, const float* codebook, int64_t lut_size, int6
 /* ---------------------------------------------------------------------------
  * Quantize-on-append (prefill block). Semantics of KVQuantizer.quantize_k /
  * quantize_v (kvquant/quant/kv_quantizer.py:72-122) with dense-and-sparse
- * outliers (kvquant/quant/dense_sparse.py:4-32): codes, outlier positions
- * and fp16 outlier values match the reference bit for bit (ties at the top-k
- * threshold: lower token / channel index wins).
+ * outliers (kvquant/quant/dense_sparse.py:4-32): codes and outlier positions
+ * match the reference bit for bit (ties at the top-k threshold: lower token /
+ * channel index wins); each outlier entry holds the reference's fp16
+ * dequantized value at its position, fp16((cb[c0] + n) * s + z).
  *
  * Input x [B, S, C_full] fp16 (the k_proj / v_proj output); the call handles
  * heads [h0, h0+n_heads). Token 0 becomes the fp16 sink when sink && S > 1.
  * Two phases: *_plan computes thresholds, per-(unit,tile) outlier counts,
  * out_ptr and the total nnz (device int64); *_emit writes the codes, outlier
  * entries, sink and (optionally) the fake-quant dequantized output
- * [B, S, n_heads*128] fp16 -- the reference's return value.
+ * [B, S, n_heads*128] fp16 -- the reference's return value. The workspace
+ * carries the plan's selections and outlier bounds to the emit call, which
+ * also writes its per-channel / per-token code bounds into it (so it is not
+ * read-only to *_emit despite the const).
  * ------------------------------------------------------------------------- */
 size_t kvq_quantize_keys_workspace(int64_t B, int64_t S, int64_t n_heads);
 int kvq_quantize_keys_plan(const void* k, int64_t B, int64_t S, int64_t C_full, int64_t h0,

@@ -48,6 +48,52 @@ __device__ __forceinline__ float normalize(float x, float zero, float scale) {
   return __fdiv_rn(__fsub_rn(x, zero), __fadd_rn(scale, 1e-8f));
 }
 
+// The same normalization for many x sharing (zero, scale), with the division
+// done from the correctly rounded reciprocal y = RN(1/b), b = scale + 1e-8:
+// q0 = RN(a y) is within 1.5 ulp of a/b, one correction q1 = RN(q0 + RN(a -
+// b q0) y) makes it faithful, and by Markstein's theorem (a faithful quotient
+// q and y within half an ulp of 1/b give RN(q + (a - b q) y) = RN(a/b), the
+// remainder a - b q being exact in an FMA) a second correction rounds it
+// correctly. Five FP instructions instead of a division. The theorem needs
+// every quantity to stay normal, which holds for fp16 inputs x when b is in
+// [2^-60, 2^30] and zero is 0 or of magnitude in [2^-60, 2^60] (then a =
+// x - zero is 0 or at least 2^-84 in magnitude, and a/b is 0 or between
+// 2^-114 and 2^77); `fast` is false otherwise and for infinite or NaN a,
+// where the IEEE division runs.
+struct Normalizer {
+  float z, b, y;
+  bool fast;
+  __device__ __forceinline__ void init(float zero, float scale) {
+    z = zero;
+    b = __fadd_rn(scale, 1e-8f);
+    y = __frcp_rn(b);
+    const float az = fabsf(zero);
+    fast = (az == 0.f || (az >= 0x1p-60f && az <= 0x1p60f)) && b >= 0x1p-60f && b <= 0x1p30f;
+  }
+  // a / b for a = x - zero, valid when `fast` holds and x is finite
+  __device__ __forceinline__ float quot(float x) const {
+    const float a = __fsub_rn(x, z);
+    float q = __fmul_rn(a, y);
+    float r = __fmaf_rn(-q, b, a);
+    q = __fmaf_rn(r, y, q);
+    r = __fmaf_rn(-q, b, a);
+    q = __fmaf_rn(r, y, q);
+    return a == 0.f ? a : q;  // the corrections turn -0 into +0; IEEE keeps the sign
+  }
+  __device__ __forceinline__ float operator()(float x) const {
+    if (!fast || !(fabsf(x) < INFINITY)) return __fdiv_rn(__fsub_rn(x, z), b);
+    return quot(x);
+  }
+};
+
+// True when all eight fp16 values of a 16-byte chunk are finite.
+__device__ __forceinline__ bool finite8(const uint4& v) {
+  auto ok = [](uint32_t w) {
+    return (w & 0x7C00u) != 0x7C00u && (w & 0x7C000000u) != 0x7C000000u;
+  };
+  return ok(v.x) && ok(v.y) && ok(v.z) && ok(v.w);
+}
+
 // First-minimum nearest centroid (kvquant/kernels/csrc/kvquant_ops.cu:141-148).
 __device__ __forceinline__ int nearest_centroid(float v, const float* cb, int n) {
   float best_d = fabsf(__fsub_rn(v, cb[0]));

@@ -236,8 +236,8 @@ constexpr int kKeyTokens = kKeyTiles * kTileTokens;  // 256
 constexpr int kKeyRows = 2 * kKeyTiles;              // CSR rows per unit and item
 constexpr int kMaxSlots = 32;                        // query heads per group
 constexpr int kKeyStages = 3;                        // units in flight per thread
-constexpr int kBRow = 9;  // B words per (slot, kb): half2(P) x4, half2(Q) x4, zero (high
-                          // parts; the low parts follow at the same offset in their own table)
+constexpr int kBRow = 9;  // B words per (slot, kb): half2(P) x4, half2(Q) x4, zero, each
+                          // as (high parts, low parts)
 constexpr int kZRow = 8;  // zero-point words per (slot, kb): half2(hi, lo) of column n's term / 256
 constexpr uint32_t kA256 = 0x5C005C00u;  // half2(256, 256)
 
@@ -250,9 +250,8 @@ template <int BITS>
 struct KeySmem {
   static constexpr int kLut = PairLutHiLo<BITS>::kBytes;
   static constexpr int kZ = kLut;
-  static constexpr int kB = kZ + kMaxSlots * 16 * kZRow * 4;
-  static constexpr int kBL = kB + kMaxSlots * 16 * kBRow * 4;  // low parts of the B words
-  static constexpr int kSc = kBL + kMaxSlots * 16 * kBRow * 4;
+  static constexpr int kB = kZ + kMaxSlots * 16 * kZRow * 4;  // uint2 (high, low) B words
+  static constexpr int kSc = kB + kMaxSlots * 16 * kBRow * 8;
   static constexpr int kSigma = kSc + kMaxSlots * kKeyTokens * 4;
   static constexpr int kInv = kSigma + kMaxSlots * 4;
   static constexpr int kPtr = kInv + kPairs * 4;
@@ -307,8 +306,7 @@ __device__ void key_build_tables(const KeyArgs& a, uint8_t* smem, int u0, int nu
   using L = KeySmem<BITS>;
   float* sigma = reinterpret_cast<float*>(smem + L::kSigma);
   uint32_t* zt = reinterpret_cast<uint32_t*>(smem + L::kZ);
-  uint32_t* bt = reinterpret_cast<uint32_t*>(smem + L::kB);
-  uint32_t* btl = reinterpret_cast<uint32_t*>(smem + L::kBL);
+  uint2* bt = reinterpret_cast<uint2*>(smem + L::kB);
   const int64_t HG = a.H * G;
   for (int s = threadIdx.x; s < kMaxSlots; s += blockDim.x) sigma[s] = 0.f;
   __syncthreads();
@@ -353,8 +351,7 @@ __device__ void key_build_tables(const KeyArgs& a, uint8_t* smem, int u0, int nu
         w = (uint32_t)__half_as_ushort(h1) | ((uint32_t)__half_as_ushort(h2) << 16);
         wl = half2_bits(v1 - __half2float(h1), v2 - __half2float(h2));
       }
-      bt[(s * 16 + kb) * kBRow + jj] = w;
-      btl[(s * 16 + kb) * kBRow + jj] = wl;
+      bt[(s * 16 + kb) * kBRow + jj] = make_uint2(w, wl);
     }
   }
   __syncthreads();
@@ -388,8 +385,7 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
   // B word of this lane: column g of the block-diagonal B is X of pair g
   // (g < 4) or Y of pair g - 4; lane (g, c) holds rows 2c, 2c+1 of it.
   const int jl = (g == c) ? c : ((g == c + 4) ? 4 + c : 8);
-  const uint8_t* bbase = smem + L::kB + jl * 4;
-  constexpr int kLoOff = L::kBL - L::kB;  // B low-part words sit this far after the high ones
+  const uint8_t* bbase = smem + L::kB + jl * 8;
   const uint8_t* zbase = smem + L::kZ + g * 4;  // zero-point word of column g
   // A columns 8, 9 = 256 (lanes c == 0 hold them), columns 10..15 = 0
   const uint32_t a23 = c == 0 ? kA256 : 0u;
@@ -480,7 +476,7 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
       sl.read(st + threadIdx.x * 16, st + kKeyThreads * 16 + threadIdx.x * 16);
       const uint32_t ent0 = *reinterpret_cast<const uint32_t*>(st + kKeyThreads * 32 + threadIdx.x * 4);
       const int slot0 = ui * G;
-      const uint8_t* brow = bbase + slot0 * (16 * kBRow * 4);
+      const uint8_t* brow = bbase + slot0 * (16 * kBRow * 8);
       const uint8_t* zrow = zbase + slot0 * (16 * kZRow * 4);
 
       uint64_t accA[G], accB[G];  // pairs of partial sums, token g / g + 8
@@ -492,9 +488,8 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
         const uint2 e1 = *reinterpret_cast<const uint2*>(lut + sl.addr(2 * kb + 1, lane8));
 #pragma unroll
         for (int gg = 0; gg < G; ++gg) {
-          const uint8_t* bw = brow + (gg * 16 + kb) * (kBRow * 4);
-          const uint32_t bh = *reinterpret_cast<const uint32_t*>(bw);
-          const uint32_t bl = *reinterpret_cast<const uint32_t*>(bw + kLoOff);
+          const uint2 bhl = *reinterpret_cast<const uint2*>(brow + (gg * 16 + kb) * (kBRow * 8));
+          const uint32_t bh = bhl.x, bl = bhl.y;
           const uint32_t bz = *reinterpret_cast<const uint32_t*>(zrow + (gg * 16 + kb) * (kZRow * 4));
           float d[4];
           mma_16816_zc(d, e0.x, e1.x, e0.x, e1.x, bh, bl);  // Lh (Ph, Qh) + Lh (Pl, Ql)

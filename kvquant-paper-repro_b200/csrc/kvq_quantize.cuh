@@ -28,6 +28,65 @@ __device__ __forceinline__ bool selected(uint32_t ab, int32_t idx, const Select&
 }
 
 // ---------------------------------------------------------------------------
+// Decisions in input space. For one (zero, scale) pair (a key channel or a
+// value token) n(x) = fl(fl(x - zero) / fl(scale + 1e-8)) is non-decreasing in
+// x, so for fp16 inputs every decision the emit step takes on n -- outlier
+// (|n| > thr, or |n| == thr subject to the tie cut), and the dense code
+// si[#(tau <= clamp(n))] -- is a comparison of x's order against a few fp16
+// boundaries found once by bisection over the fp16 order with the exact n.
+// ord16 maps fp16 bits to a monotone integer (both zeros to 0); finite inputs
+// lie in [-31743, 31743]. Non-finite inputs take the per-element path.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int ord16(uint32_t h) {
+  return (h & 0x8000u) ? -(int)(h & 0x7fffu) : (int)(h & 0x7fffu);
+}
+__device__ __forceinline__ float ord16_value(int o) {
+  const unsigned short hb = o < 0 ? (unsigned short)(0x8000 | -o) : (unsigned short)o;
+  return __half2float(__ushort_as_half(hb));
+}
+
+// Outlier boundaries (int4 {op, om, tpa, tmb}): |n| > thr <=> o >= op || o <= om,
+// |n| == thr <=> o in [tpa, op) or (om, tmb]; so out(x) <=> o >= op || o <= om ||
+// ((o >= tpa || o <= tmb) && index <= cut). op = kNoOrder marks a (zero, scale)
+// pair where the decisions do not apply (non-positive or non-finite divisor).
+constexpr int kNoOrder = -1000000;
+
+// Smallest finite order o in [lo, hi] with pred(n(o)) true (pred monotone
+// false -> true), or hi + 1 if none.
+template <class P>
+__device__ __forceinline__ int first_order(int lo, int hi, const Normalizer& nz, P pred) {
+  int a = lo, b = hi + 1;  // pred false below a, true from b
+  while (a < b) {
+    const int m = a + ((b - a) >> 1);
+    if (pred(nz(ord16_value(m)))) b = m; else a = m + 1;
+  }
+  return a;
+}
+
+// Whether input-space decisions apply to (zero, scale): the divisor must be
+// positive and finite (then n is monotone in x).
+__device__ __forceinline__ bool xspace_ok(float zero, float scale) {
+  const float b = __fadd_rn(scale, 1e-8f);
+  return b > 0.f && b < INFINITY && fabsf(zero) < INFINITY;
+}
+
+// One of the four outlier boundaries (which = 0..3: op, om, tpa, tmb).
+__device__ inline int out_bound(const Normalizer& nz, uint32_t thr_bits, int which) {
+  constexpr int kLo = -31743, kHi = 31743;
+  const float thr = __uint_as_float(thr_bits);
+  switch (which) {
+    case 0: return first_order(kLo, kHi, nz, [&](float n) { return n > thr; });
+    case 1: return first_order(kLo, kHi, nz, [&](float n) { return n >= -thr; }) - 1;
+    case 2: return first_order(kLo, kHi, nz, [&](float n) { return n >= thr; });
+    default: return first_order(kLo, kHi, nz, [&](float n) { return n > -thr; }) - 1;
+  }
+}
+
+__device__ __forceinline__ bool out_by_order(int o, const int4& ob, int32_t idx, int32_t cut) {
+  return o >= ob.x || o <= ob.y || ((o >= ob.z || o <= ob.w) && idx <= cut);
+}
+
+// ---------------------------------------------------------------------------
 // Keys: radix select along tokens, per (b, channel) column.
 // Columns are numbered col = b * CL + c, CL = n_heads * 128 local channels.
 // ---------------------------------------------------------------------------
@@ -39,10 +98,6 @@ struct KeyShape {
   const float* zero;
 };
 
-__device__ __forceinline__ float key_norm(const KeyShape& ks, int64_t b, int64_t t, int64_t c) {
-  const float x = __half2float(ks.k[(b * ks.S + t) * ks.C_full + ks.c0 + c]);
-  return normalize(x, ks.zero[ks.c0 + c], ks.scale[ks.c0 + c]);
-}
 
 constexpr int kHistCols = 32;  // columns per histogram CTA
 
@@ -68,7 +123,8 @@ __global__ void __launch_bounds__(256) key_hist_kernel(KeyShape ks, int shift,
   const int64_t col = b * ks.CL + c;
   const uint32_t mask_hi = shift >= 24 ? 0u : (0xffffffffu << (shift + 8));
   const uint32_t prefix = sel[col].thr & mask_hi;
-  const float z = ks.zero[ks.c0 + c], sc = ks.scale[ks.c0 + c];
+  Normalizer nz;
+  nz.init(ks.zero[ks.c0 + c], ks.scale[ks.c0 + c]);
   const int64_t n_rest = ks.S - ks.off;
   const int64_t r0 = (int64_t)blockIdx.z * rows_per_block;
   const int64_t r1 = min(n_rest, r0 + rows_per_block);
@@ -83,7 +139,7 @@ __global__ void __launch_bounds__(256) key_hist_kernel(KeyShape ks, int shift,
 #pragma unroll
     for (int i = 0; i < kHistUnroll; ++i) {
       if (rb + 8 * i < r1) {
-        const uint32_t ab = abs_bits(normalize(__half2float(xv[i]), z, sc));
+        const uint32_t ab = abs_bits(nz(__half2float(xv[i])));
         if ((ab & mask_hi) == prefix) atomicAdd(&h[lc][(ab >> shift) & 0xffu], 1u);
       }
     }
@@ -116,77 +172,119 @@ __global__ void key_select_kernel(Select* __restrict__ sel, uint32_t* __restrict
   for (int i = 0; i < 256; ++i) hc[i] = 0;  // ready for the next pass
 }
 
-// Columns where only some of the entries equal to thr are taken
-// (kleft < ties): the tie cut is the token index of the kleft-th entry equal to
-// thr in token order; other columns take every tie (tie_cut = INT_MAX).
-// grid = (CL/32 column groups, B); block 256: lane = column, warp w takes rows
-// w*32 .. w*32+31 of each 256-row chunk and keeps a bit mask of its ties; the
-// per-column prefix over the warps finds the warp (and bit) holding the cut.
-// The CTA stops once every column of the group has its cut.
-__global__ void __launch_bounds__(256) key_ties_kernel(KeyShape ks, Select* __restrict__ sel) {
+// Columns where only some of the entries equal to thr are taken (kleft <
+// ties): the tie cut is the token index of the kleft-th entry equal to thr in
+// token order; other columns take every tie (tie_cut = INT_MAX). Two kernels:
+// key_ties_count_kernel counts each column's ties per row block (grid and load
+// pattern of key_hist_kernel; CTAs whose 32 columns all take every tie skip),
+// key_ties_find_kernel (one warp per column) finds the row block holding the
+// cut from those counts and walks only that block's rows in order.
+constexpr int kTieBlocksMax = 256;  // row blocks per column (the counts reuse the histogram)
+
+inline int64_t tie_rows_per_block(int64_t n_rest) {
+  const int64_t r = (n_rest + kTieBlocksMax - 1) / kTieBlocksMax;
+  return r < 4096 ? 4096 : r;
+}
+
+__global__ void __launch_bounds__(256) key_ties_count_kernel(KeyShape ks,
+                                                             const Select* __restrict__ sel,
+                                                             int32_t* __restrict__ counts,
+                                                             int64_t rows_per_block, int nrb) {
   __shared__ int32_t s_cnt[8][32];
-  __shared__ int32_t s_need[32];   // ties still to pass, per column (0 = done)
-  __shared__ int32_t s_cut[32];
-  __shared__ int s_open;
   const int64_t b = blockIdx.y;
   const int64_t cg = (int64_t)blockIdx.x * kHistCols;
   const int lc = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t c = cg + lc;
   const int64_t col = b * ks.CL + c;
   const Select s0 = sel[col];
-  if (warp == 0) {
-    const bool partial = s0.kleft < s0.ties;
-    s_need[lc] = partial ? s0.kleft : 0;
-    s_cut[lc] = partial ? -1 : 0x7fffffff;
-    const unsigned open = __ballot_sync(0xffffffffu, partial);
-    if (lc == 0) s_open = open != 0u;
-  }
-  __syncthreads();
-  const float z = ks.zero[ks.c0 + c], sc = ks.scale[ks.c0 + c];
+  if (!__syncthreads_or(s0.kleft < s0.ties)) return;
+  Normalizer nz;
+  nz.init(ks.zero[ks.c0 + c], ks.scale[ks.c0 + c]);
   const int64_t n_rest = ks.S - ks.off;
+  const int64_t r0 = (int64_t)blockIdx.z * rows_per_block;
+  const int64_t r1 = min(n_rest, r0 + rows_per_block);
   const __half* xcol = ks.k + (b * ks.S + ks.off) * ks.C_full + ks.c0 + c;
-  for (int64_t r0 = 0; r0 < n_rest && s_open; r0 += 256) {
-    uint32_t mask = 0u;
-    const int64_t rw = r0 + warp * 32;
-#pragma unroll 8
-    for (int i = 0; i < 32; ++i) {
-      const int64_t r = rw + i;
-      if (r < n_rest && abs_bits(normalize(__half2float(xcol[r * ks.C_full]), z, sc)) == s0.thr)
-        mask |= 1u << i;
-    }
-    s_cnt[warp][lc] = __popc(mask);
-    __syncthreads();
-    // the warp whose rows hold this column's cut, and the rank inside them
-    const int need = s_need[lc];
-    int before = 0, tot = 0;
+  int cnt = 0;
+  for (int64_t rb = r0 + warp; rb < r1; rb += 8 * kHistUnroll) {
+    __half xv[kHistUnroll];
 #pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      const int x = s_cnt[w][lc];
-      before += w < warp ? x : 0;
-      tot += x;
+    for (int i = 0; i < kHistUnroll; ++i) {
+      const int64_t r = rb + 8 * i;
+      xv[i] = r < r1 ? xcol[r * ks.C_full] : __float2half(0.f);
     }
-    const int mine = s_cnt[warp][lc];
-    __syncthreads();  // every thread has read s_need and s_cnt
-    if (need > 0 && before < need && need <= before + mine) {
-      uint32_t m = mask;
-      for (int k = 1; k < need - before; ++k) m &= m - 1;
-      s_cut[lc] = (int32_t)(rw + __ffs(m) - 1);
-      s_need[lc] = 0;
-    } else if (warp == 7 && need > tot) {
-      s_need[lc] = need - tot;
-    }
-    __syncthreads();
-    if (warp == 0) {
-      const unsigned open = __ballot_sync(0xffffffffu, s_need[lc] > 0);
-      if (lc == 0) s_open = open != 0u;
-    }
-    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kHistUnroll; ++i)
+      if (rb + 8 * i < r1 && abs_bits(nz(__half2float(xv[i]))) == s0.thr) ++cnt;
   }
+  s_cnt[warp][lc] = cnt;
+  __syncthreads();
   if (warp == 0) {
-    Select s = s0;
-    s.tie_cut = s_cut[lc];
-    sel[col] = s;
+    int t = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += s_cnt[w][lc];
+    counts[col * nrb + blockIdx.z] = t;
   }
+}
+
+__global__ void __launch_bounds__(256) key_ties_find_kernel(KeyShape ks, Select* __restrict__ sel,
+                                                            const int32_t* __restrict__ counts,
+                                                            int64_t rows_per_block, int nrb,
+                                                            int64_t ncols) {
+  const int64_t col = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (col >= ncols) return;
+  Select s = sel[col];
+  if (s.kleft >= s.ties) {
+    if (lane == 0) { s.tie_cut = 0x7fffffff; sel[col] = s; }
+    return;
+  }
+  // the row block where the running tie count reaches kleft
+  int32_t need = s.kleft;
+  int rb = -1;
+  for (int i0 = 0; i0 < nrb && rb < 0; i0 += 32) {
+    const int i = i0 + lane;
+    const int32_t v = i < nrb ? counts[col * nrb + i] : 0;
+    int32_t incl = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int32_t o = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += o;
+    }
+    const uint32_t hit = __ballot_sync(0xffffffffu, incl >= need);
+    if (hit) {
+      const int L = __ffs(hit) - 1;
+      need -= __shfl_sync(0xffffffffu, incl - v, L);
+      rb = i0 + L;
+    } else {
+      need -= __shfl_sync(0xffffffffu, incl, 31);
+    }
+  }
+  int32_t cut = -1;
+  if (rb >= 0) {
+    const int64_t b = col / ks.CL, c = col % ks.CL;
+    Normalizer nz;
+    nz.init(ks.zero[ks.c0 + c], ks.scale[ks.c0 + c]);
+    const int64_t n_rest = ks.S - ks.off;
+    const int64_t r0 = (int64_t)rb * rows_per_block;
+    const int64_t r1 = min(n_rest, r0 + rows_per_block);
+    const __half* xcol = ks.k + (b * ks.S + ks.off) * ks.C_full + ks.c0 + c;
+    for (int64_t q0 = r0; q0 < r1 && need > 0; q0 += 32) {
+      const int64_t r = q0 + lane;
+      const bool tie =
+          r < r1 && abs_bits(nz(__half2float(xcol[r * ks.C_full]))) == s.thr;
+      const uint32_t bal = __ballot_sync(0xffffffffu, tie);
+      const int n = __popc(bal);
+      if (n >= need) {
+        uint32_t m = bal;
+        for (int k = 1; k < need; ++k) m &= m - 1;
+        cut = (int32_t)(q0 + __ffs(m) - 1);
+        need = 0;
+      } else {
+        need -= n;
+      }
+    }
+  }
+  if (lane == 0) { s.tie_cut = cut; sel[col] = s; }
 }
 
 // ---------------------------------------------------------------------------
@@ -279,7 +377,8 @@ __device__ __forceinline__ float plan_block_max(float v, float* red) {
 __global__ void __launch_bounds__(1024) value_plan_kernel(
     const __half* __restrict__ v, int64_t B, int64_t S, int64_t C_full, int64_t off,
     int64_t kv, float* __restrict__ v_scale, float* __restrict__ v_zero, int64_t ld_stats,
-    Select* __restrict__ sel) {
+    Select* __restrict__ sel, int32_t* __restrict__ counts, int64_t h0, int64_t n_heads,
+    int64_t nt_cap, int4* __restrict__ obnd) {
   extern __shared__ uint32_t vsm[];  // C_full words: the row's |n| bits, or a candidate list
   __shared__ uint32_t hist[256];
   __shared__ float red[32];
@@ -317,9 +416,14 @@ __global__ void __launch_bounds__(1024) value_plan_kernel(
   }
   uint32_t u[kPlanEPT];
   int emax_t = -1;
+  Normalizer nz;
+  nz.init(zero, scale);
+  const bool quick = nz.fast && finite8(raw[0]) && finite8(raw[1]);
 #pragma unroll
   for (int e = 0; e < kPlanEPT; ++e) {
-    u[e] = c0 + e < C_full ? abs_bits(normalize(__half2float(xh[e]), zero, scale)) : 0u;
+    const float xv = __half2float(xh[e]);
+    const float n = quick ? nz.quot(xv) : __fdiv_rn(__fsub_rn(xv, nz.z), nz.b);
+    u[e] = c0 + e < C_full ? abs_bits(n) : 0u;
     if (c0 + e < C_full) emax_t = max(emax_t, (int)(u[e] >> 23));
   }
   if (kv <= 0) {  // no outliers: a threshold nothing reaches
@@ -437,6 +541,29 @@ __global__ void __launch_bounds__(1024) value_plan_kernel(
     s.tie_cut = sh_cut;
     sel[b * S + t] = s;
   }
+  // the token's outlier bounds in input order (one bound per lane)
+  if (obnd && tid < 4) {
+    const int v = xspace_ok(zero, scale) ? out_bound(nz, thr, tid) : kNoOrder;
+    reinterpret_cast<int*>(obnd + b * S + t)[tid] = v;
+  }
+  // Outlier counts of the token's heads in [h0, h0 + n_heads), added into the
+  // CSR row of (unit, tile, 16-token block) (counts[row + 1], zeroed by the
+  // caller): the 8 threads of a head (16 channels each) sum their selections.
+  if (counts) {
+    const int32_t cut = sh_cut;
+    int cnt = 0;
+#pragma unroll
+    for (int e = 0; e < kPlanEPT; ++e)
+      cnt += (c0 + e < C_full && (u[e] > thr || (u[e] == thr && (int32_t)(c0 + e) <= cut))) ? 1 : 0;
+    cnt += __shfl_xor_sync(0xffffffffu, cnt, 1);
+    cnt += __shfl_xor_sync(0xffffffffu, cnt, 2);
+    cnt += __shfl_xor_sync(0xffffffffu, cnt, 4);
+    const int64_t hf = c0 / kHeadDim;
+    if ((tid & 7) == 0 && cnt > 0 && c0 < C_full && hf >= h0 && hf < h0 + n_heads) {
+      const int64_t unit = b * n_heads + (hf - h0);
+      atomicAdd(counts + 2 * (unit * nt_cap + t / kTileTokens) + (t % kTileTokens) / 16 + 1, cnt);
+    }
+  }
 }
 
 // One packed outlier entry: position (token_in_tile << 7 | channel) in the low
@@ -503,6 +630,73 @@ __device__ void build_nearest_table(const float* sv, const uint8_t* si, int n, N
   if (k == 0) t->fast = fast ? 1 : 0;
 }
 
+// Sorted position of an input's code: #(cbnd[k] <= o) over the code bounds.
+template <int BITS>
+__device__ __forceinline__ int pos_by_order(int o, const int16_t* cbnd) {
+  int pos = 0;
+#pragma unroll
+  for (int step = 1 << (BITS - 1); step >= 1; step >>= 1)
+    if (cbnd[pos + step - 1] <= o) pos += step;
+  return pos;
+}
+
+// Outlier bounds of every key column [B * CL] (thread = (column, bound)).
+__global__ void key_out_bounds_kernel(KeyShape ks, const Select* __restrict__ sel,
+                                      int4* __restrict__ obnd, int64_t ncols) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= ncols * 4) return;
+  const int64_t col = i >> 2, c = col % ks.CL;
+  const float z = ks.zero[ks.c0 + c], sc = ks.scale[ks.c0 + c];
+  int v = kNoOrder;
+  if (xspace_ok(z, sc)) {
+    Normalizer nz;
+    nz.init(z, sc);
+    v = out_bound(nz, sel[col].thr, (int)(i & 3));
+  }
+  reinterpret_cast<int*>(obnd)[i] = v;
+}
+
+// Code bounds of n_groups (zero, scale) pairs: group g uses zero/scale at
+// (g / per_row) * ld + g % per_row (keys: the CL channels, per_row = CL;
+// values: the tokens (b, t), per_row = S, ld = the stats' row stride).
+// cbnd[g][k] (k < 2^bits - 1) = the smallest fp16 order whose dense value
+// reaches tau[k]; cbnd[g][15] = 1 where the bounds are valid.
+__global__ void __launch_bounds__(256) code_bounds_kernel(const float* __restrict__ zero,
+                                                          const float* __restrict__ scale,
+                                                          int64_t n_groups, int64_t per_row,
+                                                          int64_t ld, const float* __restrict__ cb,
+                                                          int bits, int16_t* __restrict__ cbnd) {
+  __shared__ float s_cb[16], s_cbs[16];
+  __shared__ uint8_t s_cbi[16];
+  __shared__ NearestTable s_nt;
+  const int ncb = 1 << bits;
+  if (threadIdx.x == 0) {
+    for (int k = 0; k < ncb; ++k) s_cb[k] = cb[k];
+    sort_codebook(s_cb, ncb, s_cbs, s_cbi);
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) build_nearest_table(s_cbs, s_cbi, ncb, &s_nt);
+  __syncthreads();
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_groups * 16) return;
+  const int64_t g = i >> 4;
+  const int k = (int)(i & 15);
+  const int64_t zi = (g / per_row) * ld + g % per_row;
+  const float z = zero[zi], sc = scale[zi];
+  const bool ok = s_nt.fast != 0 && xspace_ok(z, sc);
+  int16_t v = 0;
+  if (k == 15) {
+    v = ok ? 1 : 0;
+  } else if (ok && k < ncb - 1) {
+    Normalizer nz;
+    nz.init(z, sc);
+    const float tau = s_nt.tau[k];
+    v = (int16_t)first_order(-31743, 31743, nz,
+                             [&](float n) { return fminf(fmaxf(n, -1.f), 1.f) >= tau; });
+  }
+  cbnd[i] = v;
+}
+
 template <int BITS>
 __device__ __forceinline__ int nearest_fast(float v, const NearestTable& t) {
   int pos = 0;
@@ -544,6 +738,11 @@ struct EmitArgs {
   int64_t nnz_cap;
   __half* sink_out;     // [B, H*128] or null
   __half* dequant_out;  // [B, S, H*128] or null
+  // input-space decisions (null: per-element path): outlier bounds per key
+  // column [B * CL] / value token [B * S]; code bounds per key channel [CL][16]
+  // / value token [B * S][16] (entry 15 = 1 where valid)
+  const int4* obnd;
+  const int16_t* cbnd;
 };
 
 // Inclusive scan of v over the CTA's 256 threads; also returns the total.
@@ -571,10 +770,12 @@ __device__ __forceinline__ int emit_block_scan(int v, int* sh, int& total) {
 template <int KIND, bool COUNT_ONLY, int BITS>
 __global__ void __launch_bounds__(kEmitThreads) emit_kernel(EmitArgs a) {
   __shared__ __align__(16) uint8_t s_code[kTileTokens][kHeadDim];  // codes of the tile
+  __shared__ __align__(16) int16_t s_cbnd[kHeadDim][16];  // code bounds: channels / tokens
   __shared__ float s_cb[16], s_cbs[16];
   __shared__ uint8_t s_cbi[16];
   __shared__ NearestTable s_nt;
   __shared__ int s_scan[kEmitThreads / 32];
+  __shared__ int s_c0;  // code of a dense 0
   const int64_t b = blockIdx.y, h = blockIdx.z;
   const int tid = threadIdx.x, r = tid >> 4, j = tid & 15;
   const int64_t unit = b * a.H + h;
@@ -591,25 +792,36 @@ __global__ void __launch_bounds__(kEmitThreads) emit_kernel(EmitArgs a) {
     }
     __syncthreads();
     if (tid < 32) build_nearest_table(s_cbs, s_cbi, ncb, &s_nt);
+    if (tid == 0) s_c0 = nearest_centroid(0.f, s_cb, ncb);
+    if (KIND == 0 && a.cbnd) {  // the head's code bounds
+      for (int i = tid; i < kHeadDim * 2; i += kEmitThreads)
+        reinterpret_cast<uint4*>(&s_cbnd[0][0])[i] =
+            reinterpret_cast<const uint4*>(a.cbnd + (h * kHeadDim) * 16)[i];
+    }
   }
-  // keys: this thread's 8 channels' zero, scale and selection (threshold, tie cut)
-  float kz[8], ks[8];
-  Select kc[8];
+  // keys: this thread's 8 channels' outlier bounds and tie cuts
+  int4 kob[8];
+  int32_t kcut[8];
+  bool kx = KIND == 0 && (!with_out || a.obnd != nullptr) && (COUNT_ONLY || a.cbnd != nullptr);
   if (KIND == 0) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      kz[e] = a.k_zero[cfull0 + e];
-      ks[e] = a.k_scale[cfull0 + e];
-      kc[e] = Select{};
+      kob[e] = make_int4(0, 0, 0, 0);
+      kcut[e] = 0;
       if (with_out) {
-        const Select* sp = a.sel + b * CL + h * kHeadDim + c0 + e;
-        kc[e].thr = sp->thr;
-        kc[e].tie_cut = sp->tie_cut;
+        kcut[e] = a.sel[b * CL + h * kHeadDim + c0 + e].tie_cut;
+        if (a.obnd) kob[e] = a.obnd[b * CL + h * kHeadDim + c0 + e];
+        kx = kx && kob[e].x != kNoOrder;
       }
     }
   }
   __syncthreads();
+  if (KIND == 0 && !COUNT_ONLY && kx) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) kx = kx && s_cbnd[c0 + e][15] == 1;
+  }
   const bool fast = COUNT_ONLY ? true : s_nt.fast != 0;
+  const int code0 = COUNT_ONLY ? 0 : s_c0;
 
   // this thread's 16-byte input chunk of token r of block blk of a tile
   auto load = [&](int64_t tile, int blk) {
@@ -627,6 +839,16 @@ __global__ void __launch_bounds__(kEmitThreads) emit_kernel(EmitArgs a) {
       nx0 = load(tile + 1, 0);
       nx1 = load(tile + 1, 1);
     }
+    if (KIND == 1 && !COUNT_ONLY && a.cbnd) {  // the tile's tokens' code bounds
+      __syncthreads();  // the previous tile is done with them
+      if (tid < 2 * kTileTokens) {
+        const int64_t t = tile * kTileTokens + (tid >> 1);
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (t < a.S) v = reinterpret_cast<const uint4*>(a.cbnd + (b * a.S + t) * 16)[tid & 1];
+        reinterpret_cast<uint4*>(&s_cbnd[0][0])[tid] = v;
+      }
+      __syncthreads();
+    }
 #pragma unroll
     for (int blk = 0; blk < 2; ++blk) {
       const int ti = 16 * blk + r;  // token within the tile
@@ -635,50 +857,83 @@ __global__ void __launch_bounds__(kEmitThreads) emit_kernel(EmitArgs a) {
       const bool is_sink = a.off == 1 && t == 0;
       const bool live = in && !is_sink;
       const uint4 raw = cur[blk];
-      float vz = 0.f, vs = 0.f;
-      Select vc{};
-      if (KIND == 1 && live) {
-        vs = a.v_scale[b * a.ld_stats + t];
-        vz = a.v_zero[b * a.ld_stats + t];
-        if (with_out) {
-          const Select* sp = a.sel + b * a.S + t;
-          vc.thr = sp->thr;
-          vc.tie_cut = sp->tie_cut;
-        }
-      }
       const __half* xh = reinterpret_cast<const __half*>(&raw);
       float nval[8];
       uint32_t m8 = 0u;
       uint32_t code_lo = 0u, code_hi = 0u;
+      if (live) {
+        // the token's outlier bounds and tie cut (values)
+        int4 vob = make_int4(0, 0, 0, 0);
+        int32_t vcut = 0;
+        bool xs = KIND == 0 ? kx : false;
+        if (KIND == 1) {
+          if (with_out) vcut = a.sel[b * a.S + t].tie_cut;
+          xs = (!with_out || a.obnd != nullptr) &&
+               (COUNT_ONLY || (a.cbnd != nullptr && s_cbnd[ti][15] == 1));
+          if (xs && with_out) {
+            vob = a.obnd[b * a.S + t];
+            xs = vob.x != kNoOrder;
+          }
+        }
+        if (xs && fast && finite8(raw)) {
+          // decisions by the input's order against the precomputed bounds
+          const int16_t* crow = KIND == 0 ? nullptr : &s_cbnd[ti][0];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float xv = __half2float(xh[e]);
-        const float n = KIND == 0 ? normalize(xv, kz[e], ks[e]) : normalize(xv, vz, vs);
-        nval[e] = n;
-        bool out = false;
-        if (live && with_out) {
-          out = KIND == 0 ? selected(abs_bits(n), (int32_t)(t - a.off), kc[e])
-                          : selected(abs_bits(n), (int32_t)(cfull0 + e), vc);
-        }
-        if (out) m8 |= 1u << e;
-        if (!COUNT_ONLY) {
-          int code = 0;
-          if (live) {
-            const float dense = out ? 0.f : fminf(fmaxf(n, -1.f), 1.f);
-            code = fast ? nearest_fast<BITS>(dense, s_nt)
-                        : nearest_centroid_sorted(dense, s_cbs, s_cbi, ncb);
+          for (int e = 0; e < 8; ++e) {
+            const uint16_t hb = __half_as_ushort(xh[e]);
+            const int o = ord16(hb);
+            const bool out = with_out && (KIND == 0 ? out_by_order(o, kob[e], (int32_t)(t - a.off), kcut[e])
+                                                    : out_by_order(o, vob, (int32_t)(cfull0 + e), vcut));
+            if (out) m8 |= 1u << e;
+            if (!COUNT_ONLY) {
+              const int code =
+                  out ? code0
+                      : (int)s_nt.si[pos_by_order<BITS>(o, KIND == 0 ? &s_cbnd[c0 + e][0] : crow)];
+              if (e < 4) code_lo |= (uint32_t)code << (8 * e);
+              else code_hi |= (uint32_t)code << (8 * (e - 4));
+            }
           }
-          if (e < 4) code_lo |= (uint32_t)code << (8 * e);
-          else code_hi |= (uint32_t)code << (8 * (e - 4));
-          if (out || (a.dequant_out && in)) {
-            const float dq = dequant_ref(s_cb[code], out ? n : 0.f, KIND == 0 ? ks[e] : vs,
-                                         KIND == 0 ? kz[e] : vz);
-            if (out) nval[e] = dq;  // the entry holds the dequantized value
-            if (a.dequant_out && in)
-              a.dequant_out[(b * a.S + t) * CL + h * kHeadDim + c0 + e] =
-                  is_sink ? xh[e] : __float2half_rn(dq);
+        } else {
+          // per element: IEEE normalization, selection and nearest centroid
+          const Select sl = KIND == 0 ? Select{} : (with_out ? a.sel[b * a.S + t] : Select{});
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float zz = KIND == 0 ? a.k_zero[cfull0 + e] : a.v_zero[b * a.ld_stats + t];
+            const float ss = KIND == 0 ? a.k_scale[cfull0 + e] : a.v_scale[b * a.ld_stats + t];
+            const float n = normalize(__half2float(xh[e]), zz, ss);
+            bool out = false;
+            if (with_out) {
+              const Select se = KIND == 0 ? a.sel[b * CL + h * kHeadDim + c0 + e] : sl;
+              out = selected(abs_bits(n), KIND == 0 ? (int32_t)(t - a.off) : (int32_t)(cfull0 + e), se);
+            }
+            if (out) m8 |= 1u << e;
+            if (!COUNT_ONLY) {
+              const float dense = out ? 0.f : fminf(fmaxf(n, -1.f), 1.f);
+              const int code = fast ? nearest_fast<BITS>(dense, s_nt)
+                                    : nearest_centroid_sorted(dense, s_cbs, s_cbi, ncb);
+              if (e < 4) code_lo |= (uint32_t)code << (8 * e);
+              else code_hi |= (uint32_t)code << (8 * (e - 4));
+            }
           }
         }
+        // outlier entries and the optional dequantized output need n and dq
+        if (!COUNT_ONLY && (m8 || a.dequant_out)) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const bool out = (m8 >> e) & 1u;
+            if (!out && !a.dequant_out) continue;
+            const float zz = KIND == 0 ? a.k_zero[cfull0 + e] : a.v_zero[b * a.ld_stats + t];
+            const float ss = KIND == 0 ? a.k_scale[cfull0 + e] : a.v_scale[b * a.ld_stats + t];
+            const int code = (int)(((e < 4 ? code_lo : code_hi) >> (8 * (e & 3))) & 0xffu);
+            const float n = out ? normalize(__half2float(xh[e]), zz, ss) : 0.f;
+            const float dq = dequant_ref(s_cb[code], n, ss, zz);
+            nval[e] = dq;  // the entry holds the dequantized value
+            if (a.dequant_out)
+              a.dequant_out[(b * a.S + t) * CL + h * kHeadDim + c0 + e] = __float2half_rn(dq);
+          }
+        }
+      } else if (!COUNT_ONLY && a.dequant_out && in) {  // the sink token: its input
+        *reinterpret_cast<uint4*>(a.dequant_out + (b * a.S + t) * CL + h * kHeadDim + c0) = raw;
       }
       if (!COUNT_ONLY) {
         *reinterpret_cast<uint2*>(&s_code[ti][c0]) = make_uint2(code_lo, code_hi);
@@ -866,12 +1121,33 @@ __global__ void zero_i32_kernel(int32_t* __restrict__ p, int64_t n) {
 
 // Workspace layout.
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+// keys: selections [B*CL], histograms [B*CL][256] (then the tie counts),
+// outlier bounds [B*CL] int4, code bounds [CL][16] int16
 inline size_t key_ws_bytes(int64_t B, int64_t n_heads) {
   const int64_t ncols = B * n_heads * kHeadDim;
-  return align256(ncols * sizeof(Select)) + align256(ncols * 256 * sizeof(uint32_t));
+  return align256(ncols * sizeof(Select)) + align256(ncols * 256 * sizeof(uint32_t)) +
+         align256(ncols * sizeof(int4)) + align256(n_heads * kHeadDim * 16 * sizeof(int16_t));
 }
+inline int4* key_obnd(void* ws, int64_t B, int64_t n_heads) {
+  const int64_t ncols = B * n_heads * kHeadDim;
+  return reinterpret_cast<int4*>((char*)ws + align256(ncols * sizeof(Select)) +
+                                 align256(ncols * 256 * sizeof(uint32_t)));
+}
+inline int16_t* key_cbnd(void* ws, int64_t B, int64_t n_heads) {
+  const int64_t ncols = B * n_heads * kHeadDim;
+  return reinterpret_cast<int16_t*>((char*)key_obnd(ws, B, n_heads) + align256(ncols * sizeof(int4)));
+}
+// values: selections [B*S], outlier bounds [B*S] int4, code bounds [B*S][16] int16
 inline size_t value_ws_bytes(int64_t B, int64_t S) {
-  return align256((size_t)B * S * sizeof(Select));
+  return align256((size_t)B * S * sizeof(Select)) + align256((size_t)B * S * sizeof(int4)) +
+         align256((size_t)B * S * 16 * sizeof(int16_t));
+}
+inline int4* value_obnd(void* ws, int64_t B, int64_t S) {
+  return reinterpret_cast<int4*>((char*)ws + align256((size_t)B * S * sizeof(Select)));
+}
+inline int16_t* value_cbnd(void* ws, int64_t B, int64_t S) {
+  return reinterpret_cast<int16_t*>((char*)value_obnd(ws, B, S) +
+                                    align256((size_t)B * S * sizeof(int4)));
 }
 
 inline bool bits_ok(int bits) { return bits >= 2 && bits <= 4; }
@@ -988,7 +1264,17 @@ extern "C" int kvq_quantize_keys_plan(const void* k, int64_t B, int64_t S, int64
       key_hist_kernel<<<hg, 256, 0, st>>>(ks, shift, sel, hist, rows_per_block);
       key_select_kernel<<<(unsigned)((ncols + 127) / 128), 128, 0, st>>>(sel, hist, ncols, shift);
     }
-    key_ties_kernel<<<dim3((unsigned)(CL / kHistCols), (unsigned)B), 256, 0, st>>>(ks, sel);
+    // tie counts per (column, row block) in the (now zero) histogram memory
+    const int64_t trb = tie_rows_per_block(n_rest);
+    const int nrb = (int)((n_rest + trb - 1) / trb);
+    int32_t* tcounts = reinterpret_cast<int32_t*>(hist);
+    key_ties_count_kernel<<<dim3((unsigned)(CL / kHistCols), (unsigned)B, (unsigned)nrb), 256, 0,
+                            st>>>(ks, sel, tcounts, trb, nrb);
+    key_ties_find_kernel<<<(unsigned)((ncols + 7) / 8), 256, 0, st>>>(ks, sel, tcounts, trb, nrb,
+                                                                      ncols);
+    // each column's outlier decisions as bounds on the input order
+    key_out_bounds_kernel<<<(unsigned)((ncols * 4 + 255) / 256), 256, 0, st>>>(
+        ks, sel, key_obnd(workspace, B, n_heads), ncols);
   }
   // Outlier counts per (unit, tile, block), then the row pointer.
   const int64_t nrows = 2 * B * n_heads * nt_cap;  // (unit, tile, 16-token block)
@@ -998,6 +1284,7 @@ extern "C" int kvq_quantize_keys_plan(const void* k, int64_t B, int64_t S, int64
   ea.off = ks.off; ea.k_scale = scale; ea.k_zero = zero; ea.sel = sel; ea.bits = 2;
   ea.nt_cap = nt_cap; ea.out_ptr = out_ptr; ea.nnz_cap = outliers ? 0 : -1;
   ea.cb = nullptr;  // COUNT_ONLY never reads the codebook
+  ea.obnd = outliers ? key_obnd(workspace, B, n_heads) : nullptr;
   launch_emit<0>(ea, true, st);
   scan_counts(out_ptr, nrows, nnz_out, st);
   return check_launch("quantize_keys_plan");
@@ -1036,6 +1323,14 @@ extern "C" int kvq_quantize_keys_emit(const void* k, int64_t B, int64_t S, int64
   ea.out_ent = out_ent;
   ea.nnz_cap = outlier_ratio > 0 ? nnz_cap : -1;
   ea.sink_out = (__half*)sink_out; ea.dequant_out = (__half*)dequant_out;
+  // code decisions of the head range's channels as bounds on the input order
+  void* ws = const_cast<void*>(workspace);
+  const int64_t CL = n_heads * kHeadDim;
+  code_bounds_kernel<<<(unsigned)((CL * 16 + 255) / 256), 256, 0, st>>>(
+      zero + h0 * kHeadDim, scale + h0 * kHeadDim, CL, CL, 0, codebook, bits,
+      key_cbnd(ws, B, n_heads));
+  ea.obnd = outlier_ratio > 0 ? key_obnd(ws, B, n_heads) : nullptr;
+  ea.cbnd = key_cbnd(ws, B, n_heads);
   launch_emit<0>(ea, false, st);
   return check_launch("quantize_keys_emit");
 }
@@ -1069,28 +1364,26 @@ extern "C" int kvq_quantize_values_plan(const void* v, int64_t B, int64_t S, int
   const int64_t n_rest = S - off;
   const bool outliers = outlier_ratio > 0;
   const int64_t kv = outliers ? outlier_count(C_full, outlier_ratio) : 0;
+  const int64_t nrows = 2 * B * n_heads * nt_cap;  // (unit, tile, 16-token block)
+  zero_i32_kernel<<<grid_for(nrows + 1, 256), 256, 0, st>>>(out_ptr, nrows + 1);
   if (B * n_rest > 0) {
+    // per-token stats, selections and the outlier counts of each CSR row
     const size_t smem = C_full * sizeof(uint32_t);
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(value_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem);
     value_plan_kernel<<<(unsigned)(B * n_rest), plan_threads(C_full), smem, st>>>(
-        (const __half*)v, B, S, C_full, off, kv, v_scale, v_zero, ld_stats, sel);
+        (const __half*)v, B, S, C_full, off, kv, v_scale, v_zero, ld_stats, sel,
+        outliers ? out_ptr : nullptr, h0, n_heads, nt_cap,
+        outliers ? value_obnd(workspace, B, S) : nullptr);
   }
   if (off) {  // the sink token carries no stats
     for (int64_t b = 0; b < B; ++b) {
-      cudaMemsetAsync(v_scale + b * ld_stats, 0, sizeof(float), st);
-      cudaMemsetAsync(v_zero + b * ld_stats, 0, sizeof(float), st);
+      if (cudaMemsetAsync(v_scale + b * ld_stats, 0, sizeof(float), st) != cudaSuccess ||
+          cudaMemsetAsync(v_zero + b * ld_stats, 0, sizeof(float), st) != cudaSuccess)
+        return check_launch("quantize_values_plan");
     }
   }
-  const int64_t nrows = 2 * B * n_heads * nt_cap;  // (unit, tile, 16-token block)
-  zero_i32_kernel<<<grid_for(nrows + 1, 256), 256, 0, st>>>(out_ptr, nrows + 1);
-  EmitArgs ea{};
-  ea.x = (const __half*)v; ea.B = B; ea.S = S; ea.C_full = C_full; ea.h0 = h0;
-  ea.H = n_heads; ea.off = off; ea.v_scale = v_scale; ea.v_zero = v_zero;
-  ea.ld_stats = ld_stats; ea.sel = sel; ea.cb = nullptr; ea.bits = 2; ea.nt_cap = nt_cap;
-  ea.out_ptr = out_ptr; ea.nnz_cap = outliers ? 0 : -1;
-  launch_emit<1>(ea, true, st);
   scan_counts(out_ptr, nrows, nnz_out, st);
   return check_launch("quantize_values_plan");
 }
@@ -1128,6 +1421,12 @@ extern "C" int kvq_quantize_values_emit(const void* v, int64_t B, int64_t S, int
   ea.out_ptr = const_cast<int32_t*>(out_ptr); ea.out_ent = out_ent;
   ea.nnz_cap = outlier_ratio > 0 ? nnz_cap : -1;
   ea.sink_out = (__half*)sink_out; ea.dequant_out = (__half*)dequant_out;
+  // code decisions of every token as bounds on the input order
+  void* ws = const_cast<void*>(workspace);
+  code_bounds_kernel<<<(unsigned)((B * S * 16 + 255) / 256), 256, 0, st>>>(
+      v_zero, v_scale, B * S, S, ld_stats, codebook, bits, value_cbnd(ws, B, S));
+  ea.obnd = outlier_ratio > 0 ? value_obnd(ws, B, S) : nullptr;
+  ea.cbnd = value_cbnd(ws, B, S);
   launch_emit<1>(ea, false, st);
   return check_launch("quantize_values_emit");
 }

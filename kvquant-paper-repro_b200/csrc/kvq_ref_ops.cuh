@@ -210,3 +210,37 @@ extern "C" int kvq_lut_lookup(const float* x, const float* codebook, int64_t lut
       x, codebook, (int)lut_size, idx_out, dq_out, N);
   return check_launch("lut_lookup");
 }
+
+// The reference's normalization n = (x - zero) / (scale + 1e-8) of quantize_k /
+// quantize_v (kvquant/quant/kv_quantizer.py:82,104) in the form the quantize
+// kernels compute it (Normalizer: reciprocal, two corrections, IEEE division
+// where its guards fail). x fp16 [rows, cols]; zero / scale fp32 per column
+// (per_channel, keys) or per row (values); out fp32.
+namespace kvq {
+__global__ void normalize_kernel(const __half* __restrict__ x, int64_t rows, int64_t cols,
+                                 const float* __restrict__ zero, const float* __restrict__ scale,
+                                 int per_channel, float* __restrict__ out) {
+  const int64_t n = rows * cols;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t k = per_channel ? i % cols : i / cols;
+    Normalizer nz;
+    nz.init(zero[k], scale[k]);
+    out[i] = nz(__half2float(x[i]));
+  }
+}
+}  // namespace kvq
+
+extern "C" int kvq_normalize(const void* x, int64_t rows, int64_t cols, const float* zero,
+                             const float* scale, int per_channel, float* out, void* stream) {
+  using namespace kvq;
+  clear_error();
+  if (rows < 0 || cols < 0) {
+    set_error("normalize: invalid shape rows=%lld cols=%lld", (long long)rows, (long long)cols);
+    return KVQ_ERR_INVALID;
+  }
+  if (rows == 0 || cols == 0) return KVQ_OK;
+  normalize_kernel<<<grid_for(rows * cols, 256), 256, 0, as_stream(stream)>>>(
+      (const __half*)x, rows, cols, zero, scale, per_channel, out);
+  return check_launch("normalize");
+}

@@ -44,6 +44,7 @@ _SIGNATURES = {
                                 _c_int, _c_p]),
     "kvq_sparse_matvec_csr": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_i64, _c_i64,
                                        _c_p]),
+    "kvq_normalize": (_c_int, [_c_p, _c_i64, _c_i64, _c_p, _c_p, _c_int, _c_p, _c_p]),
     "kvq_lut_lookup": (_c_int, [_c_p, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p]),
     "kvq_quantize_keys_workspace": (_c_size, [_c_i64, _c_i64, _c_i64]),
     "kvq_quantize_keys_plan": (_c_int, [_c_p, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p,
@@ -219,6 +220,25 @@ class CudaOps:
             _check(self.lib.kvq_lut_lookup(_ptr(xc), _ptr(cb), cb.numel(), _ptr(idx), _ptr(dq),
                                            xc.numel(), _stream(xc)), self.lib)
         return [idx, dq]
+
+    def normalize(self, x, zero, scale, per_channel: bool):
+        """The quantizers' n = (x - zero) / (scale + 1e-8) (kv_quantizer.py:82,104) of
+        x [rows, cols] fp16, zero/scale per column (per_channel) or per row: fp32."""
+        _require_cuda(x, zero, scale)
+        if x.dim() != 2 or x.dtype != torch.float16:
+            raise RuntimeError("x must be fp16 [rows, cols]")
+        xc = x.contiguous()
+        rows, cols = xc.shape
+        zc = zero.to(torch.float32).contiguous()
+        sc = scale.to(torch.float32).contiguous()
+        if zc.numel() != (cols if per_channel else rows) or sc.numel() != zc.numel():
+            raise RuntimeError("zero/scale must have one entry per column (per_channel) or row")
+        out = torch.empty((rows, cols), dtype=torch.float32, device=xc.device)
+        with torch.cuda.device(xc.device):
+            _check(self.lib.kvq_normalize(_ptr(xc), rows, cols, _ptr(zc), _ptr(sc),
+                                          int(bool(per_channel)), _ptr(out), _stream(xc)),
+                   self.lib)
+        return out
 
     # -- status --------------------------------------------------------------------
     def check_status(self, device=None):

@@ -107,3 +107,36 @@ def test_lut_lookup_bit_exact(cuda):
     ri, rd = O.lut_lookup(x, cb)
     np.testing.assert_array_equal(idx.cpu().numpy(), ri)
     np.testing.assert_array_equal(dq.cpu().numpy(), rd)
+
+
+def test_normalize_matches_ieee_division_for_every_fp16_input(cuda):
+    """The quantizers' n = (x - z) / (s + 1e-8) (kv_quantizer.py:82,104), computed by
+    the kernels from the reciprocal of the divisor, equals numpy's IEEE fp32
+    quotient bit for bit for all 65536 fp16 inputs and per-column (zero, scale)
+    pairs spanning the guarded range and beyond it (tiny, huge and zero scales,
+    tiny and huge offsets, divisors whose mantissa is all ones)."""
+    from kvquant.kernels import get_cuda_ops
+    x = np.arange(65536, dtype=np.uint32).astype(np.uint16).view(np.float16)
+    rng = np.random.default_rng(5)
+    allones = np.array([(e << 23) | 0x7FFFFF for e in (100, 120, 126, 127, 128, 135)],
+                       np.uint32).view(np.float32)
+    scale = np.concatenate([rng.uniform(1e-3, 50, 40).astype(np.float32),
+                            np.exp(rng.uniform(-30, 30, 20)).astype(np.float32), allones,
+                            np.array([0, 1e-8, 1e-30, 1e12, 3e38], np.float32)])
+    zero = np.concatenate([rng.standard_normal(scale.size - 12).astype(np.float32) * 10,
+                           np.array([0, -0.0, 1e-20, -1e-38, 1e-45, 2e20, -7e30, 65504,
+                                     -65504, 0.5, 1.0, -3.0], np.float32)])
+    rows = x.reshape(-1, 1).repeat(scale.size, 1)          # [65536, n_pairs] fp16
+    got = get_cuda_ops().normalize(t(rows, cuda), t(zero, cuda), t(scale, cuda),
+                                   True).cpu().numpy()
+    with np.errstate(all="ignore"):
+        ref = ((rows.astype(np.float32) - zero) / (scale + np.float32(1e-8))).astype(np.float32)
+    same = (got.view(np.uint32) == ref.view(np.uint32)) | (np.isnan(got) & np.isnan(ref))
+    assert same.all(), (int((~same).sum()), np.argwhere(~same)[:5])
+    # per-row (values) orientation
+    vr = rng.standard_normal((64, 512)).astype(np.float16)
+    vz = rng.standard_normal(64).astype(np.float32)
+    vs = rng.uniform(0.5, 30, 64).astype(np.float32)
+    got = get_cuda_ops().normalize(t(vr, cuda), t(vz, cuda), t(vs, cuda), False).cpu().numpy()
+    ref = ((vr.astype(np.float32) - vz[:, None]) / (vs[:, None] + np.float32(1e-8))).astype(np.float32)
+    np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
