@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--codebook", action="store_true",
                     help="benchmark NUQ codebook fitting (offline calibration) instead of decode")
     ap.add_argument("--codebook-samples", type=int, default=1 << 24)
+    ap.add_argument("--quantize", action="store_true",
+                    help="measure quantize-on-append of one prefill layer on its own line")
     ap.add_argument("--config3", action="store_true",
                     help="full decode of a random-init LLaMA-2-7B through the Hugging Face "
                          "packed cache (32K-token prefill, then one-token steps)")
@@ -899,6 +901,33 @@ def run_config3(args):
     }), flush=True)
 
 
+def run_quantize(args):
+    """Quantize-on-append of one prefill layer on its own JSON line: quantize_keys +
+    quantize_values of the workload's layer (all heads, --tokens tokens), kernels
+    only, best of 2 after a warm call (the same measurement as the default line's
+    quantize_append)."""
+    import dataclasses
+    import torch
+    from kvquant import synthetic as syn
+    dev = torch.device("cuda", 0)
+    log = (lambda m: print(f"[quantize] {m}", file=sys.stderr, flush=True))
+    wl = syn.WORKLOADS[args.workload]
+    if args.tokens:
+        wl = dataclasses.replace(wl, tokens=args.tokens, name=f"{wl.name}@{args.tokens}tok")
+    _, q = build_cache(wl, 2, 0, wl.kv_heads, dev, log)
+    print(json.dumps({
+        "metric": "quantize-on-append of one prefill layer (keys + values): tokens/s",
+        "value": wl.tokens / (q["ms_per_layer"] / 1e3), "unit": "tokens/s", "n_gpus": 1,
+        "higher_is_better": True, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"quantize-{wl.name}", "tokens": wl.tokens,
+                   "kv_heads": wl.kv_heads, "bits": wl.bits, "outlier_ratio": wl.outlier_ratio},
+        "ms_per_layer": q["ms_per_layer"],
+        "roofline": {"bound": "hbm", "achieved": q["achieved_GBps"], "peak": q["peak_GBps"],
+                     "peak_source": q["peak_source"], "unit": "GB/s", "frac": q["frac"],
+                     "traffic": None, "bytes_per_launch": q["algorithmic_bytes"]},
+        "what": q["what"]}), flush=True)
+
+
 def main():
     args = parse()
     if args.config3:
@@ -907,6 +936,10 @@ def main():
     if args.codebook:
         if int(os.environ.get("RANK", "0")) == 0:
             run_codebook(args)
+        return
+    if args.quantize:
+        if int(os.environ.get("RANK", "0")) == 0:
+            run_quantize(args)
         return
     if args.impl == "reference":
         run_reference(args)

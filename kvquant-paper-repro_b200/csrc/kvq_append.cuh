@@ -362,7 +362,7 @@ extern "C" int kvq_append_values(const void* v_new, int64_t B, int64_t S_new, in
     cudaFuncSetAttribute(value_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   value_plan_kernel<<<(unsigned)(B * S_new), plan_threads(C_full), smem, st>>>(
       (const __half*)v_new, B, S_new, C_full, 0, kv, v_scale + T_old, v_zero + T_old, ld_stats,
-      sel, nullptr, 0, 0, 0, nullptr);
+      sel, nullptr, 0, 0, 0);
   AppendArgs aa{};
   aa.x = (const __half*)v_new; aa.B = B; aa.S_new = S_new; aa.C_full = C_full; aa.h0 = h0;
   aa.H = n_heads; aa.T_old = T_old; aa.v_scale = v_scale; aa.v_zero = v_zero;

@@ -810,11 +810,11 @@ __global__ void __launch_bounds__(256) value_prep_kernel(const float* __restrict
 // rest), (scale, zero) pairs [32], probabilities [G][kPRow], entries [32].
 template <int BITS, int G>
 struct ValSmem {
-  static constexpr bool kWarpAcc = G <= 4;
+  static constexpr bool kWarpAcc = G <= 2;  // per-warp outlier sums (shared by all warps above)
   static constexpr int kLut = PairLutHiLo<BITS>::kBytes;
   static constexpr int kAcc = kLut;
   static constexpr int kAccFloats = (kWarpAcc ? kValWarps : 1) * G * kHeadDim;
-  static constexpr int kZ = kAcc + kAccFloats * 4;
+  static constexpr int kZ = kAcc + kAccFloats * 8;  // outlier sums: 64-bit fixed point
   static constexpr int kW = kZ + 64;  // fp16 token weights [warp][2G][32]: high parts, low parts
   static constexpr int kPtr = kW + kValWarps * 2 * G * 64;
   // ring and stages on 128-byte boundaries, so that a warp's 512-byte copies
@@ -841,17 +841,17 @@ __global__ void __launch_bounds__(kValThreads, 1)
   extern __shared__ __align__(16) uint8_t smem[];
   using S = ValSmem<BITS, G>;
   const uint8_t* lut = smem;
-  float* acc = reinterpret_cast<float*>(smem + S::kAcc);
+  unsigned long long* acc = reinterpret_cast<unsigned long long*>(smem + S::kAcc);
   float* zacc = reinterpret_cast<float*>(smem + S::kZ);
   int32_t* tptr = reinterpret_cast<int32_t*>(smem + S::kPtr);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const uint32_t lane8 = (uint32_t)lane << 3;
-  float* wacc = acc + (S::kWarpAcc ? warp * G * kHeadDim : 0);
+  unsigned long long* wacc = acc + (S::kWarpAcc ? warp * G * kHeadDim : 0);
   PairLutHiLo<BITS>::build(smem, a.cb);
   __shared__ float s_cb0;
   if (threadIdx.x == 0) s_cb0 = dense_zero_value(a.cb, 1 << BITS);
-  for (int idx = threadIdx.x; idx < S::kAccFloats; idx += blockDim.x) acc[idx] = 0.f;
+  for (int idx = threadIdx.x; idx < S::kAccFloats; idx += blockDim.x) acc[idx] = 0ull;
   if (threadIdx.x < G) zacc[threadIdx.x] = 0.f;
 
   const int nt = (int)((a.T + kTileTokens - 1) / kTileTokens);
@@ -871,6 +871,11 @@ __global__ void __launch_bounds__(kValThreads, 1)
   // largest possible weight is 2^14 in fp16
   const float e_scale = ldexpf(1.f, 14 - pow2_exponent(row_max[b]));
   const float inv_e = 1.f / e_scale;
+  // Outlier terms p (d - dense) are at most about max_t s_t (|n| <= 1 for values):
+  // summed as integers in units of 2^(e - 40), e = exponent of that maximum
+  // (native 64-bit shared-memory integer adds instead of float compare-and-swap
+  // loops; exact, and far below 2^63 for any token count below 2^22).
+  const float fix = ldexpf(1.f, min(100, max(-100, 40 - pow2_exponent(row_max[b]))));
   for (int k = threadIdx.x; k <= tb - ta; k += blockDim.x)
     tptr[k] = __ldg(a.out_ptr + 2 * (u * a.nt_cap + ta + k));
   // Softmax of raw scores: (M, 1/L) of each head of the unit.
@@ -1009,7 +1014,9 @@ __global__ void __launch_bounds__(kValThreads, 1)
         const int tok = (int)((en >> 7) & 31), ch = (int)(en & 127);
         const float so = entry_value(en) - fmaf(s_cb0, sz[tok].x, sz[tok].y);
 #pragma unroll
-        for (int hd = 0; hd < G; ++hd) atomicAdd(wacc + hd * kHeadDim + ch, fp[hd * S::kPRow + tok] * so);
+        for (int hd = 0; hd < G; ++hd)
+          atomicAdd(wacc + hd * kHeadDim + ch,
+                    (unsigned long long)__float2ll_rn(fp[hd * S::kPRow + tok] * so * fix));
       }
     }
   }
@@ -1018,15 +1025,6 @@ __global__ void __launch_bounds__(kValThreads, 1)
   for (int hd = 0; hd < G; ++hd) {
     const float z = warp_sum(zs[hd]);
     if (lane == 0) atomicAdd(zacc + hd, z);
-  }
-  // Sink (token 0, in the first split): p_0 * v_sink, fp32.
-  if (sink && ta == 0) {
-    for (int idx = threadIdx.x; idx < G * kHeadDim; idx += blockDim.x) {
-      const int hd = idx / kHeadDim, dd = idx % kHeadDim;
-      float p0 = prow[hd * a.T];
-      if (a.ml) p0 = __expf(p0 * a.stat_scale - s_ml[hd].x) * s_ml[hd].y;
-      atomicAdd(acc + hd * kHeadDim + dd, p0 * __half2float(a.v_sink[(b * a.H + h) * kHeadDim + dd]));
-    }
   }
   __syncthreads();  // all warps are done with their rings and accumulators
   float* red = reinterpret_cast<float*>(smem + S::kRing);  // [warp][G][128]
@@ -1055,16 +1053,23 @@ __global__ void __launch_bounds__(kValThreads, 1)
   }
   __syncthreads();
   for (int idx = threadIdx.x; idx < G * kHeadDim; idx += blockDim.x) {
-    float sum = 0.f, side = 0.f;
+    float sum = 0.f;
 #pragma unroll
     for (int w = 0; w < kValWarps; ++w) sum += red[w * G * kHeadDim + idx];
+    long long isum = 0;
     if (S::kWarpAcc) {
 #pragma unroll
-      for (int w = 0; w < kValWarps; ++w) side += acc[w * G * kHeadDim + idx];
+      for (int w = 0; w < kValWarps; ++w) isum += (long long)acc[w * G * kHeadDim + idx];
     } else {
-      side = acc[idx];
+      isum = (long long)acc[idx];
     }
+    float side = (float)isum / fix;
     const int hd = idx / kHeadDim, dd = idx % kHeadDim;
+    if (sink && ta == 0) {  // the sink (token 0, in the first split): p_0 * v_sink, fp32
+      float p0 = prow[hd * a.T];
+      if (a.ml) p0 = __expf(p0 * a.stat_scale - s_ml[hd].x) * s_ml[hd].y;
+      side = fmaf(p0, __half2float(a.v_sink[(b * a.H + h) * kHeadDim + dd]), side);
+    }
     float* dst = a.partial + ((int64_t)split * (U * G) + u * G + hd) * 129;
     dst[dd] = fmaf(sum, inv_e, side);
     if (dd == 0) dst[128] = zacc[hd];

@@ -378,7 +378,7 @@ __global__ void __launch_bounds__(1024) value_plan_kernel(
     const __half* __restrict__ v, int64_t B, int64_t S, int64_t C_full, int64_t off,
     int64_t kv, float* __restrict__ v_scale, float* __restrict__ v_zero, int64_t ld_stats,
     Select* __restrict__ sel, int32_t* __restrict__ counts, int64_t h0, int64_t n_heads,
-    int64_t nt_cap, int4* __restrict__ obnd) {
+    int64_t nt_cap) {
   extern __shared__ uint32_t vsm[];  // C_full words: the row's |n| bits, or a candidate list
   __shared__ uint32_t hist[256];
   __shared__ float red[32];
@@ -541,11 +541,6 @@ __global__ void __launch_bounds__(1024) value_plan_kernel(
     s.tie_cut = sh_cut;
     sel[b * S + t] = s;
   }
-  // the token's outlier bounds in input order (one bound per lane)
-  if (obnd && tid < 4) {
-    const int v = xspace_ok(zero, scale) ? out_bound(nz, thr, tid) : kNoOrder;
-    reinterpret_cast<int*>(obnd + b * S + t)[tid] = v;
-  }
   // Outlier counts of the token's heads in [h0, h0 + n_heads), added into the
   // CSR row of (unit, tile, 16-token block) (counts[row + 1], zeroed by the
   // caller): the 8 threads of a head (16 channels each) sum their selections.
@@ -640,6 +635,61 @@ __device__ __forceinline__ int pos_by_order(int o, const int16_t* cbnd) {
   return pos;
 }
 
+// The codebook as the emit and bound kernels use it, prepared once per call:
+// original and sorted values, the sorted entries' original indices, the
+// switching points and the code of a dense 0.
+struct __align__(16) EmitCodebook {
+  float cb[16], cbs[16];
+  uint8_t cbi[16];
+  NearestTable nt;
+  int c0;
+  int pad[6];
+};
+static_assert(sizeof(EmitCodebook) % 16 == 0, "copied as 16-byte words");
+
+__global__ void codebook_setup_kernel(const float* __restrict__ cb, int bits,
+                                      EmitCodebook* __restrict__ out) {
+  __shared__ EmitCodebook e;
+  const int ncb = 1 << bits;
+  if (threadIdx.x == 0) {
+    for (int k = 0; k < 16; ++k) e.cb[k] = k < ncb ? cb[k] : 0.f;
+    sort_codebook(e.cb, ncb, e.cbs, e.cbi);
+    e.c0 = nearest_centroid(0.f, e.cb, ncb);
+  }
+  __syncwarp();
+  build_nearest_table(e.cbs, e.cbi, ncb, &e.nt);
+  __syncwarp();
+  for (int i = threadIdx.x; i < (int)(sizeof(EmitCodebook) / 4); i += 32)
+    reinterpret_cast<uint32_t*>(out)[i] = reinterpret_cast<const uint32_t*>(&e)[i];
+}
+
+// Copies an EmitCodebook from global to shared memory (all threads, then sync).
+__device__ __forceinline__ void load_emit_codebook(const EmitCodebook* g, EmitCodebook* s) {
+  for (int i = threadIdx.x; i < (int)(sizeof(EmitCodebook) / 16); i += blockDim.x)
+    reinterpret_cast<uint4*>(s)[i] = reinterpret_cast<const uint4*>(g)[i];
+  __syncthreads();
+}
+
+// Outlier bounds of every value token (thread = (token, bound)); tokens before
+// `off` (the sink) have none.
+__global__ void value_out_bounds_kernel(const float* __restrict__ v_zero,
+                                        const float* __restrict__ v_scale, int64_t ld,
+                                        const Select* __restrict__ sel, int64_t B, int64_t S,
+                                        int64_t off, int4* __restrict__ obnd) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= B * S * 4) return;
+  const int64_t row = i >> 2, b = row / S, t = row % S;
+  if (t < off) return;
+  const float z = v_zero[b * ld + t], sc = v_scale[b * ld + t];
+  int v = kNoOrder;
+  if (xspace_ok(z, sc)) {
+    Normalizer nz;
+    nz.init(z, sc);
+    v = out_bound(nz, sel[row].thr, (int)(i & 3));
+  }
+  reinterpret_cast<int*>(obnd)[i] = v;
+}
+
 // Outlier bounds of every key column [B * CL] (thread = (column, bound)).
 __global__ void key_out_bounds_kernel(KeyShape ks, const Select* __restrict__ sel,
                                       int4* __restrict__ obnd, int64_t ncols) {
@@ -664,19 +714,13 @@ __global__ void key_out_bounds_kernel(KeyShape ks, const Select* __restrict__ se
 __global__ void __launch_bounds__(256) code_bounds_kernel(const float* __restrict__ zero,
                                                           const float* __restrict__ scale,
                                                           int64_t n_groups, int64_t per_row,
-                                                          int64_t ld, const float* __restrict__ cb,
+                                                          int64_t ld,
+                                                          const EmitCodebook* __restrict__ ecb,
                                                           int bits, int16_t* __restrict__ cbnd) {
-  __shared__ float s_cb[16], s_cbs[16];
-  __shared__ uint8_t s_cbi[16];
-  __shared__ NearestTable s_nt;
+  __shared__ EmitCodebook s_ec;
+  load_emit_codebook(ecb, &s_ec);
+  const NearestTable& s_nt = s_ec.nt;
   const int ncb = 1 << bits;
-  if (threadIdx.x == 0) {
-    for (int k = 0; k < ncb; ++k) s_cb[k] = cb[k];
-    sort_codebook(s_cb, ncb, s_cbs, s_cbi);
-  }
-  __syncthreads();
-  if (threadIdx.x < 32) build_nearest_table(s_cbs, s_cbi, ncb, &s_nt);
-  __syncthreads();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n_groups * 16) return;
   const int64_t g = i >> 4;
@@ -743,6 +787,7 @@ struct EmitArgs {
   // / value token [B * S][16] (entry 15 = 1 where valid)
   const int4* obnd;
   const int16_t* cbnd;
+  const EmitCodebook* ecb;  // the prepared codebook (emit; unused when counting)
 };
 
 // Inclusive scan of v over the CTA's 256 threads; also returns the total.
@@ -770,12 +815,14 @@ __device__ __forceinline__ int emit_block_scan(int v, int* sh, int& total) {
 template <int KIND, bool COUNT_ONLY, int BITS>
 __global__ void __launch_bounds__(kEmitThreads) emit_kernel(EmitArgs a) {
   __shared__ __align__(16) uint8_t s_code[kTileTokens][kHeadDim];  // codes of the tile
-  __shared__ __align__(16) int16_t s_cbnd[kHeadDim][16];  // code bounds: channels / tokens
-  __shared__ float s_cb[16], s_cbs[16];
-  __shared__ uint8_t s_cbi[16];
-  __shared__ NearestTable s_nt;
+  // code bounds: keys: the head's 128 channels; values: two buffers of a tile's 32 tokens
+  __shared__ __align__(16) int16_t s_cbnd[kHeadDim][16];
+  __shared__ EmitCodebook s_ec;
   __shared__ int s_scan[kEmitThreads / 32];
-  __shared__ int s_c0;  // code of a dense 0
+  const float* s_cb = s_ec.cb;
+  const float* s_cbs = s_ec.cbs;
+  const uint8_t* s_cbi = s_ec.cbi;
+  const NearestTable& s_nt = s_ec.nt;
   const int64_t b = blockIdx.y, h = blockIdx.z;
   const int tid = threadIdx.x, r = tid >> 4, j = tid & 15;
   const int64_t unit = b * a.H + h;
@@ -786,13 +833,7 @@ __global__ void __launch_bounds__(kEmitThreads) emit_kernel(EmitArgs a) {
   const bool with_out = a.nnz_cap >= 0;
   constexpr int ncb = 1 << BITS;
   if (!COUNT_ONLY) {
-    if (tid == 0) {
-      for (int k = 0; k < ncb; ++k) s_cb[k] = a.cb[k];
-      sort_codebook(s_cb, ncb, s_cbs, s_cbi);
-    }
-    __syncthreads();
-    if (tid < 32) build_nearest_table(s_cbs, s_cbi, ncb, &s_nt);
-    if (tid == 0) s_c0 = nearest_centroid(0.f, s_cb, ncb);
+    load_emit_codebook(a.ecb, &s_ec);
     if (KIND == 0 && a.cbnd) {  // the head's code bounds
       for (int i = tid; i < kHeadDim * 2; i += kEmitThreads)
         reinterpret_cast<uint4*>(&s_cbnd[0][0])[i] =
@@ -821,8 +862,17 @@ __global__ void __launch_bounds__(kEmitThreads) emit_kernel(EmitArgs a) {
     for (int e = 0; e < 8; ++e) kx = kx && s_cbnd[c0 + e][15] == 1;
   }
   const bool fast = COUNT_ONLY ? true : s_nt.fast != 0;
-  const int code0 = COUNT_ONLY ? 0 : s_c0;
+  const int code0 = COUNT_ONLY ? 0 : s_ec.c0;
 
+  // values: a tile's code bounds, 16 bytes per thread for threads 0..63
+  const bool vtab = KIND == 1 && !COUNT_ONLY && a.cbnd != nullptr;
+  auto load_cb = [&](int64_t tile) {
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    const int64_t t = tile * kTileTokens + (tid >> 1);
+    if (tid < 2 * kTileTokens && t < a.S)
+      v = reinterpret_cast<const uint4*>(a.cbnd + (b * a.S + t) * 16)[tid & 1];
+    return v;
+  };
   // this thread's 16-byte input chunk of token r of block blk of a tile
   auto load = [&](int64_t tile, int blk) {
     const int64_t t = tile * kTileTokens + 16 * blk + r;
@@ -833,21 +883,18 @@ __global__ void __launch_bounds__(kEmitThreads) emit_kernel(EmitArgs a) {
   const int64_t tile_begin = (int64_t)blockIdx.x * kEmitTiles;
   const int64_t tile_end = min(nt, tile_begin + kEmitTiles);
   uint4 nx0 = load(tile_begin, 0), nx1 = load(tile_begin, 1);  // one tile ahead
+  uint4 nxb = make_uint4(0u, 0u, 0u, 0u);  // values: the next tile's code bounds
+  if (vtab) {
+    if (tid < 2 * kTileTokens) reinterpret_cast<uint4*>(&s_cbnd[0][0])[tid] = load_cb(tile_begin);
+    __syncthreads();
+  }
   for (int64_t tile = tile_begin; tile < tile_end; ++tile) {
     const uint4 cur[2] = {nx0, nx1};
+    const int cbuf = (int)((tile - tile_begin) & 1) * kTileTokens;  // values: this tile's rows
     if (tile + 1 < tile_end) {
       nx0 = load(tile + 1, 0);
       nx1 = load(tile + 1, 1);
-    }
-    if (KIND == 1 && !COUNT_ONLY && a.cbnd) {  // the tile's tokens' code bounds
-      __syncthreads();  // the previous tile is done with them
-      if (tid < 2 * kTileTokens) {
-        const int64_t t = tile * kTileTokens + (tid >> 1);
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (t < a.S) v = reinterpret_cast<const uint4*>(a.cbnd + (b * a.S + t) * 16)[tid & 1];
-        reinterpret_cast<uint4*>(&s_cbnd[0][0])[tid] = v;
-      }
-      __syncthreads();
+      if (vtab) nxb = load_cb(tile + 1);
     }
 #pragma unroll
     for (int blk = 0; blk < 2; ++blk) {
@@ -869,7 +916,7 @@ __global__ void __launch_bounds__(kEmitThreads) emit_kernel(EmitArgs a) {
         if (KIND == 1) {
           if (with_out) vcut = a.sel[b * a.S + t].tie_cut;
           xs = (!with_out || a.obnd != nullptr) &&
-               (COUNT_ONLY || (a.cbnd != nullptr && s_cbnd[ti][15] == 1));
+               (COUNT_ONLY || (a.cbnd != nullptr && s_cbnd[cbuf + ti][15] == 1));
           if (xs && with_out) {
             vob = a.obnd[b * a.S + t];
             xs = vob.x != kNoOrder;
@@ -877,7 +924,7 @@ __global__ void __launch_bounds__(kEmitThreads) emit_kernel(EmitArgs a) {
         }
         if (xs && fast && finite8(raw)) {
           // decisions by the input's order against the precomputed bounds
-          const int16_t* crow = KIND == 0 ? nullptr : &s_cbnd[ti][0];
+          const int16_t* crow = KIND == 0 ? nullptr : &s_cbnd[cbuf + ti][0];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const uint16_t hb = __half_as_ushort(xh[e]);
@@ -998,7 +1045,10 @@ __global__ void __launch_bounds__(kEmitThreads) emit_kernel(EmitArgs a) {
         *reinterpret_cast<uint32_t*>(dst) = wd[k];
       }
     }
-    __syncthreads();  // s_code is rewritten by the next tile
+    // values: the next tile's code bounds into the other buffer (nobody reads it now)
+    if (vtab && tid < 2 * kTileTokens && tile + 1 < tile_end)
+      reinterpret_cast<uint4*>(&s_cbnd[kTileTokens - cbuf][0])[tid] = nxb;
+    __syncthreads();  // s_code is rewritten by the next tile; the bounds are visible
   }
 }
 
@@ -1126,7 +1176,8 @@ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 inline size_t key_ws_bytes(int64_t B, int64_t n_heads) {
   const int64_t ncols = B * n_heads * kHeadDim;
   return align256(ncols * sizeof(Select)) + align256(ncols * 256 * sizeof(uint32_t)) +
-         align256(ncols * sizeof(int4)) + align256(n_heads * kHeadDim * 16 * sizeof(int16_t));
+         align256(ncols * sizeof(int4)) + align256(n_heads * kHeadDim * 16 * sizeof(int16_t)) +
+         align256(sizeof(EmitCodebook));
 }
 inline int4* key_obnd(void* ws, int64_t B, int64_t n_heads) {
   const int64_t ncols = B * n_heads * kHeadDim;
@@ -1137,10 +1188,14 @@ inline int16_t* key_cbnd(void* ws, int64_t B, int64_t n_heads) {
   const int64_t ncols = B * n_heads * kHeadDim;
   return reinterpret_cast<int16_t*>((char*)key_obnd(ws, B, n_heads) + align256(ncols * sizeof(int4)));
 }
+inline EmitCodebook* key_ecb(void* ws, int64_t B, int64_t n_heads) {
+  return reinterpret_cast<EmitCodebook*>(
+      (char*)key_cbnd(ws, B, n_heads) + align256(n_heads * kHeadDim * 16 * sizeof(int16_t)));
+}
 // values: selections [B*S], outlier bounds [B*S] int4, code bounds [B*S][16] int16
 inline size_t value_ws_bytes(int64_t B, int64_t S) {
   return align256((size_t)B * S * sizeof(Select)) + align256((size_t)B * S * sizeof(int4)) +
-         align256((size_t)B * S * 16 * sizeof(int16_t));
+         align256((size_t)B * S * 16 * sizeof(int16_t)) + align256(sizeof(EmitCodebook));
 }
 inline int4* value_obnd(void* ws, int64_t B, int64_t S) {
   return reinterpret_cast<int4*>((char*)ws + align256((size_t)B * S * sizeof(Select)));
@@ -1148,6 +1203,10 @@ inline int4* value_obnd(void* ws, int64_t B, int64_t S) {
 inline int16_t* value_cbnd(void* ws, int64_t B, int64_t S) {
   return reinterpret_cast<int16_t*>((char*)value_obnd(ws, B, S) +
                                     align256((size_t)B * S * sizeof(int4)));
+}
+inline EmitCodebook* value_ecb(void* ws, int64_t B, int64_t S) {
+  return reinterpret_cast<EmitCodebook*>((char*)value_cbnd(ws, B, S) +
+                                         align256((size_t)B * S * 16 * sizeof(int16_t)));
 }
 
 inline bool bits_ok(int bits) { return bits >= 2 && bits <= 4; }
@@ -1326,9 +1385,11 @@ extern "C" int kvq_quantize_keys_emit(const void* k, int64_t B, int64_t S, int64
   // code decisions of the head range's channels as bounds on the input order
   void* ws = const_cast<void*>(workspace);
   const int64_t CL = n_heads * kHeadDim;
+  codebook_setup_kernel<<<1, 32, 0, st>>>(codebook, bits, key_ecb(ws, B, n_heads));
   code_bounds_kernel<<<(unsigned)((CL * 16 + 255) / 256), 256, 0, st>>>(
-      zero + h0 * kHeadDim, scale + h0 * kHeadDim, CL, CL, 0, codebook, bits,
+      zero + h0 * kHeadDim, scale + h0 * kHeadDim, CL, CL, 0, key_ecb(ws, B, n_heads), bits,
       key_cbnd(ws, B, n_heads));
+  ea.ecb = key_ecb(ws, B, n_heads);
   ea.obnd = outlier_ratio > 0 ? key_obnd(ws, B, n_heads) : nullptr;
   ea.cbnd = key_cbnd(ws, B, n_heads);
   launch_emit<0>(ea, false, st);
@@ -1374,8 +1435,10 @@ extern "C" int kvq_quantize_values_plan(const void* v, int64_t B, int64_t S, int
                            (int)smem);
     value_plan_kernel<<<(unsigned)(B * n_rest), plan_threads(C_full), smem, st>>>(
         (const __half*)v, B, S, C_full, off, kv, v_scale, v_zero, ld_stats, sel,
-        outliers ? out_ptr : nullptr, h0, n_heads, nt_cap,
-        outliers ? value_obnd(workspace, B, S) : nullptr);
+        outliers ? out_ptr : nullptr, h0, n_heads, nt_cap);
+    if (outliers)  // each token's outlier decisions as bounds on the input order
+      value_out_bounds_kernel<<<(unsigned)((B * S * 4 + 255) / 256), 256, 0, st>>>(
+          v_zero, v_scale, ld_stats, sel, B, S, off, value_obnd(workspace, B, S));
   }
   if (off) {  // the sink token carries no stats
     for (int64_t b = 0; b < B; ++b) {
@@ -1423,8 +1486,10 @@ extern "C" int kvq_quantize_values_emit(const void* v, int64_t B, int64_t S, int
   ea.sink_out = (__half*)sink_out; ea.dequant_out = (__half*)dequant_out;
   // code decisions of every token as bounds on the input order
   void* ws = const_cast<void*>(workspace);
+  codebook_setup_kernel<<<1, 32, 0, st>>>(codebook, bits, value_ecb(ws, B, S));
   code_bounds_kernel<<<(unsigned)((B * S * 16 + 255) / 256), 256, 0, st>>>(
-      v_zero, v_scale, B * S, S, ld_stats, codebook, bits, value_cbnd(ws, B, S));
+      v_zero, v_scale, B * S, S, ld_stats, value_ecb(ws, B, S), bits, value_cbnd(ws, B, S));
+  ea.ecb = value_ecb(ws, B, S);
   ea.obnd = outlier_ratio > 0 ? value_obnd(ws, B, S) : nullptr;
   ea.cbnd = value_cbnd(ws, B, S);
   launch_emit<1>(ea, false, st);
