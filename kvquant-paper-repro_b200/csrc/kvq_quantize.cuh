@@ -627,11 +627,11 @@ __device__ void build_nearest_table(const float* sv, const uint8_t* si, int n, N
 
 // Sorted position of an input's code: #(cbnd[k] <= o) over the code bounds.
 template <int BITS>
-__device__ __forceinline__ int pos_by_order(int o, const int16_t* cbnd) {
+__device__ __forceinline__ int pos_by_order(int o, const int16_t* cbnd, int stride = 1) {
   int pos = 0;
 #pragma unroll
   for (int step = 1 << (BITS - 1); step >= 1; step >>= 1)
-    if (cbnd[pos + step - 1] <= o) pos += step;
+    if (cbnd[(pos + step - 1) * stride] <= o) pos += step;
   return pos;
 }
 
@@ -834,10 +834,14 @@ __global__ void __launch_bounds__(kEmitThreads) emit_kernel(EmitArgs a) {
   constexpr int ncb = 1 << BITS;
   if (!COUNT_ONLY) {
     load_emit_codebook(a.ecb, &s_ec);
-    if (KIND == 0 && a.cbnd) {  // the head's code bounds
-      for (int i = tid; i < kHeadDim * 2; i += kEmitThreads)
-        reinterpret_cast<uint4*>(&s_cbnd[0][0])[i] =
-            reinterpret_cast<const uint4*>(a.cbnd + (h * kHeadDim) * 16)[i];
+    if (KIND == 0 && a.cbnd) {
+      // the head's code bounds, transposed to [bound][channel]: a warp's 16
+      // channel chunks then hit distinct bank pairs instead of one bank
+      int16_t* t16 = &s_cbnd[0][0];
+      for (int i = tid; i < kHeadDim * 16; i += kEmitThreads) {
+        const int c = i >> 4, k = i & 15;
+        t16[k * kHeadDim + c] = a.cbnd[(h * kHeadDim + c) * 16 + k];
+      }
     }
   }
   // keys: this thread's 8 channels' outlier bounds and tie cuts
@@ -859,7 +863,7 @@ __global__ void __launch_bounds__(kEmitThreads) emit_kernel(EmitArgs a) {
   __syncthreads();
   if (KIND == 0 && !COUNT_ONLY && kx) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) kx = kx && s_cbnd[c0 + e][15] == 1;
+    for (int e = 0; e < 8; ++e) kx = kx && (&s_cbnd[0][0])[15 * kHeadDim + c0 + e] == 1;
   }
   const bool fast = COUNT_ONLY ? true : s_nt.fast != 0;
   const int code0 = COUNT_ONLY ? 0 : s_ec.c0;
@@ -935,7 +939,9 @@ __global__ void __launch_bounds__(kEmitThreads) emit_kernel(EmitArgs a) {
             if (!COUNT_ONLY) {
               const int code =
                   out ? code0
-                      : (int)s_nt.si[pos_by_order<BITS>(o, KIND == 0 ? &s_cbnd[c0 + e][0] : crow)];
+                      : (int)s_nt.si[KIND == 0
+                                         ? pos_by_order<BITS>(o, &s_cbnd[0][0] + c0 + e, kHeadDim)
+                                         : pos_by_order<BITS>(o, crow)];
               if (e < 4) code_lo |= (uint32_t)code << (8 * e);
               else code_hi |= (uint32_t)code << (8 * (e - 4));
             }
