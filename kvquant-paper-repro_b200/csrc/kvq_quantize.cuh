@@ -357,7 +357,70 @@ __device__ uint32_t radix_select_list(const uint32_t* u, int n, uint32_t prefix,
   return prefix;
 }
 
+// The same select by one warp (no block barriers): for the short candidate
+// lists of the value plan's fast path.
+__device__ uint32_t radix_select_list_warp(const uint32_t* u, int n, uint32_t prefix, int shift0,
+                                           uint32_t* hist, int32_t* sh_kleft, int32_t* sh_digit,
+                                           int32_t* sh_ties) {
+  const int lane = threadIdx.x & 31;
+  for (int shift = shift0; shift >= 0; shift -= 8) {
+    const uint32_t mask_hi = shift >= 24 ? 0u : (0xffffffffu << (shift + 8));
+    for (int i = lane; i < 256; i += 32) hist[i] = 0;
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) {
+      const uint32_t ab = u[i];
+      if ((ab & mask_hi) == prefix) atomicAdd(&hist[(ab >> shift) & 0xffu], 1u);
+    }
+    __syncwarp();
+    radix_pick(hist, sh_kleft, sh_digit, sh_ties);
+    __syncwarp();
+    prefix |= (uint32_t)*sh_digit << shift;
+    __syncwarp();
+  }
+  return prefix;
+}
+
+// Tie cut by one warp: the index (or chan[index]) of the need-th entry of
+// list[0..n) equal to thr, INT_MAX when need is 0.
+__device__ int32_t tie_cut_warp(const uint32_t* list, const uint32_t* chan, int n, uint32_t thr,
+                                int32_t need) {
+  const int lane = threadIdx.x & 31;
+  int32_t cut = 0x7fffffff;
+  for (int i0 = 0; i0 < n && need > 0; i0 += 32) {
+    const int i = i0 + lane;
+    const bool tie = i < n && list[i] == thr;
+    const uint32_t bal = __ballot_sync(0xffffffffu, tie);
+    const int cnt = __popc(bal);
+    if (cnt >= need) {
+      uint32_t m = bal;
+      for (int k = 1; k < need; ++k) m &= m - 1;
+      const int at = i0 + (__ffs(m) - 1);
+      cut = chan ? (int32_t)chan[at] : at;
+      need = 0;
+    } else {
+      need -= cnt;
+    }
+  }
+  return cut;
+}
+
 // Block-wide reductions of the plan kernel (any blockDim multiple of 32).
+// Max of a and of b over the block in one pass (two barriers).
+__device__ __forceinline__ float2 plan_block_max2(float a, float b, float2* red) {
+  a = warp_max(a);
+  b = warp_max(b);
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[w] = make_float2(a, b);
+  __syncthreads();
+  float2 r = make_float2(-INFINITY, -INFINITY);
+  for (int k = 0; k < (int)(blockDim.x >> 5); ++k) {
+    r.x = fmaxf(r.x, red[k].x);
+    r.y = fmaxf(r.y, red[k].y);
+  }
+  __syncthreads();
+  return r;
+}
+
 __device__ __forceinline__ float plan_block_max(float v, float* red) {
   v = warp_max(v);
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -382,8 +445,10 @@ __global__ void __launch_bounds__(1024) value_plan_kernel(
   extern __shared__ uint32_t vsm[];  // C_full words: the row's |n| bits, or a candidate list
   __shared__ uint32_t hist[256];
   __shared__ float red[32];
+  __shared__ float2 red2[32];
   __shared__ int32_t s_bc[32][8];  // per-warp counts of the top binades
   __shared__ int32_t sh_kleft, sh_digit, sh_ties, sh_cut, sh_bin, sh_m;
+  __shared__ uint32_t sh_thr;
   const int64_t row = blockIdx.x;  // over B * (S - off)
   const int64_t n_rest = S - off;
   const int64_t b = row / n_rest, t = row % n_rest + off;
@@ -405,8 +470,11 @@ __global__ void __launch_bounds__(1024) value_plan_kernel(
       mx = fmaxf(mx, f);
     }
   }
-  mn = -plan_block_max(-mn, red);
-  mx = plan_block_max(mx, red);
+  {
+    const float2 r = plan_block_max2(-mn, mx, reinterpret_cast<float2*>(red2));
+    mn = -r.x;
+    mx = r.y;
+  }
   // kv_quantizer.py:106-107: scale = (max - min) / 2, zero = (max + min) / 2 (fp32).
   const float scale = __fdiv_rn(__fsub_rn(mx, mn), 2.0f);
   const float zero = __fdiv_rn(__fadd_rn(mx, mn), 2.0f);
@@ -498,9 +566,21 @@ __global__ void __launch_bounds__(1024) value_plan_kernel(
     list = vsm;
     chan = vsm + cap;
     n = sh_m;
-    // bits 31..24 are fixed by the binade; the first digit (bits 23..16) holds its
+    // one warp selects among the binade's entries and finds the tie cut: bits
+    // 31..24 are fixed by the binade; the first digit (bits 23..16) holds its
     // exponent's low bit, the same for every entry of the list
-    thr = radix_select_list(list, n, (eb >> 1) << 24, 16, hist, &sh_kleft, &sh_digit, &sh_ties);
+    if (tid < 32) {
+      const uint32_t th =
+          radix_select_list_warp(list, n, (eb >> 1) << 24, 16, hist, &sh_kleft, &sh_digit, &sh_ties);
+      const int32_t cut = sh_kleft < sh_ties ? tie_cut_warp(list, chan, n, th, sh_kleft)
+                                              : 0x7fffffff;
+      if (lane == 0) {
+        sh_thr = th;
+        sh_cut = cut;
+      }
+    }
+    __syncthreads();
+    thr = sh_thr;
   } else {
 #pragma unroll
     for (int e = 0; e < kPlanEPT; ++e)
@@ -509,30 +589,14 @@ __global__ void __launch_bounds__(1024) value_plan_kernel(
     list = vsm;
     n = (int)C_full;
     thr = radix_select_list(list, n, 0u, 24, hist, &sh_kleft, &sh_digit, &sh_ties);
-  }
-  // Tie cut: the channel index of the kleft-th entry equal to the threshold
-  // (list order is channel order on both paths).
-  if (tid == 0) sh_cut = 0x7fffffff;
-  __syncthreads();
-  if (sh_kleft < sh_ties && tid < 32) {
-    int32_t need = sh_kleft;
-    for (int i0 = 0; i0 < n && need > 0; i0 += 32) {
-      const int i = i0 + lane;
-      const bool tie = i < n && list[i] == thr;
-      const uint32_t bal = __ballot_sync(0xffffffffu, tie);
-      const int cnt = __popc(bal);
-      if (cnt >= need) {
-        uint32_t m = bal;
-        for (int k = 1; k < need; ++k) m &= m - 1;
-        const int at = i0 + (__ffs(m) - 1);
-        if (lane == 0) sh_cut = chan ? (int32_t)chan[at] : at;
-        need = 0;
-      } else {
-        need -= cnt;
-      }
+    // tie cut: the channel index of the kleft-th entry equal to the threshold
+    if (tid < 32) {
+      const int32_t cut = sh_kleft < sh_ties ? tie_cut_warp(list, nullptr, n, thr, sh_kleft)
+                                              : 0x7fffffff;
+      if (lane == 0) sh_cut = cut;
     }
+    __syncthreads();
   }
-  __syncthreads();
   if (tid == 0) {
     Select s;
     s.thr = thr;
