@@ -100,6 +100,27 @@ struct PairLutHiLo {
 // An outlier entry's value: the reference's fp16 dequantized key / value at
 // its position (see outlier_entry). The decode kernels add (value - dense) *
 // coefficient, dense = cb[c0] * s + z being what the code tiles hold there.
+// Pair LUT with the code values' fp16 high parts at byte (v << 8) | (lane << 2)
+// and their low parts 128 bytes further, so that a lane loads each of the four
+// words straight into the register of the MMA operand that needs it.
+template <int BITS>
+struct PairLutSplit {
+  static constexpr int kEntries = 1 << (2 * BITS);
+  static constexpr int kBytes = kEntries * 256;
+  __device__ static void build(uint8_t* smem, const float* cb) {
+    constexpr int mask = (1 << BITS) - 1;
+    for (int idx = threadIdx.x; idx < kEntries * 32; idx += blockDim.x) {
+      const int v = idx >> 5, lane = idx & 31;
+      const float c0 = cb[v & mask], c1 = cb[v >> BITS];
+      const __half h0 = __float2half_rn(c0), h1 = __float2half_rn(c1);
+      const uint32_t hi = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+      *reinterpret_cast<uint32_t*>(smem + (v << 8) + (lane << 2)) = hi;
+      *reinterpret_cast<uint32_t*>(smem + (v << 8) + 128 + (lane << 2)) =
+          half2_bits(c0 - __half2float(h0), c1 - __half2float(h1));
+    }
+  }
+};
+
 __device__ __forceinline__ float entry_value(uint32_t ent) {
   return __half2float(__ushort_as_half((unsigned short)(ent >> 16)));
 }
@@ -248,7 +269,7 @@ constexpr uint32_t kA256 = 0x5C005C00u;  // half2(256, 256)
 // slab and one entry).
 template <int BITS>
 struct KeySmem {
-  static constexpr int kLut = PairLutHiLo<BITS>::kBytes;
+  static constexpr int kLut = PairLutSplit<BITS>::kBytes;
   static constexpr int kZ = kLut;
   static constexpr int kB = kZ + kMaxSlots * 16 * kZRow * 4;  // uint2 (high, low) B words
   static constexpr int kSc = kB + kMaxSlots * 16 * kBRow * 8;
@@ -287,6 +308,11 @@ __device__ __forceinline__ float f2sum(uint64_t v) {
   float lo, hi;
   asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
   return lo + hi;
+}
+__device__ __forceinline__ uint64_t f2add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
 }
 __device__ __forceinline__ void ffma2(uint64_t& acc, uint64_t a, uint64_t b) {
   asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
@@ -381,7 +407,7 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
-  const uint32_t lane8 = (uint32_t)lane << 3;
+  const uint32_t lane4 = (uint32_t)lane << 2;
   // B word of this lane: column g of the block-diagonal B is X of pair g
   // (g < 4) or Y of pair g - 4; lane (g, c) holds rows 2c, 2c+1 of it.
   const int jl = (g == c) ? c : ((g == c + 4) ? 4 + c : 8);
@@ -391,7 +417,7 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
   const uint32_t a23 = c == 0 ? kA256 : 0u;
   float* invf = reinterpret_cast<float*>(smem + L::kInv);
   __shared__ float s_cb0;
-  PairLutHiLo<BITS>::build(smem, a.cb);
+  PairLutSplit<BITS>::build(smem, a.cb);
   if (threadIdx.x < kPairs) invf[threadIdx.x] = a.inv_freq[threadIdx.x];
   if (threadIdx.x == 0) s_cb0 = dense_zero_value(a.cb, 1 << BITS);
 
@@ -484,19 +510,22 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
       for (int gg = 0; gg < G; ++gg) accA[gg] = accB[gg] = 0ull;
 #pragma unroll
       for (int kb = 0; kb < 16; ++kb) {
-        const uint2 e0 = *reinterpret_cast<const uint2*>(lut + sl.addr(2 * kb, lane8));
-        const uint2 e1 = *reinterpret_cast<const uint2*>(lut + sl.addr(2 * kb + 1, lane8));
+        const uint8_t* p0 = lut + sl.addr(2 * kb, lane4);
+        const uint8_t* p1 = lut + sl.addr(2 * kb + 1, lane4);
+        const uint32_t h0 = *reinterpret_cast<const uint32_t*>(p0);
+        const uint32_t h1 = *reinterpret_cast<const uint32_t*>(p1);
+        const uint32_t l0 = *reinterpret_cast<const uint32_t*>(p0 + 128);
+        const uint32_t l1 = *reinterpret_cast<const uint32_t*>(p1 + 128);
 #pragma unroll
         for (int gg = 0; gg < G; ++gg) {
           const uint2 bhl = *reinterpret_cast<const uint2*>(brow + (gg * 16 + kb) * (kBRow * 8));
           const uint32_t bh = bhl.x, bl = bhl.y;
           const uint32_t bz = *reinterpret_cast<const uint32_t*>(zrow + (gg * 16 + kb) * (kZRow * 4));
-          float d[4];
-          mma_16816_zc(d, e0.x, e1.x, e0.x, e1.x, bh, bl);  // Lh (Ph, Qh) + Lh (Pl, Ql)
-          const uint32_t al[4] = {e0.y, e1.y, a23, a23};
-          mma_16816(d, al, bh, bz);                          // + Ll (Ph, Qh) + (OX, OY)
-          ffma2(accA[gg], tw[kb][0], f2pack(d[0], d[1]));
-          ffma2(accB[gg], tw[kb][1], f2pack(d[2], d[3]));
+          float d[4], e[4];
+          mma_16816_zc(d, h0, h1, l0, l1, bh, bh);    // (Lh + Ll) (Ph, Qh)
+          mma_16816_zc(e, h0, h1, a23, a23, bl, bz);  // Lh (Pl, Ql) + (OX, OY)
+          ffma2(accA[gg], tw[kb][0], f2add(f2pack(d[0], d[1]), f2pack(e[0], e[1])));
+          ffma2(accB[gg], tw[kb][1], f2add(f2pack(d[2], d[3]), f2pack(e[2], e[3])));
         }
       }
 #pragma unroll
@@ -1154,15 +1183,20 @@ static int launch_key(const KeyArgs& a0, cudaStream_t st) {
   const int64_t U = a.B * a.H;
   const int64_t nt = (a.T + kTileTokens - 1) / kTileTokens;
   const int64_t n_oct = (nt + kKeyTiles - 1) / kKeyTiles;
-  // Units per work item: as many as fit (the RoPE twiddles of an item are shared by
-  // its units), unless that leaves fewer than two items per SM: short contexts then
-  // split the units into more, smaller groups so that every SM gets work.
-  int64_t UG = U < (int64_t)(kMaxSlots / G) ? U : (int64_t)(kMaxSlots / G);
-  const int64_t want_items = 2 * (int64_t)kValSlots;
-  if (n_oct * ((U + UG - 1) / UG) < want_items) {
-    const int64_t groups = (want_items + n_oct - 1) / n_oct;
-    const int64_t ug = (U + groups - 1) / groups;
-    UG = ug < 1 ? 1 : (ug < UG ? ug : UG);
+  // Units per work item. An item costs about UG unit passes plus 0.75 of one for
+  // its RoPE twiddles (shared by its units), and the persistent CTAs (one per SM)
+  // take the items in rounds: pick the group size that minimises rounds x item
+  // cost, e.g. 32 units at 1M tokens (28 rounds) but 16 at 128K tokens (7 rounds
+  // of half-size items instead of 4 rounds of full ones, the last one mostly idle).
+  const int64_t ug_max = U < (int64_t)(kMaxSlots / G) ? U : (int64_t)(kMaxSlots / G);
+  int64_t UG = ug_max;
+  double best = 1e300;
+  for (int64_t ug = ug_max; ug >= 1; --ug) {
+    const int64_t groups = (U + ug - 1) / ug;
+    if (groups * ug - U >= ug) continue;  // a group size that leaves an empty group
+    const int64_t rounds = (n_oct * groups + kValSlots - 1) / kValSlots;
+    const double cost = (double)rounds * ((double)((U + groups - 1) / groups) + 0.75);
+    if (cost < best * 0.999) { best = cost; UG = (U + groups - 1) / groups; }
   }
   a.units_per_group = (int)UG;
   a.n_groups = (int)((U + UG - 1) / UG);
