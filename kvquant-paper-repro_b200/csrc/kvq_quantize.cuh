@@ -826,7 +826,7 @@ __device__ __forceinline__ int nearest_fast(float v, const NearestTable& t) {
 // blocks' lane slabs in the decode kernels' fragment-native order.
 // ---------------------------------------------------------------------------
 constexpr int kEmitThreads = 256;
-constexpr int kEmitTiles = 4;
+constexpr int kEmitTiles = 16;
 
 struct EmitArgs {
   const __half* x;
@@ -877,7 +877,7 @@ __device__ __forceinline__ int emit_block_scan(int v, int* sh, int& total) {
 }
 
 template <int KIND, bool COUNT_ONLY, int BITS>
-__global__ void __launch_bounds__(kEmitThreads) emit_kernel(EmitArgs a) {
+__global__ void __launch_bounds__(kEmitThreads, 3) emit_kernel(EmitArgs a) {
   __shared__ __align__(16) uint8_t s_code[kTileTokens][kHeadDim];  // codes of the tile
   // code bounds: keys: the head's 128 channels; values: two buffers of a tile's 32 tokens
   __shared__ __align__(16) int16_t s_cbnd[kHeadDim][16];
