@@ -62,7 +62,7 @@ inline CbLayout cb_layout(int64_t n) {
   };
   L.mm = take(sizeof(float2) * kCbStreamMul * G);
   L.bins = take(sizeof(CbBins));
-  L.hist = take(sizeof(float) * 2 * kCbBins * (size_t)G);
+  L.hist = take(sizeof(double) * 2 * kCbBins * (size_t)G);
   L.wsum = take(sizeof(double) * kCbBins);
   L.ssum = take(sizeof(double) * kCbBins);
   L.drow = take(sizeof(double) * (kCbBins + 1));
@@ -205,34 +205,36 @@ __global__ void __launch_bounds__(256) cb_range_kernel(const float* __restrict__
   }
 }
 
-// 2. Per-CTA weighted histogram: part[cta][0][bin] = sum w, part[cta][1][bin] = sum w*(x - centre).
+// 2. Per-CTA weighted histogram: part[cta][0][bin] = sum w, part[cta][1][bin] = sum w*(x - centre),
+// accumulated in double (a CTA adds up to n / 148 samples into a bin; fp32 sums of that
+// length lose 1e-4 .. 1e-3 relative in concentrated bins).
 __global__ void __launch_bounds__(kCbHistThreads) cb_hist_kernel(const float* __restrict__ x,
                                                                  const float* __restrict__ w,
                                                                  int64_t n,
                                                                  const float2* __restrict__ mm,
                                                                  int Gm, CbBins* __restrict__ bins_out,
-                                                                 float* __restrict__ part,
+                                                                 double* __restrict__ part,
                                                                  int32_t* __restrict__ status) {
-  extern __shared__ float cb_hist_sh[];  // [2][kCbBins]
-  float* sw = cb_hist_sh;
-  float* sd = cb_hist_sh + kCbBins;
-  for (int i = threadIdx.x; i < 2 * kCbBins; i += blockDim.x) cb_hist_sh[i] = 0.f;
+  extern __shared__ double cb_hist_sh[];  // [2][kCbBins]
+  double* sw = cb_hist_sh;
+  double* sd = cb_hist_sh + kCbBins;
+  for (int i = threadIdx.x; i < 2 * kCbBins; i += blockDim.x) cb_hist_sh[i] = 0.0;
   const CbBins bins = cb_bins_block(mm, Gm);  // ends with a block barrier
   if (blockIdx.x == 0 && threadIdx.x == 0) *bins_out = bins;
   bool bad = false;
   cb_for_each(x, w, n, [&](float v, float wt) {
     const int k = cb_bin(bins, v);
     bad |= !(wt >= 0.f && wt < INFINITY);
-    atomicAdd(&sw[k], wt);
-    atomicAdd(&sd[k], wt * __fsub_rn(v, cb_centre(bins, k)));
+    atomicAdd(&sw[k], (double)wt);
+    atomicAdd(&sd[k], (double)wt * (double)__fsub_rn(v, cb_centre(bins, k)));
   });
   if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(&status[0], kCbBadWeight);
-  float* out = part + (size_t)blockIdx.x * 2 * kCbBins;
+  double* out = part + (size_t)blockIdx.x * 2 * kCbBins;
   for (int i = threadIdx.x; i < 2 * kCbBins; i += blockDim.x) out[i] = cb_hist_sh[i];
 }
 
 // 3. Bin sums over the CTAs (double, fixed order); status[1] counts the occupied bins.
-__global__ void __launch_bounds__(256) cb_reduce_kernel(const float* __restrict__ part, int G,
+__global__ void __launch_bounds__(256) cb_reduce_kernel(const double* __restrict__ part, int G,
                                                         const CbBins* __restrict__ bins_in,
                                                         double* __restrict__ wsum,
                                                         double* __restrict__ ssum,
@@ -242,9 +244,9 @@ __global__ void __launch_bounds__(256) cb_reduce_kernel(const float* __restrict_
   double W = 0.0, D = 0.0;
 #pragma unroll 8
   for (int g = 0; g < G; ++g) {
-    const float* p = part + (size_t)g * 2 * kCbBins;
-    W += (double)p[k];
-    D += (double)p[kCbBins + k];
+    const double* p = part + (size_t)g * 2 * kCbBins;
+    W += p[k];
+    D += p[kCbBins + k];
   }
   wsum[k] = W;
   ssum[k] = D + (double)cb_centre(bins, k) * W;
@@ -555,11 +557,11 @@ extern "C" int kvq_fit_codebook(const float* x, const float* weights, int64_t n,
   cudaStream_t s = as_stream(stream);
   char* ws = reinterpret_cast<char*>(workspace);
   float2* mm = reinterpret_cast<float2*>(ws + L.mm);
-  float* hist = reinterpret_cast<float*>(ws + L.hist);
+  double* hist = reinterpret_cast<double*>(ws + L.hist);
   double* wsum = reinterpret_cast<double*>(ws + L.wsum);
   double* ssum = reinterpret_cast<double*>(ws + L.ssum);
   CbBins* bins = reinterpret_cast<CbBins*>(ws + L.bins);
-  const size_t hist_smem = sizeof(float) * 2 * kCbBins;
+  const size_t hist_smem = sizeof(double) * 2 * kCbBins;
   const size_t solve_smem = kCbSolveSmem;
   cudaFuncSetAttribute(cb_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)hist_smem);

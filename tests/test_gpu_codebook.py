@@ -144,3 +144,19 @@ def test_non_finite_samples_and_bad_weights_raise(cuda):
         with pytest.raises(ValueError):
             _fit(xx, ww, 3, cuda)
     _fit(x, w, 3, cuda)  # a clean call after the flagged ones
+
+
+def test_sixteen_million_samples_on_few_values_reach_the_optimum(cuda):
+    """16,777,216 samples on 400 distinct values (each far from the others in bin
+    terms) with gamma weights: every CTA adds about 113K samples into few bins, the
+    case where fp32 bin sums lose 1e-4..1e-3 relative. The fit must reach the
+    exact optimum of the aggregated (value, weight) problem."""
+    rng = np.random.default_rng(16)
+    vals = np.sort(rng.uniform(-1, 1, 400)).astype(np.float32)
+    n = 1 << 24
+    x = vals[rng.integers(0, vals.size, n)]
+    w = rng.gamma(2.0, 1.0, n).astype(np.float32)
+    got = _fit(x, w, 4, cuda)
+    agg = np.bincount(np.searchsorted(vals, x), weights=w.astype(np.float64), minlength=vals.size)
+    opt = O.kmeans_1d_optimal(vals, agg, 16)
+    assert O.kmeans_1d_inertia(vals, agg, got) <= O.kmeans_1d_inertia(vals, agg, opt) * (1 + 1e-6)
