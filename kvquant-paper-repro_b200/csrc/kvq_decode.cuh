@@ -613,40 +613,34 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
       __syncthreads();
     }
 
-    // Scores of the item, one warp per slot (row u * G + gg = u0 * G + s), and
-    // the item's softmax partials of scores * stat_scale when asked for.
+    // Scores of the item, one warp per (slot, 32-token chunk) (row u * G + gg =
+    // u0 * G + s), so that items of few slots still use every warp, and the
+    // item's softmax partials of scores * stat_scale when asked for.
     {
       const int nvalid = (int)min((int64_t)kKeyTokens, a.T - (int64_t)tile0 * kTileTokens);
       const float f = a.stat_scale;
-      for (int s = warp; s < nu * G; s += kKeyWarps) {
-        const int64_t row = (int64_t)u0 * G + s;
-        float* dst = a.scores + row * a.T + (int64_t)tile0 * kTileTokens;
-        const float sg = sigma[s];
-        float x[kKeyTokens / 32];
-#pragma unroll
-        for (int k = 0; k < kKeyTokens / 32; ++k) {
-          const int tt = lane + 32 * k;
-          x[k] = sc[s * kKeyTokens + tt] * sg;
-          if (tt < nvalid) dst[tt] = x[k];
-        }
+      constexpr int kChunks = kKeyTokens / 32;
+      const int64_t nblk = (a.T + 15) / 16;
+      const int64_t b0 = (int64_t)tile0 * kTileTokens / 16;
+      for (int idx = warp; idx < nu * G * kChunks; idx += kKeyWarps) {
+        const int sl = idx / kChunks, k = idx % kChunks;
+        const int64_t row = (int64_t)u0 * G + sl;
+        const int tt = lane + 32 * k;
+        const float x = sc[sl * kKeyTokens + tt] * sigma[sl];
+        if (tt < nvalid) a.scores[row * a.T + (int64_t)tile0 * kTileTokens + tt] = x;
         if (a.stats) {
-          // partials per 16-token block (lanes 0-15 / 16-31 of each x[k]), with
-          // the same rounding as the value kernel's (score * scale) on the stored score
-          const int64_t nblk = (a.T + 15) / 16;
-          const int64_t b0 = (int64_t)tile0 * kTileTokens / 16;
+          // partials per 16-token block (lanes 0-15 / 16-31), with the same
+          // rounding as the value kernel's (score * scale) on the stored score
+          const bool valid = tt < nvalid;
+          const float v = valid ? x * f : -INFINITY;
+          float m = v;
 #pragma unroll
-          for (int k = 0; k < kKeyTokens / 32; ++k) {
-            const bool valid = lane + 32 * k < nvalid;
-            const float v = valid ? x[k] * f : -INFINITY;
-            float m = v;
+          for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          float l = valid ? __expf(v - m) : 0.f;
 #pragma unroll
-            for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            float l = valid ? __expf(v - m) : 0.f;
-#pragma unroll
-            for (int o = 1; o < 16; o <<= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-            if ((lane & 15) == 0 && 32 * k + (lane & 16) < nvalid)
-              a.stats[row * nblk + b0 + 2 * k + (lane >> 4)] = make_float2(m, l);
-          }
+          for (int o = 1; o < 16; o <<= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+          if ((lane & 15) == 0 && 32 * k + (lane & 16) < nvalid)
+            a.stats[row * nblk + b0 + 2 * k + (lane >> 4)] = make_float2(m, l);
         }
       }
     }
