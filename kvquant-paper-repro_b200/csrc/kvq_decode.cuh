@@ -777,16 +777,25 @@ __device__ __forceinline__ float2 ml_merge(float2 a, float2 b) {
   return make_float2(m, a.y * __expf(a.x - m) + b.y * __expf(b.x - m));
 }
 
-// row_max_kernel for blockIdx.y < B; blocks with y >= B merge the key
-// kernel's softmax partials stats[row, 0..n_oct) into ml[row] = (M, 1/L).
+// Softmax partials folded by one merge block of value_prep_kernel (256 threads x 8).
+constexpr int kMlChunk = 2048;
+
+// row_max_kernel for blockIdx.y < B. Blocks with y >= B merge the key
+// kernel's softmax partials stats[row, 0..n_oct): work item (row, c) folds
+// the chunk stats[row, c*kMlChunk ..) into part[row*n_mc + c]; the block that
+// completes a row's last chunk (counted in count[row], zero at launch) folds
+// the row's n_mc chunk pairs into ml[row] = (M, 1/L). Nothing waits on
+// another block: the count only elects the block that finishes the row.
 __global__ void __launch_bounds__(256) value_prep_kernel(const float* __restrict__ vs, int64_t T,
                                                          int64_t ld, float* __restrict__ out,
                                                          int64_t B,
                                                          const float2* __restrict__ stats,
-                                                         int n_oct, int64_t rows,
+                                                         int n_oct, int64_t rows, int n_mc,
+                                                         float2* part, unsigned* count,
                                                          float2* __restrict__ ml) {
   __shared__ float red[8];
   __shared__ float2 red2[8];
+  __shared__ int s_last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if ((int64_t)blockIdx.y < B) {
     const int64_t b = blockIdx.y;
@@ -804,9 +813,27 @@ __global__ void __launch_bounds__(256) value_prep_kernel(const float* __restrict
     return;
   }
   const int64_t nb = (int64_t)gridDim.x * (gridDim.y - B);
-  for (int64_t r = blockIdx.x + (int64_t)gridDim.x * (blockIdx.y - B); r < rows; r += nb) {
-    float2 acc = make_float2(-INFINITY, 0.f);
-    for (int k = threadIdx.x; k < n_oct; k += blockDim.x) acc = ml_merge(acc, stats[r * n_oct + k]);
+  const int64_t items = rows * n_mc;
+  for (int64_t w = blockIdx.x + (int64_t)gridDim.x * (blockIdx.y - B); w < items; w += nb) {
+    const int64_t r = w / n_mc;
+    const int c = (int)(w - r * n_mc);
+    const float2* src = stats + r * n_oct;
+    const int k1 = min(n_oct, (c + 1) * kMlChunk);
+    float2 v[kMlChunk / 256];
+#pragma unroll
+    for (int i = 0; i < kMlChunk / 256; ++i) {
+      const int k = c * kMlChunk + i * 256 + (int)threadIdx.x;
+      v[i] = k < k1 ? src[k] : make_float2(-INFINITY, 0.f);
+    }
+    float m = v[0].x;
+#pragma unroll
+    for (int i = 1; i < kMlChunk / 256; ++i) m = fmaxf(m, v[i].x);
+    float l = 0.f;
+    if (m != -INFINITY) {
+#pragma unroll
+      for (int i = 0; i < kMlChunk / 256; ++i) l += v[i].y * __expf(v[i].x - m);
+    }
+    float2 acc = make_float2(m, l);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       float2 other;
@@ -818,8 +845,35 @@ __global__ void __launch_bounds__(256) value_prep_kernel(const float* __restrict
     __syncthreads();
     if (threadIdx.x == 0) {
       float2 t = red2[0];
-      for (int w = 1; w < (int)(blockDim.x >> 5); ++w) t = ml_merge(t, red2[w]);
-      ml[r] = make_float2(t.x, 1.f / t.y);
+      for (int q = 1; q < (int)(blockDim.x >> 5); ++q) t = ml_merge(t, red2[q]);
+      if (n_mc == 1) {
+        ml[r] = make_float2(t.x, 1.f / t.y);
+        s_last = 0;
+      } else {
+        part[w] = t;
+        __threadfence();
+        s_last = atomicAdd(count + r, 1u) == (unsigned)(n_mc - 1);
+      }
+    }
+    __syncthreads();
+    if (s_last) {  // every other chunk pair of this row is visible in L2
+      __threadfence();
+      float2 t = make_float2(-INFINITY, 0.f);
+      for (int k = threadIdx.x; k < n_mc; k += blockDim.x) t = ml_merge(t, __ldcg(part + r * n_mc + k));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        float2 other;
+        other.x = __shfl_xor_sync(0xffffffffu, t.x, o);
+        other.y = __shfl_xor_sync(0xffffffffu, t.y, o);
+        t = ml_merge(t, other);
+      }
+      if (lane == 0) red2[warp] = t;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        float2 u = red2[0];
+        for (int q = 1; q < (int)(blockDim.x >> 5); ++q) u = ml_merge(u, red2[q]);
+        ml[r] = make_float2(u.x, 1.f / u.y);
+      }
     }
     __syncthreads();
   }
@@ -1303,15 +1357,20 @@ inline size_t softmax_ws(int64_t rows, int64_t T) {
   return align256((size_t)(rows > 0 ? rows : 0) * (nch > 0 ? nch : 0) * sizeof(float2));
 }
 
+// Value-path workspace: [split partials][row maxima [B] + softmax merge counts [B*H*G]].
 inline size_t value_ws(int64_t B, int64_t H, int64_t G, int64_t T) {
   const int64_t U = B * H;
   const int64_t nt = (T + kTileTokens - 1) / kTileTokens;
   return align256((size_t)value_splits(U, nt, G) * U * G * 129 * sizeof(float)) +
-         align256((size_t)B * sizeof(float));
+         align256((size_t)B * sizeof(float) + (size_t)U * G * sizeof(unsigned));
 }
-// ... of the raw-score variant: plus the merged (M, 1/L) per row.
+inline int64_t ml_chunks(int64_t T) { return (key_items(T) + kMlChunk - 1) / kMlChunk; }
+// ... of the raw-score variant: plus the merged (M, 1/L) per row and the
+// merge's chunk pairs [B*H*G, ml_chunks(T)].
 inline size_t value_scores_ws(int64_t B, int64_t H, int64_t G, int64_t T) {
-  return value_ws(B, H, G, T) + align256((size_t)(B * H * G > 0 ? B * H * G : 0) * sizeof(float2));
+  const size_t rows = (size_t)(B * H * G > 0 ? B * H * G : 0);
+  return value_ws(B, H, G, T) + align256(rows * sizeof(float2)) +
+         align256(rows * (size_t)ml_chunks(T > 0 ? T : 1) * sizeof(float2));
 }
 
 static int value_impl(const uint8_t* codes, const uint32_t* out_ent, const int32_t* out_ptr,
@@ -1331,8 +1390,8 @@ static int value_impl(const uint8_t* codes, const uint32_t* out_ent, const int32
   const int64_t nt = (T + kTileTokens - 1) / kTileTokens;
   const int n_splits = value_splits(U, nt, G);
   const size_t part_bytes = align256((size_t)n_splits * U * G * 129 * sizeof(float));
-  const size_t need = stats ? value_scores_ws(B, H, G, T)
-                            : part_bytes + align256((size_t)B * sizeof(float));
+  const size_t base_bytes = value_ws(B, H, G, T);
+  const size_t need = stats ? value_scores_ws(B, H, G, T) : base_bytes;
   if (!workspace || workspace_bytes < need) {
     set_error("value_output: workspace too small (%zu < %zu)", workspace_bytes, need);
     return KVQ_ERR_INVALID;
@@ -1345,8 +1404,10 @@ static int value_impl(const uint8_t* codes, const uint32_t* out_ent, const int32
   a.stat_scale = stat_scale;
   a.partial = reinterpret_cast<float*>(workspace);
   float* row_max = reinterpret_cast<float*>((char*)workspace + part_bytes);
+  unsigned* ml_count = reinterpret_cast<unsigned*>(row_max + B);
   {
-    const cudaError_t me = cudaMemsetAsync(row_max, 0, (size_t)B * sizeof(float), st);
+    const size_t clear = (size_t)B * sizeof(float) + (stats ? (size_t)U * G * sizeof(unsigned) : 0);
+    const cudaError_t me = cudaMemsetAsync(row_max, 0, clear, st);
     if (me != cudaSuccess) {
       set_error("value_output: clearing the row maxima failed: %s", cudaGetErrorString(me));
       return KVQ_ERR_CUDA;
@@ -1355,20 +1416,21 @@ static int value_impl(const uint8_t* codes, const uint32_t* out_ent, const int32
   const unsigned n_chunks = (unsigned)((T + kRowMaxChunk - 1) / kRowMaxChunk);
   if (stats) {
     // one launch: the row maxima and the merge of the key kernel's partials
-    float2* ml = ml_out ? ml_out
-                        : reinterpret_cast<float2*>((char*)workspace + part_bytes +
-                                                    align256((size_t)B * sizeof(float)));
-    a.ml = ml;
     const int64_t rows = U * G;
+    char* tail = (char*)workspace + base_bytes;
+    float2* ml = ml_out ? ml_out : reinterpret_cast<float2*>(tail);
+    float2* ml_part = reinterpret_cast<float2*>(tail + align256((size_t)rows * sizeof(float2)));
+    a.ml = ml;
     const int n_oct = (int)key_items(T);
+    const int n_mc = (int)ml_chunks(T);
     if (B >= 65535) {
       set_error("value_output_scores: batch %lld leaves no grid rows for the softmax merge",
                 (long long)B);
       return KVQ_ERR_INVALID;
     }
-    const int64_t merge_y = min((rows + n_chunks - 1) / n_chunks, (int64_t)65535 - B);
+    const int64_t merge_y = min((rows * n_mc + n_chunks - 1) / n_chunks, (int64_t)65535 - B);
     value_prep_kernel<<<dim3(n_chunks, (unsigned)(B + merge_y)), 256, 0, st>>>(
-        v_scale, T, ld_stats, row_max, B, stats, n_oct, rows, ml);
+        v_scale, T, ld_stats, row_max, B, stats, n_oct, rows, n_mc, ml_part, ml_count, ml);
   } else {
     row_max_kernel<<<dim3(n_chunks, (unsigned)B), 256, 0, st>>>(v_scale, T, ld_stats, row_max);
   }
