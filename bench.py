@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--workload", default="longctx-1m-4bit")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count")
     ap.add_argument("--tokens", type=int, default=None, help="override the cached token count")
+    ap.add_argument("--kv-heads", type=int, default=None,
+                    help="override the KV head count (e.g. one rank's share of a head split)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-append", action="store_true")
@@ -350,6 +352,10 @@ def run_gpu(args):
     if args.tokens:
         import dataclasses
         wl = dataclasses.replace(wl, tokens=args.tokens, name=f"{wl.name}@{args.tokens}tok")
+    if args.kv_heads:
+        import dataclasses
+        wl = dataclasses.replace(wl, kv_heads=args.kv_heads,
+                                 name=f"{wl.name}@{args.kv_heads}kvheads")
     layers = args.layers or wl.layers
     from kvquant.sharding import (shard_heads, shard_tokens, gather_buffer, gather_head_outputs,
                                   gather_shard_partials)
