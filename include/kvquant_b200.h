@@ -184,7 +184,9 @@ int kvq_append_values(const void* v_new, int64_t B, int64_t S_new, int64_t C_ful
 /* ---------------------------------------------------------------------------
  * Decode attention over the packed cache (T cached tokens at positions
  * 0..T-1, token 0 = sink). q fp16 [B, n_heads*group, 128] (already rotated
- * to its own position); query head hq reads KV head hq / group.
+ * to its own position); query head hq reads KV head hq / group. codes must be
+ * 16-byte aligned (tiles are staged with 16-byte copies); a null or unaligned
+ * codes pointer returns KVQ_ERR_INVALID before any launch.
  * ------------------------------------------------------------------------- */
 
 /* Fused key kernel: scores[b,hq,t] = q . RoPE_t(Khat_t) (raw, unscaled) fp32

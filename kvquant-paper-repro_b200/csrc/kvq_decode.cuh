@@ -1329,6 +1329,20 @@ static int check_decode_shape(const char* what, int64_t B, int64_t H, int64_t G,
   return KVQ_OK;
 }
 
+// Bit width, then the code tiles' address: the kernels stage code tiles with
+// 16-byte cp.async copies.
+static int check_codes_aligned(const char* what, const void* codes, int bits) {
+  if (bits < 2 || bits > 4) {
+    set_error("%s: bits must be 2, 3 or 4 (got %d)", what, bits);
+    return KVQ_ERR_UNSUPPORTED;
+  }
+  if (!codes || ((uintptr_t)codes & 15u)) {
+    set_error("%s: codes must be a 16-byte aligned device pointer (got %p)", what, codes);
+    return KVQ_ERR_INVALID;
+  }
+  return KVQ_OK;
+}
+
 static int softmax_impl(const float* scores, int64_t rows, int64_t T, float scale, float* probs,
                         void* workspace, size_t workspace_bytes, cudaStream_t st) {
   if (rows < 0 || T < 1) {
@@ -1381,6 +1395,8 @@ static int value_impl(const uint8_t* codes, const uint32_t* out_ent, const int32
                       const float2* stats = nullptr, float stat_scale = 0.f,
                       float2* ml_out = nullptr) {
   int rc = check_decode_shape("value_output", B, H, G, T, nt_cap);
+  if (rc) return rc;
+  rc = check_codes_aligned("value_output", codes, bits);
   if (rc) return rc;
   if (ld_stats < T) {
     set_error("value_output: ld_stats=%lld < T=%lld", (long long)ld_stats, (long long)T);
@@ -1478,6 +1494,8 @@ static int key_impl(const uint8_t* codes, const uint32_t* out_ent, const int32_t
                     float* scores, float2* stats, float stat_scale, cudaStream_t st,
                     int64_t pos0 = 0) {
   int rc = check_decode_shape("key_scores", B, n_heads, group, T, nt_cap);
+  if (rc) return rc;
+  rc = check_codes_aligned("key_scores", codes, bits);
   if (rc) return rc;
   if (pos0 < 0 || pos0 + T > (1LL << 24)) {  // positions are exact fp32 integers up to 2^24
     set_error("key_scores: positions [%lld, %lld) outside [0, 2^24]", (long long)pos0,

@@ -68,6 +68,12 @@ def test_invalid_arguments_are_rejected_before_any_launch(lib):
     rc = lib.kvq_key_scores(None, None, None, None, None, None, None, 4, None, None,
                             1, 1, 1, 65, 2, None, None)
     assert rc == 1
+    # code tiles are staged with 16-byte copies: a null or unaligned codes pointer
+    # is refused (the pointer is never dereferenced on this path)
+    for codes in (None, ctypes.c_void_p(8)):
+        rc = lib.kvq_key_scores(codes, None, None, None, None, None, None, 4, None, None,
+                                1, 1, 1, 64, 2, None, None)
+        assert rc == 1 and b"16-byte aligned" in lib.kvq_last_error()
     # workspace too small
     rc = lib.kvq_quantize_keys_plan(None, 1, 64, 128, 0, 1, None, None, 0.01, 1, None, 2, None,
                                     None, 0, None)
