@@ -280,7 +280,8 @@ struct KeySmem {
   static constexpr int kISig = kQh + kMaxSlots * kHeadDim * 2;        // [slots] 1 / sigma
   static constexpr int kRing = (kISig + kMaxSlots * 4 + 15) / 16 * 16;
   static constexpr int kStage = kKeyThreads * (16 + 16 + 4);
-  static constexpr int kBytes = kRing + kKeyStages * kStage;
+  static constexpr int kSZ = kRing + kKeyStages * kStage;  // per thread: (scale, zero) of its entry
+  static constexpr int kBytes = kSZ + kKeyThreads * 8;
   static_assert(kBytes <= 232448, "key kernel shared memory");
 };
 
@@ -493,15 +494,32 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
     }
 
     int rd_stage = 0;
+    int ho = (int)(u0 % a.H);  // KV head of unit u0 + ui
+    float2* szs = reinterpret_cast<float2*>(smem + L::kSZ) + threadIdx.x;
     for (int ui = 0; ui < nu; ++ui) {
-      issue(ui + kKeyStages - 1);
-      cp_async_wait<kKeyStages - 1>();
+      // cp.async groups per iteration: this unit's (scale, zero) pair, then the
+      // ring copy kKeyStages - 1 units ahead; waiting for all but the newest
+      // one therefore completes ring copy ui (and every pair before it).
+      cp_async_wait<kKeyStages - 2>();
       const uint8_t* st = ring + rd_stage * L::kStage;
       rd_stage = rd_stage == kKeyStages - 1 ? 0 : rd_stage + 1;
       LaneSlab<BITS> sl;
       sl.read(st + threadIdx.x * 16, st + kKeyThreads * 16 + threadIdx.x * 16);
       const uint32_t ent0 = *reinterpret_cast<const uint32_t*>(st + kKeyThreads * 32 + threadIdx.x * 4);
       const int slot0 = ui * G;
+      // Scale and zero of the channel of this lane's entry among the block's
+      // first 32, fetched now so that the outlier pass after the MMA loop finds
+      // them in shared memory instead of waiting on L2.
+      {
+        const int32_t f0 = uptr[ui * (kKeyRows + 1) + warp], f1 = uptr[ui * (kKeyRows + 1) + warp + 1];
+        const bool fv = f0 + lane < f1;
+        const int64_t off = fv ? (int64_t)ho * kHeadDim + (ent0 & 127) : 0;
+        const uint32_t dst = smem_u32(szs);
+        cp_async4(dst, a.k_scale + off, fv ? 4u : 0u);
+        cp_async4(dst + 4, a.k_zero + off, fv ? 4u : 0u);
+        cp_async_commit();
+      }
+      issue(ui + kKeyStages - 1);
       const uint8_t* brow = bbase + slot0 * (16 * kBRow * 8);
       const uint8_t* zrow = zbase + slot0 * (16 * kZRow * 4);
 
@@ -546,7 +564,7 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
       // p < 64 and (q2, -q1) for p + 64.
       const int32_t e0 = uptr[ui * (kKeyRows + 1) + warp], e1 = uptr[ui * (kKeyRows + 1) + warp + 1];
       if (e0 < e1) {
-        const int64_t ho = (u0 + ui) % a.H;
+        cp_async_wait<1>();  // this unit's (scale, zero) pairs
         const __half* qrow = reinterpret_cast<const __half*>(smem + L::kQh) + slot0 * kHeadDim;
         const float* isig = reinterpret_cast<const float*>(smem + L::kISig) + slot0;
         __syncwarp();
@@ -558,10 +576,10 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
           const int ch = (int)(en & 127), p = ch & 63;
           float sv, cv;
           __sincosf(rope_reduce(tok0 + (tok & 15), invf[p]), &sv, &cv);
-          const float ov =
-              valid ? entry_value(en) - fmaf(s_cb0, a.k_scale[ho * kHeadDim + ch],
-                                             a.k_zero[ho * kHeadDim + ch])
-                    : 0.f;
+          const float2 kz = eb == e0 ? *szs
+                                     : make_float2(a.k_scale[(int64_t)ho * kHeadDim + ch],
+                                                   a.k_zero[(int64_t)ho * kHeadDim + ch]);
+          const float ov = valid ? entry_value(en) - fmaf(s_cb0, kz.x, kz.y) : 0.f;
           // Entries are ordered by token: suffix sums within runs of equal
           // tokens; runs are almost always at most 4 long (two steps), longer
           // ones take the remaining steps.
@@ -594,6 +612,7 @@ __global__ void __launch_bounds__(kKeyThreads, 1) key_scores_kernel(KeyArgs a) {
           __syncwarp();
         }
       }
+      ho = ho + 1 == (int)a.H ? 0 : ho + 1;
     }
     cp_async_wait<0>();
     __syncthreads();
