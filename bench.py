@@ -264,8 +264,8 @@ def measure_decode_append(wl, h0, hl, dev, cbk, cbv, log, T0=4096, steps=32):
 # byte of each decode kernel, from one capture of the 4-bit 1%-outlier workload
 # at 262144 tokens x 32 KV heads, fused softmax (traffic grows in proportion to
 # the tokens).
-DRAM_PER_ALGORITHMIC_BYTE = {"key_scores": (588017920 + 35300096) / 619708416,
-                             "value_output": (618740224 + 3824384) / 620773216}
+DRAM_PER_ALGORITHMIC_BYTE = {"key_scores": (589057792 + 35775488) / 619708416,
+                             "value_output": (618741248 + 4753664) / 620773216}
 
 
 TRAFFIC_SOURCE = ("not measured on this launch: the DRAM bytes per algorithmic byte of one "
