@@ -121,6 +121,33 @@ def test_fused_vs_explicit_softmax(cuda, T):
     assert rel_l2(fused, explicit) <= TOL
 
 
+@pytest.mark.parametrize("T", [32769, 70001])
+def test_fused_long_context_chunked_merge(cuda, T):
+    """Past 32,768 tokens a row has more than 2048 softmax partials, which the value
+    prep merges in 2048-partial chunks over many blocks (the block that completes a
+    row's last chunk folds the chunk pairs): (M, 1/L) against float64 over the
+    scores, the output against the explicit softmax path and the oracle, on two
+    calls in a row (the merge counts are cleared per call)."""
+    from kvquant.kernels import qk_scores_stats, pv_out_scores, pv_out, softmax, rope_inv_freq
+    pk, pv, q, (rs, rp, ro), vh = _case(cuda, 1, 2, 2, T, 4, 0.01, 23 + T, want_v=True)
+    inv = rope_inv_freq(128, 10000.0)
+    s, st = qk_scores_stats(t(q, cuda), pk, inv)
+    assert rel_l2(s.cpu().numpy(), rs) <= TOL
+    x = s.cpu().numpy().reshape(4, T).astype(np.float64) * np.float32(SCALE)
+    m = x.max(axis=1)
+    inv_l = 1.0 / np.exp(x - m[:, None]).sum(axis=1)
+    ro_k = O.value_output(O.softmax_probs(s.cpu().numpy().astype(np.float64), 128), vh, 2)
+    o_explicit = pv_out(softmax(s), pv).cpu().numpy()
+    for _ in range(2):
+        ml = torch.full((4, 2), float("nan"), dtype=torch.float32, device=cuda)
+        o = pv_out_scores(s, st, pv, ml_out=ml).cpu().numpy()
+        got = ml.cpu().numpy().astype(np.float64)
+        np.testing.assert_allclose(got[:, 0], m, rtol=1e-6, atol=1e-6)
+        np.testing.assert_allclose(got[:, 1], inv_l, rtol=3e-5)
+        assert rel_l2(o, o_explicit) <= TOL, rel_l2(o, o_explicit)
+        assert rel_l2(o, ro_k) <= TOL, rel_l2(o, ro_k)
+
+
 def test_fused_without_sink(cuda):
     from kvquant.kernels import decode_attention, rope_inv_freq
     pk, pv, q, (rs, rp, ro), vh = _case(cuda, 1, 2, 1, 700, 3, 0.01, 9, sink=False, want_v=True)
