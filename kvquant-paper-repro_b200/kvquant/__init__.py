@@ -2,7 +2,7 @@
 
 Mirrors the reference package's public API for this path; the calibration,
 sensitivity, model-loading and perplexity tooling of the reference are not
-part of this build.
+part of this package.
 """
 from .quant.kv_quantizer import KVQuantizer
 from .attention_patch import patch_model, unpatch_model

@@ -2,7 +2,7 @@
 
 Same functions, arguments and results as the reference; every call runs an
 sm_100a kernel of the kvquant_b200 library. The reference's PyTorch fallbacks
-(matvec_ds.py:18-23, 40-49, 69-72) are not part of this build: inputs must be
+(matvec_ds.py:18-23, 40-49, 69-72) are not part of this library: inputs must be
 CUDA tensors.
 """
 from __future__ import annotations

@@ -4,7 +4,7 @@ Same constructor and methods. quantize_k / quantize_v return the reference's
 fake-quant output (quantize, then dequantize to the input dtype) computed by
 the sm_100a quantize kernels; on the same inputs the result equals the
 reference's bit for bit, except where torch.topk's unspecified order among
-equal |n| at the top-k threshold picks a different position (this build takes
+equal |n| at the top-k threshold picks a different position (the kernels take
 the lower index). pack_k / pack_v return the packed cache dict instead.
 """
 from __future__ import annotations

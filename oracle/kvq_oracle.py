@@ -13,7 +13,7 @@ KVQuant-Paper-Repro project root). Parity of this restatement is pinned by
 reference's own PyTorch code (``tests/golden/make_golden.py``).
 
 Packed-format helpers (``pack_codes``/``unpack_codes``/``tile_outliers``) define
-this build's HBM layout for the quantized cache; the reference stores one code
+the library's HBM layout for the quantized cache; the reference stores one code
 per byte and has no bit packing, so the format is new and is checked here by
 round trips to the reference's indices.
 """
@@ -60,7 +60,7 @@ def outlier_count(n: int, ratio: float) -> int:
 def topk_mask(xabs: np.ndarray, k: int, axis: int) -> np.ndarray:
     """Top-k mask of |x| along `axis` (kvquant/quant/dense_sparse.py:25-28).
 
-    torch.topk leaves the order of equal values unspecified; this build fixes
+    torch.topk leaves the order of equal values unspecified; the library fixes
     it: among values equal to the k-th largest, lower indices win.
     """
     order = np.argsort(-xabs, axis=axis, kind="stable")
@@ -384,7 +384,7 @@ def merge_shards(os_, ms, ls):
 
 
 # --------------------------------------------------------------------------
-# Packed cache format (this build's layout; round-trips to reference indices)
+# Packed cache format (the library's layout; round-trips to reference indices)
 # --------------------------------------------------------------------------
 def slab_map(kind: str):
     """Layout of one 32-token code tile: (block, lane, pair slot) -> elements.
