@@ -2,7 +2,7 @@
 
 The reference JIT-builds a pybind11 extension and returns ``None`` when that
 fails, silently falling back to PyTorch (kvquant/kernels/cuda_ops.py:13-46).
-This build ships a prebuilt sm_100a C-ABI library (``_lib/libkvquant_b200.so``)
+This package ships a prebuilt sm_100a C-ABI library (``_lib/libkvquant_b200.so``)
 and binds it with ctypes; ``get_cuda_ops()`` returns an object exposing the
 reference's four op names with the reference's signatures and return types
 (kvquant/kernels/csrc/kvquant_ops.cu:265-270), plus the fused decode ops.
